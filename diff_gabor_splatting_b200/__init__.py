@@ -1,0 +1,11 @@
+"""B200-native differentiable classic and neural Gabor surface rasterization.
+
+Drop-in for the render path of ``gabor_splatting`` (luisrodolfo10/diff_gabor_splatting
+v0.1.1): ``rasterize_gabors`` and ``rasterize_neural_gabors`` keep the reference's
+signatures and contracts; projection, binning and compositing run as hand-written
+sm_100a kernels in ``libgabor_b200.so`` behind a C ABI (include/gabor_b200.h).
+"""
+
+from .rendering import rasterize_gabors, rasterize_neural_gabors
+
+__all__ = ["rasterize_gabors", "rasterize_neural_gabors"]

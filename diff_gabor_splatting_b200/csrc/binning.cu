@@ -1,0 +1,264 @@
+// Tile binning: per-tile, depth-ordered record lists.
+//
+// The reference (rasterize.cu:32-69, 454-493) counts tiles per record, scans,
+// emits one 64-bit key (image*tw*th + tile) << 32 | depth_bits per (record, tile)
+// in record order, and radix-sorts all I keys over 64 bits (8 passes over 12-byte
+// pairs).  The stable sort makes the order within a tile (depth bits, record
+// index).
+//
+// Here the same order is produced with far less traffic:
+//   1. stable radix sort of the R records by their 32-bit depth bits (R << I);
+//   2. tile counts gathered in that order, inclusive scan, one host read of I
+//      (the reference's one synchronisation, rasterize.cu:466-468);
+//   3. expansion of every (record, tile) slot in depth order, writing a 32-bit
+//      tile id and the record index (8 bytes per slot, coalesced);
+//   4. stable radix sort of the slots by tile id over only ceil(log2(tiles)) bits
+//      (2 passes for up to 65536 tiles), which keeps the depth order inside each
+//      tile;
+//   5. tile ranges from the sorted tile ids.
+// Result: point_list and ranges identical to the reference's.
+#include <cub/cub.cuh>
+
+#include "common.cuh"
+
+namespace gs {
+namespace {
+
+constexpr int kBinThreads = 256;
+
+inline size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct CountLayout {
+    size_t keys_in, keys_out, idx_in, idx_out, counts, offsets, temp, temp_bytes, total;
+};
+
+CountLayout count_layout(int64_t R) {
+    CountLayout L{};
+    size_t sort_bytes = 0, scan_bytes = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                    (const int*)nullptr, (int*)nullptr, int(R), 0, 32);
+    cub::DeviceScan::InclusiveSum(nullptr, scan_bytes, (const int64_t*)nullptr, (int64_t*)nullptr,
+                                  int(R));
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t at = off; off += align_up(bytes); return at; };
+    L.keys_in = take(sizeof(uint32_t) * R);
+    L.keys_out = take(sizeof(uint32_t) * R);
+    L.idx_in = take(sizeof(int) * R);
+    L.idx_out = take(sizeof(int) * R);
+    L.counts = take(sizeof(int64_t) * R);
+    L.offsets = take(sizeof(int64_t) * R);
+    L.temp_bytes = std::max(sort_bytes, scan_bytes);
+    L.temp = take(L.temp_bytes);
+    L.total = off;
+    return L;
+}
+
+struct SortLayout {
+    size_t keys_in, keys_out, vals_in, temp, temp_bytes, total;
+};
+
+int tile_bits(int64_t n_tiles) {
+    int bits = 1;
+    while ((int64_t(1) << bits) < n_tiles) ++bits;
+    return bits;
+}
+
+SortLayout sort_layout(int64_t I, int64_t n_tiles) {
+    SortLayout L{};
+    size_t sort_bytes = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                    (const int*)nullptr, (int*)nullptr, int(I), 0, tile_bits(n_tiles));
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t at = off; off += align_up(bytes); return at; };
+    L.keys_in = take(sizeof(uint32_t) * I);
+    L.keys_out = take(sizeof(uint32_t) * I);
+    L.vals_in = take(sizeof(int) * I);
+    L.temp_bytes = sort_bytes;
+    L.temp = take(sort_bytes);
+    L.total = off;
+    return L;
+}
+
+// Depth sort keys: the 32 bits of the record's centre depth T[2][2] (record slot 8),
+// the low half of the reference's key (rasterize.cu:52-53).
+__global__ void depth_keys_kernel(int64_t R, const float* __restrict__ records, int stride,
+                                  const int* __restrict__ radii, uint32_t* __restrict__ keys,
+                                  int* __restrict__ idx) {
+    const int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    keys[r] = radii[r] > 0 ? __float_as_uint(records[r * stride + 8]) : 0xffffffffu;
+    idx[r] = int(r);
+}
+
+__global__ void tile_counts_kernel(int64_t R, const float* __restrict__ records, int stride,
+                                   const int* __restrict__ radii, const int* __restrict__ order,
+                                   int tw, int th, int64_t* __restrict__ counts) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= R) return;
+    const int r = order[i];
+    const int radius = radii[r];
+    if (radius <= 0) { counts[i] = 0; return; }
+    const int4 b = tile_rect(records[int64_t(r) * stride + 9], records[int64_t(r) * stride + 10],
+                             radius, tw, th);
+    counts[i] = int64_t(b.z - b.x) * (b.w - b.y);
+}
+
+// One thread per (record, tile) slot, slots in depth order: binary search of the
+// owning record in the inclusive offsets, then its row-major tile.
+__global__ void expand_kernel(int64_t I, int64_t R, const int64_t* __restrict__ offsets,
+                              const int* __restrict__ order, const float* __restrict__ records,
+                              int stride, const int* __restrict__ radii,
+                              const int64_t* __restrict__ image_ids, int64_t per_image, int tw,
+                              int th, uint32_t* __restrict__ tile_keys, int* __restrict__ values) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= I) return;
+    int64_t lo = 0, hi = R - 1;   // first j with offsets[j] > i
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (offsets[mid] > i) hi = mid; else lo = mid + 1;
+    }
+    const int r = order[lo];
+    const int64_t start = lo ? offsets[lo - 1] : 0;
+    const int64_t local = i - start;
+    const int4 b = tile_rect(records[int64_t(r) * stride + 9], records[int64_t(r) * stride + 10],
+                             radii[r], tw, th);
+    const int w = b.z - b.x;
+    const int tx = b.x + int(local % w), ty = b.y + int(local / w);
+    const int64_t image = image_ids ? image_ids[r] : r / per_image;
+    tile_keys[i] = uint32_t(image * tw * th + int64_t(ty) * tw + tx);
+    values[i] = r;
+}
+
+__global__ void ranges_kernel(int64_t I, const uint32_t* __restrict__ keys, int2* __restrict__ ranges) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= I) return;
+    const uint32_t t = keys[i];
+    if (i == 0 || keys[i - 1] != t) ranges[t].x = int(i);
+    if (i == I - 1 || keys[i + 1] != t) ranges[t].y = int(i + 1);
+}
+
+unsigned blocks_for(int64_t n) { return unsigned((n + kBinThreads - 1) / kBinThreads); }
+
+int check_common(const char* fn, const float* records, int stride, const int32_t* radii,
+                 int64_t R, int64_t per_image, int64_t images, int width, int height) {
+    if (!records && R > 0) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": records is NULL");
+    if (!radii && R > 0) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": radii is NULL");
+    if (stride < 11) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": record stride below 11");
+    if (R < 0 || images < 1 || width < 1 || height < 1 || per_image < 0)
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": invalid sizes");
+    if (R > INT_MAX) return fail(GS_ERR_LIMIT, std::string(fn) + ": too many projected primitives");
+    const int64_t tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    if (images * tw * th > INT_MAX)
+        return fail(GS_ERR_LIMIT, std::string(fn) + ": image tile count exceeds int32");
+    return GS_OK;
+}
+
+}  // namespace
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_bin_count_workspace(int64_t records, size_t* bytes) {
+    if (records < 0 || !bytes) return fail(GS_ERR_ARGUMENT, "gs_bin_count_workspace: invalid arguments");
+    if (records > INT_MAX) return fail(GS_ERR_LIMIT, "gs_bin_count_workspace: too many projected primitives");
+    *bytes = records ? count_layout(records).total : 0;
+    return GS_OK;
+}
+
+extern "C" int gs_bin_count(const float* records, int record_stride, const int32_t* radii,
+                            const int64_t* image_ids, int64_t R, int64_t records_per_image,
+                            int64_t images, int width, int height, void* workspace1,
+                            size_t workspace1_bytes, int64_t* intersections, void* stream) {
+    int st = check_common("gs_bin_count", records, record_stride, radii, R, records_per_image,
+                          images, width, height);
+    if (st) return st;
+    if (!intersections) return fail(GS_ERR_ARGUMENT, "gs_bin_count: intersections is NULL");
+    *intersections = 0;
+    if (R == 0) return GS_OK;
+    if (!image_ids && records_per_image < 1)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_count: records_per_image must be positive without image_ids");
+    const CountLayout L = count_layout(R);
+    if (!workspace1 || workspace1_bytes < L.total)
+        return fail(GS_ERR_WORKSPACE, "gs_bin_count: workspace too small");
+    auto* base = static_cast<char*>(workspace1);
+    auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
+    auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
+    auto* idx_in = reinterpret_cast<int*>(base + L.idx_in);
+    auto* idx_out = reinterpret_cast<int*>(base + L.idx_out);
+    auto* counts = reinterpret_cast<int64_t*>(base + L.counts);
+    auto* offsets = reinterpret_cast<int64_t*>(base + L.offsets);
+    void* temp = base + L.temp;
+    auto s = as_stream(stream);
+    const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    depth_keys_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
+                                                            keys_in, idx_in);
+    GS_CHECK_LAUNCH("depth_keys_kernel");
+    size_t temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx_in, idx_out,
+                                            int(R), 0, 32, s));
+    tile_counts_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
+                                                             idx_out, tw, th, counts);
+    GS_CHECK_LAUNCH("tile_counts_kernel");
+    temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, counts, offsets, int(R), s));
+    int64_t total = 0;
+    GS_CUDA(cudaMemcpyAsync(&total, offsets + R - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    GS_CUDA(cudaStreamSynchronize(s));
+    *intersections = total;
+    if (total > INT_MAX)
+        return fail(GS_ERR_LIMIT, "gs_bin_count: tile intersection count exceeds int32");
+    return GS_OK;
+}
+
+extern "C" int gs_bin_sort_workspace(int64_t records, int64_t intersections, int64_t images,
+                                     int width, int height, size_t* bytes) {
+    if (!bytes || records < 0 || intersections < 0 || images < 1 || width < 1 || height < 1)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_sort_workspace: invalid arguments");
+    if (intersections > INT_MAX)
+        return fail(GS_ERR_LIMIT, "gs_bin_sort_workspace: tile intersection count exceeds int32");
+    const int64_t tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    *bytes = intersections ? sort_layout(intersections, images * tw * th).total : 0;
+    return GS_OK;
+}
+
+extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_t* radii,
+                           const int64_t* image_ids, int64_t R, int64_t records_per_image,
+                           int64_t images, int width, int height, const void* workspace1,
+                           size_t workspace1_bytes, void* workspace2, size_t workspace2_bytes,
+                           int64_t I, int32_t* point_list, int32_t* ranges, void* stream) {
+    int st = check_common("gs_bin_sort", records, record_stride, radii, R, records_per_image,
+                          images, width, height);
+    if (st) return st;
+    if (I < 0 || I > INT_MAX) return fail(GS_ERR_LIMIT, "gs_bin_sort: tile intersection count exceeds int32");
+    if (!ranges) return fail(GS_ERR_ARGUMENT, "gs_bin_sort: ranges is NULL");
+    const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    const int64_t n_tiles = images * tw * th;
+    auto s = as_stream(stream);
+    GS_CUDA(cudaMemsetAsync(ranges, 0, sizeof(int2) * n_tiles, s));
+    if (I == 0 || R == 0) return GS_OK;
+    if (!point_list) return fail(GS_ERR_ARGUMENT, "gs_bin_sort: point_list is NULL");
+    const CountLayout C = count_layout(R);
+    if (!workspace1 || workspace1_bytes < C.total)
+        return fail(GS_ERR_WORKSPACE, "gs_bin_sort: workspace 1 too small");
+    const SortLayout L = sort_layout(I, n_tiles);
+    if (!workspace2 || workspace2_bytes < L.total)
+        return fail(GS_ERR_WORKSPACE, "gs_bin_sort: workspace 2 too small");
+    const auto* base1 = static_cast<const char*>(workspace1);
+    const auto* order = reinterpret_cast<const int*>(base1 + C.idx_out);
+    const auto* offsets = reinterpret_cast<const int64_t*>(base1 + C.offsets);
+    auto* base = static_cast<char*>(workspace2);
+    auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
+    auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
+    auto* vals_in = reinterpret_cast<int*>(base + L.vals_in);
+    void* temp = base + L.temp;
+    expand_kernel<<<blocks_for(I), kBinThreads, 0, s>>>(I, R, offsets, order, records, record_stride,
+                                                        radii, image_ids, records_per_image, tw, th,
+                                                        keys_in, vals_in);
+    GS_CHECK_LAUNCH("expand_kernel");
+    size_t temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, point_list,
+                                            int(I), 0, tile_bits(n_tiles), s));
+    ranges_kernel<<<blocks_for(I), kBinThreads, 0, s>>>(I, keys_out, reinterpret_cast<int2*>(ranges));
+    GS_CHECK_LAUNCH("ranges_kernel");
+    return GS_OK;
+}

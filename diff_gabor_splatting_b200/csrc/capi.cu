@@ -1,0 +1,120 @@
+// Error plumbing, version, and the layout converters used by the reference-layout
+// (`_C`-style) entry points.
+#include <string>
+
+#include "common.cuh"
+
+namespace gs {
+
+namespace {
+thread_local std::string g_last_error;
+constexpr int kPackThreads = 256;
+unsigned blocks_for(int64_t n) { return unsigned((n + kPackThreads - 1) / kPackThreads); }
+
+// geometry[Q][17] + opacity of the record's primitive -> 20-float record
+__global__ void pack_geometry_kernel(int64_t Q, const float* __restrict__ geometry,
+                                     const float* __restrict__ opacities,
+                                     const int64_t* __restrict__ prim_ids,
+                                     float* __restrict__ records) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= Q * kRec) return;
+    const int64_t q = i / kRec;
+    const int k = int(i % kRec);
+    float v = 0.f;
+    if (k < 17) v = geometry[q * 17 + k];
+    else if (k == 17) v = opacities[prim_ids[q]];
+    records[i] = v;
+}
+
+__global__ void pack_rows_kernel(int64_t A, int width, int padded, const float* __restrict__ in,
+                                 float* __restrict__ out) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= A * padded) return;
+    const int64_t a = i / padded;
+    const int k = int(i % padded);
+    out[i] = k < width ? in[a * width + k] : 0.f;
+}
+
+__global__ void unpack_rows_kernel(int64_t A, int width, int padded, const float* __restrict__ in,
+                                   float* __restrict__ out) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= A * width) return;
+    out[i] = in[(i / width) * padded + i % width];
+}
+
+__global__ void unpack_geometry_kernel(int64_t Q, const float* __restrict__ grad_records,
+                                       const int64_t* __restrict__ prim_ids,
+                                       float* __restrict__ grad_geometry,
+                                       float* __restrict__ grad_opacities) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= Q * 18) return;
+    const int64_t q = i / 18;
+    const int k = int(i % 18);
+    const float v = grad_records[q * kRec + k];
+    if (k < 17) grad_geometry[q * 17 + k] = v;
+    else if (v != 0.f) atomicAdd(grad_opacities + prim_ids[q], v);
+}
+}  // namespace
+
+void set_error(const std::string& message) { g_last_error = message; }
+
+int fail(int code, const std::string& message) {
+    set_error(message);
+    return code;
+}
+
+int cuda_status(cudaError_t error, const char* what) {
+    return fail(GS_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(error));
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_version(void) { return 1; }
+
+extern "C" const char* gs_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int gs_pack_geometry(const float* geometry, const float* opacities,
+                                const int64_t* primitive_ids, int64_t Q, int64_t opacity_count,
+                                float* records, void* stream) {
+    if (Q < 0 || opacity_count < 0) return fail(GS_ERR_ARGUMENT, "gs_pack_geometry: invalid sizes");
+    if (Q == 0) return GS_OK;
+    pack_geometry_kernel<<<blocks_for(Q * kRec), kPackThreads, 0, as_stream(stream)>>>(
+        Q, geometry, opacities, primitive_ids, records);
+    GS_CHECK_LAUNCH("pack_geometry_kernel");
+    return GS_OK;
+}
+
+extern "C" int gs_pack_rows(const float* appearance, int64_t A, int width, float* rows, void* stream) {
+    if (A < 0 || (width != 18 && width != 57)) return fail(GS_ERR_ARGUMENT, "gs_pack_rows: invalid sizes");
+    if (A == 0) return GS_OK;
+    const int padded = width == 18 ? GS_CLASSIC_ROW_FLOATS : GS_NEURAL_ROW_FLOATS;
+    pack_rows_kernel<<<blocks_for(A * padded), kPackThreads, 0, as_stream(stream)>>>(
+        A, width, padded, appearance, rows);
+    GS_CHECK_LAUNCH("pack_rows_kernel");
+    return GS_OK;
+}
+
+extern "C" int gs_unpack_geometry_grads(const float* grad_records, const int64_t* primitive_ids,
+                                        int64_t Q, int64_t opacity_count, float* grad_geometry,
+                                        float* grad_opacities, void* stream) {
+    if (Q < 0 || opacity_count < 0) return fail(GS_ERR_ARGUMENT, "gs_unpack_geometry_grads: invalid sizes");
+    auto s = as_stream(stream);
+    if (opacity_count) GS_CUDA(cudaMemsetAsync(grad_opacities, 0, sizeof(float) * opacity_count, s));
+    if (Q == 0) return GS_OK;
+    unpack_geometry_kernel<<<blocks_for(Q * 18), kPackThreads, 0, s>>>(Q, grad_records, primitive_ids,
+                                                                        grad_geometry, grad_opacities);
+    GS_CHECK_LAUNCH("unpack_geometry_kernel");
+    return GS_OK;
+}
+
+extern "C" int gs_unpack_rows(const float* rows, int64_t A, int width, float* appearance, void* stream) {
+    if (A < 0 || (width != 18 && width != 57)) return fail(GS_ERR_ARGUMENT, "gs_unpack_rows: invalid sizes");
+    if (A == 0) return GS_OK;
+    const int padded = width == 18 ? GS_CLASSIC_ROW_FLOATS : GS_NEURAL_ROW_FLOATS;
+    unpack_rows_kernel<<<blocks_for(A * width), kPackThreads, 0, as_stream(stream)>>>(
+        A, width, padded, rows, appearance);
+    GS_CHECK_LAUNCH("unpack_rows_kernel");
+    return GS_OK;
+}

@@ -1,0 +1,633 @@
+// Tile compositor: front-to-back forward and reverse-order backward.
+//
+// One CTA of 16x16 threads per image tile, one thread per pixel, the tile's
+// depth-sorted record list walked in batches staged in shared memory.
+//   forward  restates renderForward  (rasterize.cu:229-281) with sampleSurface
+//            (:84-103) and appearanceForward (:105-138);
+//   backward restates renderBackward (rasterize.cu:283-399) with
+//            appearanceBackward (:146-197).
+// Per-pixel arithmetic follows the reference expression by expression (same
+// operation order, full-precision expf/sinf/cosf), so images agree to rounding.
+//
+// Differences, all in data movement:
+//   * records and appearance rows are 80/240-byte aligned rows staged with
+//     16-byte vector loads (the reference gathers scalars through two levels of
+//     indirection, :219-226);
+//   * opacity travels inside the record, so no per-primitive opacity gather;
+//   * backward gradients of one record are reduced across the warp with a
+//     reduce-scatter (each lane ends up owning one field: ~36 shuffles for 33
+//     fields instead of 5 per field), summed across the CTA's 8 warps in shared
+//     memory, and added to global memory once per (tile, record) -- 8x fewer
+//     global atomics than one per warp.
+#include "common.cuh"
+
+namespace gs {
+namespace {
+
+constexpr int kBatch = 64;
+constexpr int kClassicRow = GS_CLASSIC_ROW_FLOATS;
+constexpr int kNeuralRow = GS_NEURAL_ROW_FLOATS;
+
+struct Params {
+    const float4* records;
+    const float4* rows;
+    int row_mode;
+    const int64_t* prim_ids;
+    int64_t cameras, surfels;
+    const float* backgrounds;
+    const int* point_list;
+    const int2* ranges;
+    int width, height, tw, th;
+    float near_plane, far_plane;
+    // forward outputs / backward inputs
+    float* maps;
+    float* state;
+    int* contributors;
+    const float* grad_maps;
+    // backward outputs
+    float* grad_records;
+    float* grad_xy;
+    float* grad_rows;
+    float* grad_backgrounds;
+    // optional work counters: [0] samples tested, [1] contributions accepted
+    unsigned long long* counters;
+};
+
+// Add this thread's counts into the block total and then into counters[0..1].
+__device__ __forceinline__ void add_counts(unsigned long long* counters, unsigned tests,
+                                           unsigned accepts) {
+    __shared__ unsigned long long block_counts[2];
+    const int rank = threadIdx.y * blockDim.x + threadIdx.x;
+    if (rank < 2) block_counts[rank] = 0;
+    __syncthreads();
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        tests += __shfl_xor_sync(0xffffffffu, tests, o);
+        accepts += __shfl_xor_sync(0xffffffffu, accepts, o);
+    }
+    if ((rank & 31) == 0) {
+        atomicAdd(block_counts, (unsigned long long)tests);
+        atomicAdd(block_counts + 1, (unsigned long long)accepts);
+    }
+    __syncthreads();
+    if (rank < 2) atomicAdd(counters + rank, block_counts[rank]);
+}
+
+__device__ __forceinline__ int64_t row_of(const Params& P, int r) {
+    if (P.row_mode == GS_ROWS_PER_RECORD) return r;
+    if (P.row_mode == GS_ROWS_EXPLICIT) return P.prim_ids[r];
+    const int64_t n = r % P.surfels;
+    const int64_t s = r / (P.surfels * P.cameras);
+    return s * P.surfels + n;
+}
+
+template <bool Neural>
+struct Batch {
+    static constexpr int kRow = Neural ? kNeuralRow : kClassicRow;
+    int ids[kBatch];
+    int64_t rows[kBatch];
+    float4 geo[kBatch][kRec / 4];
+    float4 app[kBatch][kRow / 4];
+};
+
+// Stage `count` records (list positions first + stride*e) and their rows.
+template <bool Neural>
+__device__ __forceinline__ void load_batch(Batch<Neural>& b, const Params& P, int first, int stride,
+                                           int count, int rank) {
+    constexpr int kRow = Batch<Neural>::kRow;
+    constexpr int kPer = kRec / 4 + kRow / 4;
+    __syncthreads();
+    if (rank < count) {
+        const int id = P.point_list[first + stride * rank];
+        b.ids[rank] = id;
+        b.rows[rank] = row_of(P, id);
+    }
+    __syncthreads();
+    for (int i = rank; i < count * kPer; i += kBlock) {
+        const int e = i / kPer, part = i % kPer;
+        if (part < kRec / 4)
+            b.geo[e][part] = __ldg(P.records + int64_t(b.ids[e]) * (kRec / 4) + part);
+        else
+            b.app[e][part - kRec / 4] = __ldg(P.rows + b.rows[e] * (kRow / 4) + (part - kRec / 4));
+    }
+    __syncthreads();
+}
+
+struct Sample {
+    float k[3], l[3], p[3], s[2], depth, expo, alpha;
+    bool surface;
+};
+
+// Ray/plane intersection and filtered opacity: rasterize.cu:84-103.
+__device__ __forceinline__ bool sample_surface(const float* g, int x, int y, bool neural,
+                                               float near_plane, Sample& v) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        v.k[k] = x * g[6 + k] - g[k];
+        v.l[k] = y * g[6 + k] - g[3 + k];
+    }
+    cross3(v.k, v.l, v.p);
+    if (v.p[2] == 0) return false;
+    v.s[0] = v.p[0] / v.p[2];
+    v.s[1] = v.p[1] / v.p[2];
+    const float rho3 = v.s[0] * v.s[0] + v.s[1] * v.s[1];
+    const float dx = g[9] - x, dy = g[10] - y;
+    const float rho2 = 2 * (dx * dx + dy * dy);
+    v.surface = rho3 <= rho2;
+    v.depth = (neural || v.surface) ? v.s[0] * g[6] + v.s[1] * g[7] + g[8] : g[8];
+    if (v.depth < near_plane || !isfinite(v.depth)) return false;
+    v.expo = expf(-0.5f * fminf(rho3, rho2));
+    v.alpha = fminf(0.99f, g[17] * v.expo);
+    return v.alpha >= 1.0f / 255.0f;
+}
+
+// Frequency directions d_f = (cos(pi f/4), sin(pi f/4)) evaluated like the reference
+// (cosf/sinf of the float angle, rasterize.cu:128, 176).
+struct Directions {
+    float c[4], s[4];
+    __device__ __forceinline__ Directions() {
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+            c[f] = cosf(kPi * f / 4);
+            s[f] = sinf(kPi * f / 4);
+        }
+    }
+};
+
+// Appearance: rasterize.cu:105-138.
+template <bool Neural>
+__device__ __forceinline__ void appearance_forward(const float* a, const float* g, const Sample& v,
+                                                   const Directions& dirs, float* color,
+                                                   float* hidden, float* pre) {
+    if constexpr (Neural) {
+        const float input[5] = {v.s[0] / 3, v.s[1] / 3, g[14], g[15], g[16]};
+#pragma unroll
+        for (int h = 0; h < 6; ++h) {
+            float z = a[30 + h];
+#pragma unroll
+            for (int k = 0; k < 5; ++k) z += a[h * 5 + k] * input[k];
+            pre[h] = z;
+            hidden[h] = sinf(30 * z);
+        }
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            float z = a[54 + c];
+#pragma unroll
+            for (int h = 0; h < 6; ++h) z += a[36 + c * 6 + h] * hidden[h];
+            color[c] = 1 / (1 + expf(-z));
+        }
+    } else {
+        float h1 = 0, h2 = 0;
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+            const float dot = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
+            const float wave = cosf(2 * kPi * a[10 + f] * dot + a[14 + f]);
+            h1 += a[6 + f] * 0.5f * (1 + wave);
+            h2 += a[6 + f] * 0.5f * (1 - wave);
+        }
+#pragma unroll
+        for (int c = 0; c < 3; ++c) color[c] = h1 * a[c] + h2 * a[3 + c];
+    }
+}
+
+template <bool Neural, bool Count>
+__global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params P) {
+    unsigned tests = 0, accepts = 0;
+    __shared__ Batch<Neural> batch;
+    const int tiles_per_image = P.tw * P.th;
+    const int tile = blockIdx.x;
+    const int image = tile / tiles_per_image, local = tile % tiles_per_image;
+    const int x = (local % P.tw) * kTile + threadIdx.x, y = (local / P.tw) * kTile + threadIdx.y;
+    const int rank = threadIdx.y * kTile + threadIdx.x;
+    const bool inside = x < P.width && y < P.height;
+    bool done = !inside;
+    const int64_t pixel = (int64_t(image) * P.height + y) * P.width + x;
+    float out[kMaps] = {}, T = 1, m1 = 0, m2 = 0;
+    int last = 0;
+    const int2 range = P.ranges[tile];
+    const Directions dirs;
+    const float mscale = P.far_plane / (P.far_plane - P.near_plane);
+    for (int start = range.x; start < range.y; start += kBatch) {
+        if (__syncthreads_count(done) == kBlock) break;
+        const int count = min(kBatch, range.y - start);
+        load_batch<Neural>(batch, P, start, 1, count, rank);
+        for (int j = 0; j < count && !done; ++j) {
+            const float* g = reinterpret_cast<const float*>(batch.geo[j]);
+            Sample v;
+            if constexpr (Count) ++tests;
+            if (!sample_surface(g, x, y, Neural, P.near_plane, v)) continue;
+            const float next = T * (1 - v.alpha);
+            if (next < 0.0001f) { done = true; break; }
+            if constexpr (Count) ++accepts;
+            float color[3], hidden[6], pre[6];
+            appearance_forward<Neural>(reinterpret_cast<const float*>(batch.app[j]), g, v, dirs,
+                                       color, hidden, pre);
+            const float w = T * v.alpha;
+            const float m = mscale * (1 - P.near_plane / v.depth);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                out[c] += w * color[c];
+                out[5 + c] += w * g[11 + c];
+            }
+            out[4] += w * v.depth;
+            out[8] += w * (m * m * (1 - T) + m2 - 2 * m * m1);
+            m1 += w * m;
+            m2 += w * m * m;
+            T = next;
+            last = start + j - range.x + 1;
+        }
+    }
+    if (inside) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) out[c] += T * P.backgrounds[image * 3 + c];
+        out[3] = 1 - T;
+#pragma unroll
+        for (int c = 0; c < kMaps; ++c) P.maps[pixel * kMaps + c] = out[c];
+        P.state[pixel * 3] = T;
+        P.state[pixel * 3 + 1] = m1;
+        P.state[pixel * 3 + 2] = m2;
+        P.contributors[pixel] = last;
+    }
+    if constexpr (Count) add_counts(P.counters, tests, accepts);
+}
+
+// ------------------------------------------------------------------------------
+// backward
+// ------------------------------------------------------------------------------
+
+// Per-record gradient fields, packed: record slots (T 0-8, xy 9-10, normal 11-13,
+// [dir 14-16 neural]), opacity (record slot 17), then the appearance row.
+template <bool Neural>
+struct Fields {
+    static constexpr int kGeo = Neural ? 17 : 14;
+    static constexpr int kRow = Neural ? 57 : 18;
+    static constexpr int kCount = kGeo + 1 + kRow;            // 33 classic, 75 neural
+    static constexpr int kSlots = kRec + (Neural ? kNeuralRow : kClassicRow);   // 40 / 80
+    // packed field -> accumulator slot (record slots 0-19, row slots 20+)
+    static __device__ __forceinline__ int slot(int i) {
+        return i < kGeo ? i : (i == kGeo ? 17 : kRec + (i - kGeo - 1));
+    }
+};
+
+// Reduce `vals` across the warp and add each field's warp sum to acc[slot].
+template <bool Neural>
+__device__ __forceinline__ void warp_accumulate(float* vals, float* acc, int lane) {
+    using F = Fields<Neural>;
+    constexpr int kFull = F::kCount / 32;
+    constexpr int kRest = F::kCount - kFull * 32;
+#pragma unroll
+    for (int chunk = 0; chunk < kFull; ++chunk) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = vals[chunk * 32 + i];
+        warp_reduce_scatter<32>(v, lane);
+        if (v[0] != 0.f) atomicAdd(acc + F::slot(chunk * 32 + lane), v[0]);
+    }
+    if constexpr (kRest > 0) {
+        constexpr int kPad = kRest <= 1 ? 1 : kRest <= 2 ? 2 : kRest <= 4 ? 4 : kRest <= 8 ? 8
+                           : kRest <= 16 ? 16 : 32;
+        constexpr int kShift = kPad == 1 ? 5 : kPad == 2 ? 4 : kPad == 4 ? 3 : kPad == 8 ? 2
+                             : kPad == 16 ? 1 : 0;
+        float v[kPad];
+#pragma unroll
+        for (int i = 0; i < kPad; ++i) v[i] = i < kRest ? vals[kFull * 32 + i] : 0.f;
+        warp_reduce_scatter<kPad>(v, lane);
+        const int field = lane >> kShift;
+        if ((lane & ((1 << kShift) - 1)) == 0 && field < kRest && v[0] != 0.f)
+            atomicAdd(acc + F::slot(kFull * 32 + field), v[0]);
+    }
+}
+
+template <bool Neural, bool Count>
+__global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params P) {
+    unsigned tests = 0, accepts = 0;
+    using F = Fields<Neural>;
+    constexpr int kRow = Batch<Neural>::kRow;
+    __shared__ Batch<Neural> batch;
+    __shared__ float acc[kBatch * F::kSlots];
+    __shared__ int warp_max[kBlock / 32];
+    __shared__ float bg_acc[3];
+    const int lane = (threadIdx.y * kTile + threadIdx.x) & 31;
+    const int warp = (threadIdx.y * kTile + threadIdx.x) >> 5;
+    const int tiles_per_image = P.tw * P.th;
+    const int tile = blockIdx.x;
+    const int image = tile / tiles_per_image, local = tile % tiles_per_image;
+    const int x = (local % P.tw) * kTile + threadIdx.x, y = (local / P.tw) * kTile + threadIdx.y;
+    const int rank = threadIdx.y * kTile + threadIdx.x;
+    const bool inside = x < P.width && y < P.height;
+    const int64_t pixel = (int64_t(image) * P.height + y) * P.width + x;
+    const int last = inside ? P.contributors[pixel] : 0;
+    for (int i = rank; i < kBatch * F::kSlots; i += kBlock) acc[i] = 0.f;
+    if (rank < 3) bg_acc[rank] = 0.f;
+    int wmax = last;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
+    if (lane == 0) warp_max[warp] = wmax;
+    float go[kMaps] = {};
+    if (inside) {
+#pragma unroll
+        for (int c = 0; c < kMaps; ++c) go[c] = P.grad_maps[pixel * kMaps + c];
+    }
+    const float final_t = inside ? P.state[pixel * 3] : 0;
+    const float total_a = 1 - final_t;
+    const float m1 = inside ? P.state[pixel * 3 + 1] : 0, m2 = inside ? P.state[pixel * 3 + 2] : 0;
+    float T = final_t, suffix = 0, background_dot = 0;
+    {
+        float bgv[4] = {};
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            background_dot += go[c] * P.backgrounds[image * 3 + c];
+            bgv[c] = final_t * go[c];
+        }
+        warp_reduce_scatter<4>(bgv, lane);
+        __syncthreads();   // bg_acc and acc initialised
+        if ((lane & 7) == 0 && (lane >> 3) < 3 && bgv[0] != 0.f) atomicAdd(bg_acc + (lane >> 3), bgv[0]);
+    }
+    int block_last = 0;
+#pragma unroll
+    for (int w = 0; w < kBlock / 32; ++w) block_last = max(block_last, warp_max[w]);
+    const int2 range = P.ranges[tile];
+    const Directions dirs;
+    const float mscale = P.far_plane / (P.far_plane - P.near_plane);
+    for (int start = block_last; start > 0; start -= kBatch) {
+        const int count = min(kBatch, start);
+        load_batch<Neural>(batch, P, range.x + start - 1, -1, count, rank);
+        for (int j = 0; j < count; ++j) {
+            const float* g = reinterpret_cast<const float*>(batch.geo[j]);
+            const float* a = reinterpret_cast<const float*>(batch.app[j]);
+            Sample v;
+            bool active = inside && start - j <= last;
+            if constexpr (Count) tests += active;
+            if (active) active = sample_surface(g, x, y, Neural, P.near_plane, v);
+            if constexpr (Count) accepts += active;
+            if (!__any_sync(0xffffffffu, active)) continue;
+            float vals[F::kCount];
+#pragma unroll
+            for (int i = 0; i < F::kCount; ++i) vals[i] = 0.f;
+            float* gg = vals;                  // record fields 0..kGeo-1
+            float& gopacity = vals[F::kGeo];
+            float* ga = vals + F::kGeo + 1;    // appearance row fields
+            if (active) {
+                float color[3], hidden[6], pre[6], gc[3], gs[2] = {0.f, 0.f};
+                T /= 1 - v.alpha;
+                const float w = T * v.alpha;
+                appearance_forward<Neural>(a, g, v, dirs, color, hidden, pre);
+                const float m = mscale * (1 - P.near_plane / v.depth);
+                float gw = go[4] * v.depth + go[8] * (m * m * total_a + m2 - 2 * m * m1);
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    gw += go[c] * color[c] + go[5 + c] * g[11 + c];
+                    gc[c] = w * go[c];
+                    gg[11 + c] += w * go[5 + c];
+                }
+                const float galpha = T * gw - suffix / (1 - v.alpha) +
+                                     final_t * (go[3] - background_dot) / (1 - v.alpha);
+                suffix += w * gw;
+                // appearance backward: rasterize.cu:146-197
+                if constexpr (Neural) {
+                    const float input[5] = {v.s[0] / 3, v.s[1] / 3, g[14], g[15], g[16]};
+                    float gh[6] = {}, gi[5] = {};
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) {
+                        const float gz = gc[c] * color[c] * (1 - color[c]);
+                        ga[54 + c] += gz;
+#pragma unroll
+                        for (int h = 0; h < 6; ++h) {
+                            ga[36 + c * 6 + h] += gz * hidden[h];
+                            gh[h] += gz * a[36 + c * 6 + h];
+                        }
+                    }
+#pragma unroll
+                    for (int h = 0; h < 6; ++h) {
+                        const float gz = gh[h] * 30 * cosf(30 * pre[h]);
+                        ga[30 + h] += gz;
+#pragma unroll
+                        for (int k = 0; k < 5; ++k) {
+                            ga[h * 5 + k] += gz * input[k];
+                            gi[k] += gz * a[h * 5 + k];
+                        }
+                    }
+                    gs[0] += gi[0] / 3;
+                    gs[1] += gi[1] / 3;
+#pragma unroll
+                    for (int k = 0; k < 3; ++k) gg[14 + k] += gi[k + 2];
+                } else {
+#pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        const float dx = dirs.c[f], dy = dirs.s[f];
+                        const float dot = dx * v.s[0] + dy * v.s[1];
+                        const float angle = 2 * kPi * a[10 + f] * dot + a[14 + f];
+                        const float wave = cosf(angle);
+                        const float sine = sinf(angle);
+                        float gwf = 0, gt = 0;
+#pragma unroll
+                        for (int c = 0; c < 3; ++c) {
+                            ga[c] += gc[c] * a[6 + f] * 0.5f * (1 + wave);
+                            ga[3 + c] += gc[c] * a[6 + f] * 0.5f * (1 - wave);
+                            gwf += gc[c] * 0.5f * ((1 + wave) * a[c] + (1 - wave) * a[3 + c]);
+                            gt += gc[c] * a[6 + f] * 0.5f * sine * (a[3 + c] - a[c]);
+                        }
+                        ga[6 + f] += gwf;
+                        ga[10 + f] += gt * 2 * kPi * dot;
+                        ga[14 + f] += gt;
+                        gs[0] += gt * 2 * kPi * a[10 + f] * dx;
+                        gs[1] += gt * 2 * kPi * a[10 + f] * dy;
+                    }
+                }
+                // geometry: rasterize.cu:359-385
+                const float gz = w * go[4] + go[8] * 2 * w * (m * total_a - m1) * mscale *
+                                                 P.near_plane / (v.depth * v.depth);
+                if (Neural || v.surface) {
+                    gs[0] += gz * g[6];
+                    gs[1] += gz * g[7];
+                    gg[6] += gz * v.s[0];
+                    gg[7] += gz * v.s[1];
+                }
+                gg[8] += gz;
+                float grho = 0;
+                if (g[17] * v.expo < 0.99f) {
+                    gopacity = galpha * v.expo;
+                    grho = -0.5f * galpha * g[17] * v.expo;
+                }
+                if (v.surface) {
+                    gs[0] += 2 * v.s[0] * grho;
+                    gs[1] += 2 * v.s[1] * grho;
+                } else {
+                    gg[9] += 4 * (g[9] - x) * grho;
+                    gg[10] += 4 * (g[10] - y) * grho;
+                }
+                const float gp[3] = {gs[0] / v.p[2], gs[1] / v.p[2],
+                                     -(gs[0] * v.s[0] + gs[1] * v.s[1]) / v.p[2]};
+                float gk[3], gl[3];
+                cross3(v.l, gp, gk);
+                cross3(gp, v.k, gl);
+#pragma unroll
+                for (int k = 0; k < 3; ++k) {
+                    gg[k] -= gk[k];
+                    gg[3 + k] -= gl[k];
+                    gg[6 + k] += x * gk[k] + y * gl[k];
+                }
+            }
+            warp_accumulate<Neural>(vals, acc + j * F::kSlots, lane);
+        }
+        // flush this batch's per-record sums: one global atomic per (tile, record, field)
+        __syncthreads();
+        for (int i = rank; i < count * F::kSlots; i += kBlock) {
+            const float val = acc[i];
+            if (val == 0.f) continue;
+            acc[i] = 0.f;
+            const int e = i / F::kSlots, slot = i % F::kSlots;
+            if (slot < kRec) {
+                const int64_t r = batch.ids[e];
+                if (P.grad_xy && (slot == 9 || slot == 10))
+                    atomicAdd(P.grad_xy + r * 2 + (slot - 9), val);
+                else
+                    atomicAdd(P.grad_records + r * kRec + slot, val);
+            } else {
+                atomicAdd(P.grad_rows + batch.rows[e] * kRow + (slot - kRec), val);
+            }
+        }
+    }
+    __syncthreads();
+    if (rank < 3 && bg_acc[rank] != 0.f) atomicAdd(P.grad_backgrounds + image * 3 + rank, bg_acc[rank]);
+    if constexpr (Count) add_counts(P.counters, tests, accepts);
+}
+
+int check_composite(const char* fn, const float* records, const float* rows, int row_mode,
+                    const int64_t* prim_ids, int64_t cameras, int64_t surfels, int64_t R,
+                    const float* backgrounds, const int32_t* ranges, int64_t images, int width,
+                    int height) {
+    if (images < 1 || width < 1 || height < 1 || R < 0)
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": invalid sizes");
+    const int64_t tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    if (images * tw * th > INT_MAX)
+        return fail(GS_ERR_LIMIT, std::string(fn) + ": image tile count exceeds int32");
+    if (int64_t(width) * height * images * kMaps > (int64_t(1) << 62))
+        return fail(GS_ERR_LIMIT, std::string(fn) + ": image too large");
+    if (!backgrounds || !ranges) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": NULL buffer");
+    if (R > 0 && (!records || !rows)) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": NULL records");
+    if (reinterpret_cast<uintptr_t>(records) % 16 || reinterpret_cast<uintptr_t>(rows) % 16)
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": records and rows must be 16-byte aligned");
+    if (row_mode == GS_ROWS_EXPLICIT && R > 0 && !prim_ids)
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": primitive_ids is NULL");
+    if (row_mode == GS_ROWS_PER_SURFEL && R > 0 && (cameras < 1 || surfels < 1))
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": cameras and surfels must be positive");
+    if (row_mode < 0 || row_mode > 2) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": bad row mode");
+    return GS_OK;
+}
+
+}  // namespace
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_composite_forward(const float* records, const float* rows, int row_mode,
+                                    const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
+                                    int64_t records_count, int64_t rows_count,
+                                    const float* backgrounds, const int32_t* point_list,
+                                    const int32_t* ranges, int64_t images, int width, int height,
+                                    int neural, float near_plane, float far_plane, float* maps,
+                                    float* state, int32_t* contributors, uint64_t* counters,
+                                    void* stream) {
+    int st = check_composite("gs_composite_forward", records, rows, row_mode, primitive_ids, cameras,
+                             surfels, records_count, backgrounds, ranges, images, width, height);
+    if (st) return st;
+    (void)rows_count;
+    if (!maps || !state || !contributors) return fail(GS_ERR_ARGUMENT, "gs_composite_forward: NULL output");
+    Params P{};
+    P.records = reinterpret_cast<const float4*>(records);
+    P.rows = reinterpret_cast<const float4*>(rows);
+    P.row_mode = row_mode;
+    P.prim_ids = primitive_ids;
+    P.cameras = cameras;
+    P.surfels = surfels;
+    P.backgrounds = backgrounds;
+    P.point_list = point_list;
+    P.ranges = reinterpret_cast<const int2*>(ranges);
+    P.width = width;
+    P.height = height;
+    P.tw = (width + kTile - 1) / kTile;
+    P.th = (height + kTile - 1) / kTile;
+    P.near_plane = near_plane;
+    P.far_plane = far_plane;
+    P.maps = maps;
+    P.state = state;
+    P.contributors = contributors;
+    const int64_t tiles = images * P.tw * P.th;
+    auto s = as_stream(stream);
+    P.counters = reinterpret_cast<unsigned long long*>(counters);
+    const dim3 block(kTile, kTile);
+    if (neural && counters)
+        composite_forward_kernel<true, true><<<unsigned(tiles), block, 0, s>>>(P);
+    else if (neural)
+        composite_forward_kernel<true, false><<<unsigned(tiles), block, 0, s>>>(P);
+    else if (counters)
+        composite_forward_kernel<false, true><<<unsigned(tiles), block, 0, s>>>(P);
+    else
+        composite_forward_kernel<false, false><<<unsigned(tiles), block, 0, s>>>(P);
+    GS_CHECK_LAUNCH("composite_forward_kernel");
+    return GS_OK;
+}
+
+extern "C" int gs_composite_backward(const float* records, const float* rows, int row_mode,
+                                     const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
+                                     int64_t records_count, int64_t rows_count,
+                                     const float* backgrounds, const int32_t* point_list,
+                                     const int32_t* ranges, const float* state,
+                                     const int32_t* contributors, const float* grad_maps,
+                                     int64_t images, int width, int height, int neural,
+                                     float near_plane, float far_plane, float* grad_records,
+                                     float* grad_xy, float* grad_rows, float* grad_backgrounds,
+                                     uint64_t* counters, void* stream) {
+    int st = check_composite("gs_composite_backward", records, rows, row_mode, primitive_ids,
+                             cameras, surfels, records_count, backgrounds, ranges, images, width,
+                             height);
+    if (st) return st;
+    if (!state || !contributors || !grad_maps || !grad_backgrounds ||
+        (records_count > 0 && (!grad_records || !grad_rows)))
+        return fail(GS_ERR_ARGUMENT, "gs_composite_backward: NULL buffer");
+    auto s = as_stream(stream);
+    const int row = neural ? kNeuralRow : kClassicRow;
+    if (records_count > 0) {
+        GS_CUDA(cudaMemsetAsync(grad_records, 0, sizeof(float) * kRec * records_count, s));
+        GS_CUDA(cudaMemsetAsync(grad_rows, 0, sizeof(float) * row * rows_count, s));
+        if (grad_xy) GS_CUDA(cudaMemsetAsync(grad_xy, 0, sizeof(float) * 2 * records_count, s));
+    }
+    GS_CUDA(cudaMemsetAsync(grad_backgrounds, 0, sizeof(float) * 3 * images, s));
+    Params P{};
+    P.records = reinterpret_cast<const float4*>(records);
+    P.rows = reinterpret_cast<const float4*>(rows);
+    P.row_mode = row_mode;
+    P.prim_ids = primitive_ids;
+    P.cameras = cameras;
+    P.surfels = surfels;
+    P.backgrounds = backgrounds;
+    P.point_list = point_list;
+    P.ranges = reinterpret_cast<const int2*>(ranges);
+    P.width = width;
+    P.height = height;
+    P.tw = (width + kTile - 1) / kTile;
+    P.th = (height + kTile - 1) / kTile;
+    P.near_plane = near_plane;
+    P.far_plane = far_plane;
+    P.state = const_cast<float*>(state);
+    P.contributors = const_cast<int*>(contributors);
+    P.grad_maps = grad_maps;
+    P.grad_records = grad_records;
+    P.grad_xy = grad_xy;
+    P.grad_rows = grad_rows;
+    P.grad_backgrounds = grad_backgrounds;
+    const int64_t tiles = images * P.tw * P.th;
+    P.counters = reinterpret_cast<unsigned long long*>(counters);
+    const dim3 block(kTile, kTile);
+    if (neural && counters)
+        composite_backward_kernel<true, true><<<unsigned(tiles), block, 0, s>>>(P);
+    else if (neural)
+        composite_backward_kernel<true, false><<<unsigned(tiles), block, 0, s>>>(P);
+    else if (counters)
+        composite_backward_kernel<false, true><<<unsigned(tiles), block, 0, s>>>(P);
+    else
+        composite_backward_kernel<false, false><<<unsigned(tiles), block, 0, s>>>(P);
+    GS_CHECK_LAUNCH("composite_backward_kernel");
+    return GS_OK;
+}

@@ -1,0 +1,90 @@
+"""Algorithmic work per stage, for roofline fractions.
+
+Memory-bound stages are charged the bytes they must move (HBM roofline).  The
+compositor is charged floating-point work (FP32 roofline): per event constants
+counted from the kernel source (an FMA counts 2; expf/sinf/cosf and a divide count
+1 each), times event counts measured by the kernels' own counters.
+
+Events (per pixel and record):
+  test    ray/splat intersection + filtered opacity (sample_surface)        40 flop
+  accept  classic forward blend incl. 4-frequency appearance               100 flop
+          neural forward blend incl. the 5->6->3 SIREN                     156 flop
+  backward per tested sample                                                40 flop
+  backward per accepted sample: classic 400 flop, neural 520 flop
+          (forward replay + appearance and geometry adjoints)
+"""
+
+from __future__ import annotations
+
+import torch
+
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # 74.4, nominal (no measured figure)
+
+TEST_FLOP = 40
+ACCEPT_FLOP = {"classic": 100, "neural": 156}
+BACKWARD_ACCEPT_FLOP = {"classic": 400, "neural": 520}
+
+
+def count_work(fn, workload, values) -> dict:
+    """Run one render + backward with the kernels' counters on; return event counts."""
+    from . import rendering
+    from .workloads import loss_of
+
+    rendering.WORK = {}
+    try:
+        for v in values.values():
+            v.grad = None
+        rgb, alpha, meta = fn(**values, **workload.kwargs(), validate=False)
+        loss_of(rgb, alpha, meta, workload.depth_normal_loss).backward()
+        torch.cuda.synchronize()
+        work = rendering.WORK
+    finally:
+        rendering.WORK = None
+    out = {k: int(v) for k, v in work.items() if k != "_counters"}
+    for stage, t in work.get("_counters", []):
+        tests, accepts = (int(x) for x in t.tolist())
+        out[f"{stage}_tests"] = out.get(f"{stage}_tests", 0) + tests
+        out[f"{stage}_accepts"] = out.get(f"{stage}_accepts", 0) + accepts
+    for v in values.values():
+        v.grad = None
+    return out
+
+
+def stage_model(name: str, counts: dict, w) -> dict:
+    """{'bound', 'unit', 'work' (bytes or flop per launch), 'basis'} for one entry point."""
+    R = counts.get("records", 0)
+    I = counts.get("intersections", 0)
+    S, C, N = w.scenes, w.cameras, w.surfels
+    K = 0 if w.sh_degree is None else (w.sh_degree + 1) ** 2
+    pixels = w.pixels
+    if name == "gs_composite_forward":
+        flop = TEST_FLOP * counts.get("forward_tests", 0) + \
+            ACCEPT_FLOP[w.method] * counts.get("forward_accepts", 0)
+        return dict(bound="fp32", unit="TFLOP/s", work=flop,
+                    basis=f"{TEST_FLOP} flop/test x tests + {ACCEPT_FLOP[w.method]} flop/accept"
+                          " x accepts (kernel counters)")
+    if name == "gs_composite_backward":
+        flop = TEST_FLOP * counts.get("backward_tests", 0) + \
+            BACKWARD_ACCEPT_FLOP[w.method] * counts.get("backward_accepts", 0)
+        return dict(bound="fp32", unit="TFLOP/s", work=flop,
+                    basis=f"{TEST_FLOP} flop/test x tests + {BACKWARD_ACCEPT_FLOP[w.method]} "
+                          "flop/accept x accepts (kernel counters)")
+    if name == "gs_bin_sort":
+        # expand writes 8 B/slot; 2 onesweep passes read+write 8 B/slot each plus a 4 B
+        # histogram read; ranges read 4 B/slot
+        return dict(bound="hbm", unit="GB/s", work=I * (8 + 2 * 16 + 4 + 4),
+                    basis="48 B per tile intersection")
+    if name == "gs_bin_count":
+        return dict(bound="hbm", unit="GB/s", work=R * (8 + 4 * 16 + 4 + 8 + 16),
+                    basis="100 B per record (keys, 4-pass depth sort, counts, scan)")
+    surfel_in = 4 * (3 + 4 + 2 + 1 + (2 * K * 3 + 12 if K else 0))
+    if name == "gs_project_forward":
+        pair_out = 4 * (20 + 2 + 1 + (20 if K else 0))
+        return dict(bound="hbm", unit="GB/s", work=S * N * surfel_in + S * C * N * pair_out,
+                    basis=f"{surfel_in} B per surfel read + {pair_out} B per pair written")
+    if name == "gs_project_backward":
+        pair_in = 4 * (20 + 2 + (20 if K else 0))
+        return dict(bound="hbm", unit="GB/s",
+                    work=S * N * 2 * surfel_in + S * C * N * pair_in,
+                    basis=f"{pair_in} B per pair read + surfel inputs read and grads written")
+    return dict(bound="hbm", unit="GB/s", work=pixels * 4, basis="unmodelled")

@@ -1,0 +1,496 @@
+"""Public renderers with the reference's contracts, over the sm_100a kernels.
+
+Mirrors ``gabor_splatting.rendering`` of luisrodolfo10/diff_gabor_splatting v0.1.1
+(src/gabor_splatting/rendering.py): the same two public functions with the same
+signatures, defaults, validation messages, outputs and metadata, and the same
+module-level names tests reach into (``check_tensor``, ``check_values``,
+``SHColors``).  What changes is underneath: projection, SH colours and record
+packing run as one fused kernel (``gs_project_forward``) with a hand-derived
+reverse kernel instead of ~30 PyTorch ops and their autograd graph; binning and
+compositing run in libgabor_b200.so.  There is no CPU fallback: inputs must be
+CUDA float32, exactly as in the reference.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Any
+
+import torch
+from torch.autograd.function import once_differentiable
+
+from . import _native as nat
+
+TILE = 16
+
+# Work accounting for benchmarks: when WORK is a dict, the next renders record their
+# record and intersection counts and the compositors' sample/accept counters in it.
+WORK = None
+
+
+def _counters(stage: str, device) -> torch.Tensor | None:
+    if WORK is None:
+        return None
+    t = torch.zeros(2, dtype=torch.int64, device=device)
+    WORK.setdefault("_counters", []).append((stage, t))
+    return t
+
+
+# ----------------------------------------------------------------------------------
+# autograd bridges
+# ----------------------------------------------------------------------------------
+class Projection(torch.autograd.Function):
+    """Fused splat setup (rendering.py:156-218, 334-374) and its reverse kernel.
+
+    Returns per-pair records [P, 20], conic centres [P, 2], per-pair appearance rows
+    [P, 20] (SH mode; empty otherwise) and int32 radii [P] (not differentiable).
+    """
+
+    @staticmethod
+    def forward(ctx, means, quaternions, scales, opacities, view_matrices, intrinsics,
+                sh_first, sh_second, frequency_weights, frequency_magnitudes, phases,
+                sh_degree, width, height, near_plane, far_plane):
+        S, N = means.shape[0], means.shape[1]
+        C = view_matrices.shape[1]
+        P = S * C * N
+        device = means.device
+        records = torch.empty((P, nat.RECORD_FLOATS), device=device, dtype=torch.float32)
+        xy = torch.empty((P, 2), device=device, dtype=torch.float32)
+        radii = torch.empty((P,), device=device, dtype=torch.int32)
+        sh = sh_degree is not None
+        rows = torch.empty((P if sh else 0, nat.CLASSIC_ROW_FLOATS), device=device,
+                           dtype=torch.float32)
+        nat.call("gs_project_forward", nat.ptr(means), nat.ptr(quaternions), nat.ptr(scales),
+                 nat.ptr(opacities), nat.ptr(view_matrices), nat.ptr(intrinsics),
+                 nat.ptr(sh_first), nat.ptr(sh_second), nat.ptr(frequency_weights),
+                 nat.ptr(frequency_magnitudes), nat.ptr(phases),
+                 -1 if sh_degree is None else sh_degree, S, C, N, width, height,
+                 near_plane, far_plane, nat.ptr(records), nat.ptr(xy), nat.ptr(rows),
+                 nat.ptr(radii), nat.stream_of(device))
+        ctx.save_for_backward(means, quaternions, scales, view_matrices, intrinsics,
+                              sh_first, sh_second)
+        ctx.sh_degree = sh_degree
+        ctx.mark_non_differentiable(radii)
+        return records, xy, rows, radii
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_records, grad_xy, grad_rows, _grad_radii):
+        means, quaternions, scales, view_matrices, intrinsics, sh_first, sh_second = \
+            ctx.saved_tensors
+        S, N = means.shape[0], means.shape[1]
+        C = view_matrices.shape[1]
+        P = S * C * N
+        device = means.device
+        sh = ctx.sh_degree is not None
+        zeros = (lambda *shape: torch.zeros(shape, device=device, dtype=torch.float32))
+        if grad_records is None:
+            grad_records = zeros(P, nat.RECORD_FLOATS)
+        if grad_xy is None:
+            grad_xy = zeros(P, 2)
+        if sh and grad_rows is None:
+            grad_rows = zeros(P, nat.CLASSIC_ROW_FLOATS)
+        grad_records, grad_xy = grad_records.contiguous(), grad_xy.contiguous()
+        if grad_rows is not None:
+            grad_rows = grad_rows.contiguous()
+        g_means = torch.empty_like(means)
+        g_quats = torch.empty_like(quaternions)
+        g_scales = torch.empty_like(scales)
+        g_opac = torch.empty((S, N), device=device, dtype=torch.float32)
+        g_views = torch.empty_like(view_matrices)
+        g_intr = torch.empty_like(intrinsics)
+        g_sh1 = torch.empty_like(sh_first) if sh else None
+        g_sh2 = torch.empty_like(sh_second) if sh else None
+        g_w = torch.empty((S, N, 4), device=device) if sh else None
+        g_m = torch.empty((S, N, 4), device=device) if sh else None
+        g_p = torch.empty((S, N, 4), device=device) if sh else None
+        nat.call("gs_project_backward", nat.ptr(means), nat.ptr(quaternions), nat.ptr(scales),
+                 nat.ptr(view_matrices), nat.ptr(intrinsics), nat.ptr(sh_first),
+                 nat.ptr(sh_second), -1 if ctx.sh_degree is None else ctx.sh_degree, S, C, N,
+                 nat.ptr(grad_records), nat.ptr(grad_xy), nat.ptr(grad_rows), nat.ptr(g_means),
+                 nat.ptr(g_quats), nat.ptr(g_scales), nat.ptr(g_opac), nat.ptr(g_views),
+                 nat.ptr(g_intr), nat.ptr(g_sh1), nat.ptr(g_sh2), nat.ptr(g_w), nat.ptr(g_m),
+                 nat.ptr(g_p), nat.stream_of(device))
+        if N == 0:
+            g_means.zero_(), g_quats.zero_(), g_scales.zero_(), g_opac.zero_()
+            if sh:
+                g_w.zero_(), g_m.zero_(), g_p.zero_()
+        return (g_means, g_quats, g_scales, g_opac, g_views, g_intr, g_sh1, g_sh2, g_w, g_m,
+                g_p, None, None, None, None, None)
+
+
+class Composite(torch.autograd.Function):
+    """Tile compositor forward/backward (rasterize.cu:229-399) over binned records.
+
+    ``projected_means`` receives the screen-centre gradient (record slots 9-10), so it
+    can be inspected with ``retain_grad`` like the reference's.
+    """
+
+    @staticmethod
+    def forward(ctx, records, projected_means, rows, backgrounds, selected, point_list, ranges,
+                row_mode, cameras, surfels, images, width, height, neural, near_plane,
+                far_plane):
+        device = records.device
+        maps = torch.empty((images, height, width, 9), device=device, dtype=torch.float32)
+        state = torch.empty((images, height, width, 3), device=device, dtype=torch.float32)
+        contributors = torch.empty((images, height, width), device=device, dtype=torch.int32)
+        nat.call("gs_composite_forward", nat.ptr(records), nat.ptr(rows), row_mode, None,
+                 cameras, surfels, records.shape[0], rows.shape[0], nat.ptr(backgrounds),
+                 nat.ptr(point_list), nat.ptr(ranges), images, width, height, int(neural),
+                 near_plane, far_plane, nat.ptr(maps), nat.ptr(state), nat.ptr(contributors),
+                 nat.ptr(_counters("forward", device)), nat.stream_of(device))
+        ctx.save_for_backward(records, rows, backgrounds, selected, point_list, ranges, state,
+                              contributors)
+        ctx.options = (row_mode, cameras, surfels, images, width, height, neural, near_plane,
+                       far_plane)
+        return maps
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_maps):
+        records, rows, backgrounds, selected, point_list, ranges, state, contributors = \
+            ctx.saved_tensors
+        row_mode, cameras, surfels, images, width, height, neural, near_plane, far_plane = \
+            ctx.options
+        device = records.device
+        grad_maps = grad_maps.contiguous()
+        g_records = torch.empty_like(records)
+        g_xy = torch.empty((records.shape[0], 2), device=device, dtype=torch.float32)
+        g_rows = torch.empty_like(rows)
+        g_bg = torch.empty_like(backgrounds)
+        nat.call("gs_composite_backward", nat.ptr(records), nat.ptr(rows), row_mode, None,
+                 cameras, surfels, records.shape[0], rows.shape[0], nat.ptr(backgrounds),
+                 nat.ptr(point_list), nat.ptr(ranges), nat.ptr(state), nat.ptr(contributors),
+                 nat.ptr(grad_maps), images, width, height, int(neural), near_plane, far_plane,
+                 nat.ptr(g_records), nat.ptr(g_xy), nat.ptr(g_rows), nat.ptr(g_bg),
+                 nat.ptr(_counters("backward", device)), nat.stream_of(device))
+        if records.shape[0] == 0:
+            g_records.zero_(), g_xy.zero_(), g_rows.zero_()
+        g_pm = g_xy if selected is None else g_xy[selected]
+        return (g_records, g_pm, g_rows, g_bg) + (None,) * 12
+
+
+def bin_records(records, record_stride, radii, image_ids, records_per_image, images, width,
+                height):
+    """Depth-ordered per-tile record lists (rasterize.cu:454-493): point_list, ranges."""
+    device = records.device
+    stream = nat.stream_of(device)
+    R = records.shape[0]
+    tw, th = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
+    bytes1 = ctypes.c_size_t()
+    nat.call("gs_bin_count_workspace", R, ctypes.byref(bytes1))
+    ws1 = torch.empty((max(bytes1.value, 1),), device=device, dtype=torch.uint8)
+    total = ctypes.c_int64()
+    nat.call("gs_bin_count", nat.ptr(records), record_stride, nat.ptr(radii), nat.ptr(image_ids),
+             R, records_per_image, images, width, height, nat.ptr(ws1), bytes1.value,
+             ctypes.byref(total), stream)
+    intersections = total.value
+    if WORK is not None:
+        WORK["records"] = WORK.get("records", 0) + R
+        WORK["intersections"] = WORK.get("intersections", 0) + intersections
+        WORK["tiles"] = WORK.get("tiles", 0) + images * tw * th
+    bytes2 = ctypes.c_size_t()
+    nat.call("gs_bin_sort_workspace", R, intersections, images, width, height,
+             ctypes.byref(bytes2))
+    ws2 = torch.empty((max(bytes2.value, 1),), device=device, dtype=torch.uint8)
+    point_list = torch.empty((intersections,), device=device, dtype=torch.int32)
+    ranges = torch.empty((images * tw * th, 2), device=device, dtype=torch.int32)
+    nat.call("gs_bin_sort", nat.ptr(records), record_stride, nat.ptr(radii), nat.ptr(image_ids),
+             R, records_per_image, images, width, height, nat.ptr(ws1), bytes1.value,
+             nat.ptr(ws2), bytes2.value, intersections, nat.ptr(point_list), nat.ptr(ranges),
+             stream)
+    return point_list, ranges
+
+
+# ----------------------------------------------------------------------------------
+# contracts (rendering.py:74-153)
+# ----------------------------------------------------------------------------------
+def check_tensor(name: str, value: torch.Tensor, shape: tuple[int, ...],
+                 device: torch.device) -> None:
+    """Require a contiguous float32 CUDA tensor with an exact shape and device."""
+    if not isinstance(value, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if value.device != device or value.dtype != torch.float32 or not value.is_cuda:
+        raise ValueError(f"{name} must be float32 on {device}")
+    if value.shape != shape:
+        raise ValueError(f"{name} must have shape {shape}, got {tuple(value.shape)}")
+    if not value.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+@torch.no_grad()
+def check_values(tensors, quaternions, scales, opacities, view_matrices, intrinsics,
+                 appearance, neural):
+    """Validate the numerical contracts with one synchronisation (rendering.py:88-153).
+
+    Raises ValueError naming every violated contract, joined by "; ", in the
+    reference's order and wording.
+    """
+    checks = [(f"{name} must contain only finite values", torch.isfinite(t).all())
+              for name, (t, _) in tensors.items()]
+    eye = torch.eye(3, device=view_matrices.device, dtype=view_matrices.dtype)
+    rotation = view_matrices[..., :3, :3]
+    checks += [
+        ("scales must be strictly positive", (scales > 0).all()),
+        ("opacities must lie in [0, 1]", ((opacities >= 0) & (opacities <= 1)).all()),
+        ("quaternions must be unit wxyz vectors",
+         torch.isclose(quaternions.square().sum(-1), quaternions.new_tensor(1),
+                       atol=1e-4, rtol=1e-4).all()),
+        ("view_matrices must have last row [0, 0, 0, 1]",
+         torch.isclose(view_matrices[..., 3, :], view_matrices.new_tensor([0, 0, 0, 1])).all()),
+        ("intrinsics must have last row [0, 0, 1]",
+         torch.isclose(intrinsics[..., 2, :], intrinsics.new_tensor([0, 0, 1])).all()),
+        ("intrinsics fx and fy must be positive",
+         ((intrinsics[..., 0, 0] > 0) & (intrinsics[..., 1, 1] > 0)).all()),
+        ("view_matrices rotations must be orthonormal",
+         torch.isclose(rotation.transpose(-1, -2) @ rotation, eye, atol=1e-4, rtol=1e-4).all()),
+        ("view_matrices rotations must have determinant +1",
+         torch.isclose(torch.linalg.det(rotation), rotation.new_tensor(1),
+                       atol=1e-4, rtol=1e-4).all()),
+    ]
+    if not neural:
+        weights, magnitudes = appearance[2], appearance[3]
+        checks += [
+            ("frequency_weights must be nonnegative", (weights >= 0).all()),
+            ("frequency_magnitudes must be nonnegative", (magnitudes >= 0).all()),
+            ("frequency_weights must sum to one",
+             torch.isclose(weights.sum(-1), weights.new_tensor(1), atol=1e-4, rtol=1e-4).all()),
+        ]
+    passed = torch.stack([ok for _, ok in checks]).tolist()
+    if not all(passed):
+        raise ValueError("; ".join(message for (message, _), ok in zip(checks, passed) if not ok))
+
+
+class SHColors(torch.autograd.Function):
+    """Both SH colour sets per (scene, camera, surfel) pair (rendering.py:221-238).
+
+    first/second [B, N, K, 3], directions [B, C, N, 3] -> colours [B, C, N, 6].
+    """
+
+    @staticmethod
+    def forward(ctx, first, second, directions, degree):
+        _check_sh(first, second, directions, degree)
+        B, C, N = directions.shape[:3]
+        colors = torch.empty((B, C, N, 6), device=first.device, dtype=torch.float32)
+        nat.call("gs_sh_forward", nat.ptr(first), nat.ptr(second), nat.ptr(directions), degree,
+                 B, C, N, nat.ptr(colors), nat.stream_of(first.device))
+        ctx.save_for_backward(first, second, directions)
+        ctx.degree = degree
+        return colors
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_colors):
+        first, second, directions = ctx.saved_tensors
+        B, C, N = directions.shape[:3]
+        grad_colors = grad_colors.contiguous()
+        gf, gs, gd = (torch.zeros_like(first), torch.zeros_like(second),
+                      torch.zeros_like(directions))
+        nat.call("gs_sh_backward", nat.ptr(first), nat.ptr(second), nat.ptr(directions),
+                 nat.ptr(grad_colors), ctx.degree, B, C, N, nat.ptr(gf), nat.ptr(gs),
+                 nat.ptr(gd), nat.stream_of(first.device))
+        return gf, gs, gd, None
+
+
+def _check_sh(first, second, directions, degree):
+    """Structural SH checks (spherical_harmonics.cu:88-103), raising RuntimeError."""
+    if not (isinstance(degree, int) and 0 <= degree <= 3):
+        raise RuntimeError("SH degree must be 0 through 3")
+    for t in (first, second, directions):
+        if not (t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()
+                and t.device == first.device):
+            raise RuntimeError("SH tensors must be contiguous float32 on the same CUDA device")
+    if not (first.dim() == 4 and second.shape == first.shape
+            and first.shape[2] == (degree + 1) ** 2 and first.shape[3] == 3):
+        raise RuntimeError("SH coefficients must have shape [B, N, K, 3]")
+    if not (directions.dim() == 4 and directions.shape[0] == first.shape[0]
+            and directions.shape[2] == first.shape[1] and directions.shape[3] == 3):
+        raise RuntimeError("SH directions must have shape [B, C, N, 3]")
+
+
+# ----------------------------------------------------------------------------------
+# render (rendering.py:241-400)
+# ----------------------------------------------------------------------------------
+def render(means, quaternions, scales, opacities, appearance, view_matrices, intrinsics, width,
+           height, backgrounds, packed, near_plane, far_plane, neural, sh_degree, validate):
+    """Validate inputs, project scene/camera pairs, bin, and composite in one call."""
+    if not isinstance(means, torch.Tensor) or means.ndim < 2 or means.shape[-1] != 3:
+        raise ValueError("means must have shape [..., N, 3]")
+    if not means.is_cuda or means.dtype != torch.float32:
+        raise ValueError("means must be a CUDA float32 tensor")
+    if (type(width) is not int or type(height) is not int
+            or not (0 < width < 2**30 and 0 < height < 2**30)):
+        raise ValueError("width and height must be positive integers smaller than 2**30")
+    if (not math.isfinite(near_plane) or not math.isfinite(far_plane)
+            or not 0 < near_plane < far_plane):
+        raise ValueError("clipping planes must be finite and satisfy 0 < near_plane < far_plane")
+    if type(packed) is not bool:
+        raise TypeError("packed must be bool")
+    batch = tuple(means.shape[:-2])
+    n = means.shape[-2]
+    if not isinstance(view_matrices, torch.Tensor) or view_matrices.ndim != len(batch) + 3:
+        raise ValueError("view_matrices must have shape [..., C, 4, 4]")
+    cameras = view_matrices.shape[-3]
+    scenes = math.prod(batch)
+    if scenes < 1 or cameras < 1:
+        raise ValueError("scene and camera dimensions must be nonempty")
+    device = means.device
+    tensors = {
+        "means": (means, batch + (n, 3)),
+        "quaternions": (quaternions, batch + (n, 4)),
+        "scales": (scales, batch + (n, 2)),
+        "opacities": (opacities, batch + (n,)),
+        "view_matrices": (view_matrices, batch + (cameras, 4, 4)),
+        "intrinsics": (intrinsics, batch + (cameras, 3, 3)),
+    }
+    if backgrounds is None:
+        backgrounds = means.new_zeros(batch + (cameras, 3))
+    tensors["backgrounds"] = backgrounds, batch + (cameras, 3)
+    if neural:
+        shapes = [(6, 5), (6,), (3, 6), (3,)]
+        names = ["input_weights", "input_biases", "output_weights", "output_biases"]
+    else:
+        if sh_degree is not None and (type(sh_degree) is not int or not 0 <= sh_degree <= 3):
+            raise ValueError("sh_degree must be None or an integer from 0 to 3")
+        color_shape = (3,) if sh_degree is None else ((sh_degree + 1) ** 2, 3)
+        shapes = [color_shape, color_shape, (4,), (4,), (4,)]
+        names = ["colors", "secondary_colors", "frequency_weights", "frequency_magnitudes",
+                 "phases"]
+    for name, tensor, shape in zip(names, appearance, shapes):
+        tensors[name] = tensor, batch + (n,) + shape
+    for name, (tensor, shape) in tensors.items():
+        check_tensor(name, tensor, shape, device)
+    if type(validate) is not bool:
+        raise TypeError("validate must be bool")
+    if validate:
+        check_values(tensors, quaternions, scales, opacities, view_matrices, intrinsics,
+                     appearance, neural)
+    with torch.cuda.device(device):
+        return _render(means, quaternions, scales, opacities, appearance, view_matrices,
+                       intrinsics, width, height, backgrounds, packed, near_plane, far_plane,
+                       neural, sh_degree, batch, scenes, cameras, n)
+
+
+def _render(means, quaternions, scales, opacities, appearance, view_matrices, intrinsics, width,
+            height, backgrounds, packed, near_plane, far_plane, neural, sh_degree, batch, scenes,
+            cameras, n):
+    device = means.device
+    S, C, N = scenes, cameras, n
+    P = S * C * N
+    sh = sh_degree is not None
+    flat = (lambda t, *shape: t.reshape(S, *shape))
+    sh_args = (flat(appearance[0], N, (sh_degree + 1) ** 2, 3),
+               flat(appearance[1], N, (sh_degree + 1) ** 2, 3),
+               flat(appearance[2], N, 4), flat(appearance[3], N, 4),
+               flat(appearance[4], N, 4)) if sh else (None,) * 5
+    records, xy, sh_rows, radii = Projection.apply(
+        flat(means, N, 3), flat(quaternions, N, 4), flat(scales, N, 2), flat(opacities, N),
+        flat(view_matrices, C, 4, 4), flat(intrinsics, C, 3, 3), *sh_args, sh_degree, width,
+        height, float(near_plane), float(far_plane))
+    if sh:
+        rows, row_mode = sh_rows, nat.ROWS_PER_RECORD
+    elif neural:
+        rows = torch.cat([t.reshape(S * N, -1) for t in appearance]
+                         + [means.new_zeros((S * N, nat.NEURAL_ROW_FLOATS - 57))], -1)
+        row_mode = nat.ROWS_PER_SURFEL
+    else:
+        rows = torch.cat([t.reshape(S * N, -1) for t in appearance]
+                         + [means.new_zeros((S * N, nat.CLASSIC_ROW_FLOATS - 18))], -1)
+        row_mode = nat.ROWS_PER_SURFEL
+    images = S * C
+    point_list, ranges = bin_records(records, nat.RECORD_FLOATS, radii, None, max(N, 1), images,
+                                     width, height)
+    selected = None
+    projected_means = xy
+    if packed:
+        selected = torch.nonzero(radii > 0).reshape(-1)
+        projected_means = xy[selected]
+    maps = Composite.apply(records, projected_means, rows, backgrounds.reshape(-1, 3), selected,
+                           point_list, ranges, row_mode, C, max(N, 1), images, width, height,
+                           neural, float(near_plane), float(far_plane))
+    maps = maps.reshape(batch + (C, height, width, 9))
+    ids = selected if packed else torch.arange(P, device=device)
+    meta = {
+        "radii": radii[selected] if packed else radii.reshape(batch + (C, N)),
+        "projected_means": projected_means,
+        "scene_ids": ids // (C * max(N, 1)),
+        "camera_ids": ids // max(N, 1) % C,
+        "primitive_ids": ids % max(N, 1),
+        "packed": packed,
+        "accumulated_depth": maps[..., 4:5],
+        "normals": maps[..., 5:8],
+        "distortion": maps[..., 8:9],
+    }
+    return maps[..., :3], maps[..., 3:4], meta
+
+
+def rasterize_gabors(
+    means: torch.Tensor,
+    quaternions: torch.Tensor,
+    scales: torch.Tensor,
+    opacities: torch.Tensor,
+    colors: torch.Tensor,
+    secondary_colors: torch.Tensor,
+    frequency_weights: torch.Tensor,
+    frequency_magnitudes: torch.Tensor,
+    phases: torch.Tensor,
+    view_matrices: torch.Tensor,
+    intrinsics: torch.Tensor,
+    width: int,
+    height: int,
+    *,
+    backgrounds: torch.Tensor | None = None,
+    packed: bool = False,
+    near_plane: float = 0.2,
+    far_plane: float = 100.0,
+    sh_degree: int | None = None,
+    validate: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor, dict[str, Any]]:
+    """Render four-frequency Gabor surfaces over arbitrary scene and camera batches.
+
+    Same contract as the reference (rendering.py:403-456): means [..., N, 3], unit
+    wxyz quaternions [..., N, 4], positive scales [..., N, 2], opacities [..., N];
+    colors and secondary_colors [..., N, 3] (or [..., N, (degree+1)**2, 3] SH
+    coefficients with ``sh_degree``); frequency weights (summing to one),
+    magnitudes and phases [..., N, 4]; cameras [..., C, 4, 4] and [..., C, 3, 3].
+    All tensors contiguous CUDA float32.  Returns RGB [..., C, H, W, 3], alpha
+    [..., C, H, W, 1] and metadata (radii, projected_means, scene/camera/primitive
+    ids, packed, accumulated_depth, normals, distortion).
+    """
+    return render(means, quaternions, scales, opacities,
+                  (colors, secondary_colors, frequency_weights, frequency_magnitudes, phases),
+                  view_matrices, intrinsics, width, height, backgrounds, packed, near_plane,
+                  far_plane, False, sh_degree, validate)
+
+
+def rasterize_neural_gabors(
+    means: torch.Tensor,
+    quaternions: torch.Tensor,
+    scales: torch.Tensor,
+    opacities: torch.Tensor,
+    input_weights: torch.Tensor,
+    input_biases: torch.Tensor,
+    output_weights: torch.Tensor,
+    output_biases: torch.Tensor,
+    view_matrices: torch.Tensor,
+    intrinsics: torch.Tensor,
+    width: int,
+    height: int,
+    *,
+    backgrounds: torch.Tensor | None = None,
+    packed: bool = False,
+    near_plane: float = 0.2,
+    far_plane: float = 100.0,
+    validate: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor, dict[str, Any]]:
+    """Render per-surface 5->6->3 SIRENs (sine frequency 30, sigmoid RGB).
+
+    Same contract as the reference (rendering.py:459-502): per-primitive input
+    weights/biases [..., N, 6, 5] / [..., N, 6], output weights/biases
+    [..., N, 3, 6] / [..., N, 3]; network input (u/3, v/3, world view direction).
+    """
+    return render(means, quaternions, scales, opacities,
+                  (input_weights, input_biases, output_weights, output_biases),
+                  view_matrices, intrinsics, width, height, backgrounds, packed, near_plane,
+                  far_plane, True, None, validate)

@@ -1,0 +1,190 @@
+/*
+ * gabor_b200.h -- C ABI of the B200-native Gabor surface-splatting render path.
+ *
+ * One shared library (diff_gabor_splatting_b200/libgabor_b200.so, sm_100a).
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t passed
+ * as void*, launches asynchronously on that stream, allocates nothing, and returns
+ * an int status: 0 on success, otherwise one of GS_ERR_* with a message readable
+ * through gs_last_error() (per calling thread).  The only entry point that waits
+ * on the stream is gs_bin_count (it returns the number of tile intersections to
+ * the host, exactly as the reference does after its CUB scan).
+ *
+ * Reference interfaces replaced (luisrodolfo10/diff_gabor_splatting v0.1.1):
+ *   _C.rasterize_forward   src/gabor_splatting/csrc/rasterize.h:5-9,  rasterize.cu:425-503
+ *   _C.rasterize_backward  src/gabor_splatting/csrc/rasterize.h:10-15, rasterize.cu:505-529
+ *   _C.evaluate_sh_forward  rasterize.h:18-19, spherical_harmonics.cu:106-126
+ *   _C.evaluate_sh_backward rasterize.h:20-21, spherical_harmonics.cu:128-150
+ *   PyTorch projection/packing ops  src/gabor_splatting/rendering.py:156-218, 334-374
+ *
+ * Layouts (all row-major, float32 unless stated):
+ *   record  [R][20]  splat record per projected pair: T (3x3 homogeneous plane
+ *                    transform, 9), xy (conic centre, 2), normal (3), view dir (3),
+ *                    opacity (1), 2 zero pad.  80 bytes, 16-byte aligned.
+ *   classic appearance row [A][20]: colour (3), secondary colour (3), frequency
+ *                    weights (4), magnitudes (4), phases (4), 2 zero pad.
+ *   neural appearance row  [A][60]: W1 (6x5), b1 (6), W2 (3x6), b2 (3), 3 zero pad.
+ *   maps   [images][H][W][9]: rgb, alpha, accumulated depth, normal (3), distortion.
+ *   state  [images][H][W][3]: final transmittance, m1, m2.
+ *   ranges [images*tw*th][2] int32: [start, end) of each 16x16 tile's list.
+ */
+#ifndef GABOR_B200_H
+#define GABOR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GS_OK 0
+#define GS_ERR_ARGUMENT 1   /* invalid size, pointer or option */
+#define GS_ERR_LIMIT 2      /* a count exceeds an index range the kernels support */
+#define GS_ERR_CUDA 3       /* a CUDA runtime call or launch failed */
+#define GS_ERR_WORKSPACE 4  /* the workspace passed is smaller than required */
+
+#define GS_RECORD_FLOATS 20
+#define GS_CLASSIC_ROW_FLOATS 20
+#define GS_NEURAL_ROW_FLOATS 60
+
+/* Appearance-row addressing of a record r (gs_composite_*). */
+#define GS_ROWS_PER_RECORD 0   /* row = r */
+#define GS_ROWS_PER_SURFEL 1   /* r = (s*C + c)*N + n  ->  row = s*N + n */
+#define GS_ROWS_EXPLICIT 2     /* row = primitive_ids[r] (int64) */
+
+int gs_version(void);
+const char* gs_last_error(void);
+
+/* ---------------------------------------------------------------------------
+ * Fused projection.  Replaces rendering.py:156-218 (quaternion_matrix,
+ * project_surfaces), the SH colour launch rendering.py:334-340 and the record
+ * packing rendering.py:341-374 with one launch over (scene, surfel) threads that
+ * loop over the scene's cameras.  Pair index p = (s*C + c)*N + n.
+ *   sh_degree < 0: no SH; app_rows may be NULL.
+ *   sh_degree 0..3: both colours are evaluated per pair (spherical_harmonics.cu:
+ *   45-85) and written with the surfel's weights/magnitudes/phases into
+ *   app_rows[p] (classic appearance row layout).
+ * Outputs: records[P][20], xy[P][2], radii[P] (int32, 0 = culled).
+ */
+int gs_project_forward(const float* means, const float* quaternions, const float* scales,
+                       const float* opacities, const float* view_matrices,
+                       const float* intrinsics, const float* sh_first,
+                       const float* sh_second, const float* frequency_weights,
+                       const float* frequency_magnitudes, const float* phases,
+                       int sh_degree, int64_t scenes, int64_t cameras, int64_t surfels,
+                       int width, int height, float near_plane, float far_plane,
+                       float* records, float* xy, float* app_rows, int32_t* radii,
+                       void* stream);
+
+/* Reverse of gs_project_forward (the PyTorch autograd of rendering.py:156-218,
+ * 334-374 and spherical_harmonics.cu:128-150).  grad_records[P][20] (slots 9-10
+ * ignored), grad_xy[P][2], grad_app_rows[P][20] (SH mode).  Surfel gradients are
+ * summed over cameras in registers; camera gradients are reduced per block and
+ * added with atomics.  Every output is overwritten (zeroed first on the stream). */
+int gs_project_backward(const float* means, const float* quaternions, const float* scales,
+                        const float* view_matrices, const float* intrinsics,
+                        const float* sh_first, const float* sh_second, int sh_degree,
+                        int64_t scenes, int64_t cameras, int64_t surfels,
+                        const float* grad_records, const float* grad_xy,
+                        const float* grad_app_rows, float* grad_means,
+                        float* grad_quaternions, float* grad_scales,
+                        float* grad_opacities, float* grad_view_matrices,
+                        float* grad_intrinsics, float* grad_sh_first,
+                        float* grad_sh_second, float* grad_frequency_weights,
+                        float* grad_frequency_magnitudes, float* grad_phases,
+                        void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Tile binning (rasterize.cu:23-69, 454-493).  Two phases around the one host
+ * synchronisation the reference also has (rasterize.cu:466-468):
+ *   gs_bin_count : depth-sort the records, count tiles, scan; returns the
+ *                  intersection count I to the host (waits on the stream).
+ *   gs_bin_sort  : expand (tile, record) pairs in depth order, stable-sort by
+ *                  tile, write point_list[I] (record indices) and ranges.
+ * The result is identical to the reference's stable 64-bit (tile << 32 | depth
+ * bits) sort: within a tile, records are ordered by depth bits, then index.
+ * records: float rows of `record_stride` floats (x, y at 9-10, depth at 8);
+ * image_ids: int64 per record, or NULL for image = r / records_per_image.
+ * Workspace 1 must stay untouched between the two calls.
+ */
+int gs_bin_count_workspace(int64_t records, size_t* bytes);
+int gs_bin_count(const float* records, int record_stride, const int32_t* radii,
+                 const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
+                 int64_t images, int width, int height, void* workspace1,
+                 size_t workspace1_bytes, int64_t* intersections, void* stream);
+int gs_bin_sort_workspace(int64_t records, int64_t intersections, int64_t images,
+                          int width, int height, size_t* bytes);
+int gs_bin_sort(const float* records, int record_stride, const int32_t* radii,
+                const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
+                int64_t images, int width, int height, const void* workspace1,
+                size_t workspace1_bytes, void* workspace2, size_t workspace2_bytes,
+                int64_t intersections, int32_t* point_list, int32_t* ranges, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Tile compositor.  Forward: renderForward (rasterize.cu:229-281); backward:
+ * renderBackward (rasterize.cu:283-399).  One CTA per 16x16 tile.
+ * row_mode selects the appearance row of a record (GS_ROWS_*); `cameras`,
+ * `surfels` are used by GS_ROWS_PER_SURFEL, primitive_ids by GS_ROWS_EXPLICIT.
+ * Backward adds into grad_records / grad_rows / grad_backgrounds, which it zeroes
+ * first; grad_xy (nullable, [R][2]) receives the slot 9-10 (screen-centre)
+ * gradients instead of grad_records when given.
+ * counters (nullable, uint64[2], zeroed by the caller) receives the work done:
+ * [0] ray/splat samples tested, [1] contributions accepted (blended forward,
+ * differentiated backward).  A NULL pointer selects kernels without counting.
+ */
+int gs_composite_forward(const float* records, const float* rows, int row_mode,
+                         const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
+                         int64_t records_count, int64_t rows_count,
+                         const float* backgrounds, const int32_t* point_list,
+                         const int32_t* ranges, int64_t images, int width, int height,
+                         int neural, float near_plane, float far_plane, float* maps,
+                         float* state, int32_t* contributors, uint64_t* counters,
+                         void* stream);
+int gs_composite_backward(const float* records, const float* rows, int row_mode,
+                          const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
+                          int64_t records_count, int64_t rows_count,
+                          const float* backgrounds, const int32_t* point_list,
+                          const int32_t* ranges, const float* state,
+                          const int32_t* contributors, const float* grad_maps,
+                          int64_t images, int width, int height, int neural,
+                          float near_plane, float far_plane, float* grad_records,
+                          float* grad_xy, float* grad_rows, float* grad_backgrounds,
+                          uint64_t* counters, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Layout converters for the reference-layout entry points (the `_C` mirror).
+ * gs_pack_geometry: geometry[Q][17] + opacities[primitive_ids[q]] -> records[Q][20].
+ * gs_pack_rows:     appearance[A][width] (18 or 57) -> rows[A][20 or 60].
+ * gs_unpack_geometry_grads: grad_records[Q][20] -> grad_geometry[Q][17] and
+ *                   grad_opacities[primitive_ids[q]] += slot 17 (zeroed first).
+ * gs_unpack_rows:   rows[A][20 or 60] -> appearance[A][width].
+ */
+int gs_pack_geometry(const float* geometry, const float* opacities,
+                     const int64_t* primitive_ids, int64_t records_count,
+                     int64_t opacity_count, float* records, void* stream);
+int gs_pack_rows(const float* appearance, int64_t rows_count, int width, float* rows,
+                 void* stream);
+int gs_unpack_geometry_grads(const float* grad_records, const int64_t* primitive_ids,
+                             int64_t records_count, int64_t opacity_count,
+                             float* grad_geometry, float* grad_opacities, void* stream);
+int gs_unpack_rows(const float* rows, int64_t rows_count, int width, float* appearance,
+                   void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Spherical-harmonic colours (spherical_harmonics.cu:45-150) for the
+ * SHColors entry points.  first/second [B][N][K][3], directions [B][C][N][3],
+ * colors [B][C][N][6].  Backward overwrites its three outputs; coefficient
+ * gradients are summed over cameras in registers (no atomics).
+ */
+int gs_sh_forward(const float* first, const float* second, const float* directions,
+                  int degree, int64_t scenes, int64_t cameras, int64_t surfels,
+                  float* colors, void* stream);
+int gs_sh_backward(const float* first, const float* second, const float* directions,
+                   const float* grad_colors, int degree, int64_t scenes, int64_t cameras,
+                   int64_t surfels, float* grad_first, float* grad_second,
+                   float* grad_directions, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GABOR_B200_H */

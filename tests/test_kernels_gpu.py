@@ -1,0 +1,208 @@
+"""Stage-by-stage parity of the sm_100a kernels with the CPU oracle.
+
+Multi-tile, multi-camera scenes (config-0 style inputs).  Each stage is checked on
+identical inputs: projection (floats to rounding, radii exact), binning (point
+lists and tile ranges bit-exact given the same records), forward compositing
+(maps within 1e-5 relative / 1e-6 absolute, contributor counts exact), and the whole
+forward + backward against the oracle's float64 autograd.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from diff_gabor_splatting_b200 import rasterize_gabors, rasterize_neural_gabors
+from diff_gabor_splatting_b200 import _C as native_c
+from diff_gabor_splatting_b200 import rendering
+from helpers import appearance_names, maps_from_result, ordered, random_scene
+from oracle import gabor_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+W, H = 70, 45   # partial edge tiles on both axes
+
+
+def project(v, sh_degree=None, width=W, height=H):
+    S, N = v["means"].shape[:2]
+    app = [v[k] for k in appearance_names("classic")] if sh_degree is not None else [None] * 5
+    with torch.no_grad():
+        return rendering.Projection.apply(
+            v["means"], v["quaternions"], v["scales"], v["opacities"], v["view_matrices"],
+            v["intrinsics"], *app, sh_degree, width, height, 0.2, 100.0)
+
+
+@pytest.mark.parametrize("sh_degree", [None, 3])
+def test_projection_matches_oracle(sh_degree):
+    v = random_scene(scenes=2, cameras=3, n=300, width=W, height=H, sh_degree=sh_degree)
+    records, xy, rows, radii = project(v, sh_degree)
+    cpu = {k: t.cpu() for k, t in v.items()}
+    T, xy_o, normals, dirs, radii_o = O.project_surfaces(
+        cpu["means"], cpu["quaternions"], cpu["scales"], cpu["view_matrices"],
+        cpu["intrinsics"], W, H, 0.2, 100.0)
+    rec = records.cpu()
+    torch.testing.assert_close(rec[:, :9], T.reshape(-1, 9), rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(rec[:, 9:11], xy_o.reshape(-1, 2), rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(xy.cpu(), xy_o.reshape(-1, 2), rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(rec[:, 11:14], normals.reshape(-1, 3), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(rec[:, 14:17], dirs.reshape(-1, 3), rtol=1e-5, atol=1e-6)
+    S, N = v["means"].shape[:2]
+    C = v["view_matrices"].shape[1]
+    opac = cpu["opacities"].reshape(S, 1, N).expand(S, C, N).reshape(-1)
+    assert torch.equal(rec[:, 17], opac)
+    assert torch.equal(radii.cpu(), radii_o.reshape(-1))
+    if sh_degree is not None:
+        colors = O.evaluate_sh(cpu["colors"], cpu["secondary_colors"], dirs, sh_degree)
+        torch.testing.assert_close(rows.cpu()[:, :6], colors.reshape(-1, 6), rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("scenes,cameras", [(1, 1), (2, 3)])
+def test_binning_bit_exact(scenes, cameras):
+    """Point lists and tile ranges equal the reference's stable 64-bit key sort."""
+    v = random_scene(scenes=scenes, cameras=cameras, n=400, width=W, height=H)
+    records, xy, rows, radii = project(v)
+    N = v["means"].shape[1]
+    images = scenes * cameras
+    point_list, ranges = rendering.bin_records(records, 20, radii, None, N, images, W, H)
+    image_ids = torch.arange(records.shape[0]) // N
+    expect = O.bin_tiles(records[:, :17].cpu(), radii.cpu(), image_ids, images, W, H)
+    assert point_list.shape[0] == expect["point_list"].shape[0]
+    np.testing.assert_array_equal(point_list.cpu().numpy(), expect["point_list"])
+    np.testing.assert_array_equal(ranges.cpu().numpy(), expect["ranges"])
+
+
+def _oracle_inputs(v, records, rows, method):
+    """Per-record oracle inputs built from the kernel's records (identical geometry)."""
+    S, N = v["means"].shape[:2]
+    C = v["view_matrices"].shape[1]
+    P = S * C * N
+    rec = records.cpu()
+    p = torch.arange(P)
+    prim = (p // (C * N)) * N + p % N
+    width = 57 if method == "neural" else 18
+    appearance = rows.cpu()[prim][:, :width]
+    return rec[:, :17], appearance, rec[:, 17], p
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_composite_forward_matches_oracle(method):
+    v = random_scene(method, scenes=1, cameras=2, n=300, width=W, height=H)
+    records, xy, rows_sh, radii = project(v)
+    S, N = v["means"].shape[:2]
+    C = v["view_matrices"].shape[1]
+    images = S * C
+    rows = torch.cat([v[k].reshape(S * N, -1) for k in appearance_names(method)]
+                     + [torch.zeros(S * N, 3 if method == "neural" else 2, device="cuda")], -1)
+    point_list, ranges = rendering.bin_records(records, 20, radii, None, N, images, W, H)
+    maps = torch.empty(images, H, W, 9, device="cuda")
+    state = torch.empty(images, H, W, 3, device="cuda")
+    contrib = torch.empty(images, H, W, dtype=torch.int32, device="cuda")
+    from diff_gabor_splatting_b200 import _native as nat
+    nat.call("gs_composite_forward", nat.ptr(records), nat.ptr(rows), nat.ROWS_PER_SURFEL, None,
+             C, N, records.shape[0], rows.shape[0], nat.ptr(v["backgrounds"]),
+             nat.ptr(point_list), nat.ptr(ranges), images, W, H, int(method == "neural"), 0.2,
+             100.0, nat.ptr(maps), nat.ptr(state), nat.ptr(contrib), None,
+             nat.stream_of(records.device))
+    geometry, appearance, opacities, prim_ids = _oracle_inputs(v, records, rows, method)
+    out = O.composite(geometry, appearance, opacities, prim_ids,
+                      v["backgrounds"].reshape(-1, 3).cpu(), point_list.cpu().numpy(),
+                      ranges.cpu().numpy(), W, H, method == "neural", 0.2, 100.0)
+    exp_maps = O.tiles_to_images(out["maps"], images, W, H)
+    exp_contrib = O.tiles_to_images(out["contributors"], images, W, H)
+    exp_state = O.tiles_to_images(out["state"], images, W, H)
+    torch.testing.assert_close(maps.cpu(), exp_maps, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(state.cpu(), exp_state, rtol=1e-5, atol=1e-6)
+    mismatch = (contrib.cpu() != exp_contrib).float().mean().item()
+    assert mismatch <= 1e-3, f"contributor counts differ on {mismatch:.2%} of pixels"
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+@pytest.mark.parametrize("packed", [False, True])
+def test_render_forward_backward_matches_float64_oracle(method, packed):
+    """Whole public call, images and every input gradient vs the float64 oracle."""
+    v = random_scene(method, scenes=2, cameras=2, n=120, width=W, height=H)
+    values = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    fn = rasterize_gabors if method == "classic" else rasterize_neural_gabors
+    actual = maps_from_result(fn(**values, width=W, height=H, packed=packed))
+    leaves = {k: t.detach().cpu().double().requires_grad_() for k, t in values.items()}
+    rgb, alpha, meta = O.render(leaves["means"], leaves["quaternions"], leaves["scales"],
+                                leaves["opacities"],
+                                [leaves[k] for k in appearance_names(method)],
+                                leaves["view_matrices"], leaves["intrinsics"], W, H,
+                                backgrounds=leaves["backgrounds"], packed=packed,
+                                neural=method == "neural", dtype=torch.float64)
+    expected = maps_from_result((rgb, alpha, meta))
+    torch.testing.assert_close(actual.cpu().double(), expected.detach(), rtol=1e-4, atol=2e-5)
+    weights = torch.linspace(-0.4, 0.7, actual.numel(), dtype=torch.float64).reshape(
+        actual.shape)
+    ag = torch.autograd.grad((actual * weights.cuda().float()).sum(), tuple(values.values()))
+    eg = torch.autograd.grad((expected * weights).sum(), tuple(leaves.values()))
+    for name, a, e in zip(values, ag, eg):
+        scale = e.abs().max().item() + 1e-12
+        err = (a.cpu().double() - e).abs().max().item() / scale
+        assert err < 2e-3, f"{name}: max error {err:.2e} of the gradient's scale"
+
+
+@pytest.mark.parametrize("degree", [1, 3])
+def test_sh_render_dense_packed_and_grads(degree):
+    v = random_scene("classic", scenes=1, cameras=3, n=150, width=W, height=H,
+                     sh_degree=degree)
+    values = {k: t.clone().requires_grad_() for k, t in ordered(v, "classic").items()}
+    dense = maps_from_result(rasterize_gabors(**values, width=W, height=H, sh_degree=degree))
+    leaves = {k: t.detach().cpu().double().requires_grad_() for k, t in values.items()}
+    rgb, alpha, meta = O.render(leaves["means"], leaves["quaternions"], leaves["scales"],
+                                leaves["opacities"],
+                                [leaves[k] for k in appearance_names("classic")],
+                                leaves["view_matrices"], leaves["intrinsics"], W, H,
+                                backgrounds=leaves["backgrounds"], sh_degree=degree,
+                                dtype=torch.float64)
+    expected = maps_from_result((rgb, alpha, meta))
+    torch.testing.assert_close(dense.cpu().double(), expected.detach(), rtol=1e-4, atol=2e-5)
+    ag = torch.autograd.grad(dense.sum(), tuple(values.values()))
+    eg = torch.autograd.grad(expected.sum(), tuple(leaves.values()))
+    for name, a, e in zip(values, ag, eg):
+        scale = e.abs().max().item() + 1e-12
+        err = (a.cpu().double() - e).abs().max().item() / scale
+        assert err < 2e-3, f"{name}: max error {err:.2e} of the gradient's scale"
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_reference_layout_entry_points(method):
+    """The `_C`-layout mirror (rasterize_forward/backward) on oracle-packed records."""
+    v = random_scene(method, scenes=1, cameras=2, n=200, width=W, height=H)
+    cpu = {k: t.cpu() for k, t in v.items()}
+    T, xy, normals, dirs, radii = O.project_surfaces(
+        cpu["means"], cpu["quaternions"], cpu["scales"], cpu["view_matrices"],
+        cpu["intrinsics"], W, H, 0.2, 100.0)
+    rec = O.pack(T, xy, normals, dirs, radii, cpu["opacities"],
+                 [cpu[k] for k in appearance_names(method)], method == "neural", None, True)
+    args = [rec[k].cuda().contiguous() for k in ("geometry", "parameters", "opacities",
+                                                   "primitive_ids", "image_ids", "radii")]
+    bg = v["backgrounds"].reshape(-1, 3).contiguous()
+    maps, point_list, ranges, state, contrib = native_c.rasterize_forward(
+        *args, bg, W, H, method == "neural", 0.2, 100.0)
+    expect = O.bin_tiles(rec["geometry"], rec["radii"], rec["image_ids"], 2, W, H)
+    np.testing.assert_array_equal(point_list.cpu().numpy(), expect["point_list"])
+    np.testing.assert_array_equal(ranges.cpu().numpy(), expect["ranges"])
+    out = O.composite(rec["geometry"], rec["parameters"], rec["opacities"], rec["primitive_ids"],
+                      bg.cpu(), expect["point_list"], expect["ranges"], W, H,
+                      method == "neural", 0.2, 100.0)
+    torch.testing.assert_close(maps.cpu(), O.tiles_to_images(out["maps"], 2, W, H),
+                               rtol=1e-5, atol=1e-6)
+    grad_maps = torch.randn(maps.shape, generator=torch.Generator().manual_seed(3)).cuda()
+    gg, ga, go, gb = native_c.rasterize_backward(args[0], args[1], args[2], args[3], bg,
+                                                 point_list, ranges, state, contrib, grad_maps,
+                                                 W, H, method == "neural", 0.2, 100.0)
+    leaves = [rec["geometry"].detach().double().requires_grad_(),
+              rec["parameters"].detach().double().requires_grad_(),
+              rec["opacities"].detach().double().requires_grad_(),
+              bg.cpu().double().requires_grad_()]
+    out64 = O.composite(leaves[0], leaves[1], leaves[2], rec["primitive_ids"], leaves[3],
+                        expect["point_list"], expect["ranges"], W, H, method == "neural", 0.2,
+                        100.0, dtype=torch.float64)
+    m64 = O.tiles_to_images(out64["maps"], 2, W, H)
+    eg = torch.autograd.grad((m64 * grad_maps.cpu().double()).sum(), leaves)
+    for name, a, e in zip(["geometry", "appearance", "opacities", "backgrounds"],
+                          (gg, ga, go, gb), eg):
+        scale = e.abs().max().item() + 1e-12
+        err = (a.cpu().double() - e).abs().max().item() / scale
+        assert err < 1e-3, f"{name}: max error {err:.2e} of the gradient's scale"

@@ -1,0 +1,262 @@
+"""Public-API parity on the GPU, restating the reference test suite.
+
+Cases and tolerances follow tests/test_rendering.py of the reference (v0.1.1).  The
+expected images and input gradients are the reference's own float64 test oracle,
+run in the build container and stored in tests/golden/render.npz; other cases check
+the same invariants the reference checks (fused == per-view loop, dense == packed,
+empty scenes, degenerate surfaces, validation paths, finite differences).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from diff_gabor_splatting_b200 import rasterize_gabors, rasterize_neural_gabors
+from helpers import golden_cases, maps_from_result, ordered, small_inputs
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = golden_cases()
+# (maps atol, maps rtol, grads atol, grads rtol) per golden case, as in the reference tests
+TOLERANCE = {
+    "basic": (3e-6, 2e-5, 2e-3, 8e-4),       # test_reference_outputs_and_gradients
+    "scenes2": (3e-6, 2e-5, 2e-3, 8e-4),
+    "batch65": (4e-6, 3e-5, 2e-3, 1e-3),     # test_shared_batch_boundary_matches_reference
+    "opacity0": (3e-6, 3e-5, 2e-3, 2e-3),    # test_opacity_cutoff_and_saturation
+    "opacity1": (3e-6, 3e-5, 2e-3, 2e-3),
+    "tiny": (2e-5, 2e-4, 5e-3, 2e-3),        # test_tiny_surfaces_use_lowpass_filter
+}
+
+
+def renderer(method):
+    return rasterize_gabors if method == "classic" else rasterize_neural_gabors
+
+
+@pytest.mark.parametrize("packed", [False, True])
+@pytest.mark.parametrize("case", sorted(GOLDEN))
+def test_golden_outputs_and_gradients(case, packed):
+    """Images and every input gradient against the reference's float64 oracle."""
+    method, loss, inputs, maps, grads = GOLDEN[case]
+    values = {k: torch.from_numpy(v).cuda().requires_grad_() for k, v in inputs.items()}
+    values = ordered(values, method)
+    actual = maps_from_result(renderer(method)(**values, width=9, height=9, packed=packed))
+    expected = torch.from_numpy(maps).cuda()
+    atol, rtol, gatol, grtol = TOLERANCE[case.split("_", 1)[1]]
+    torch.testing.assert_close(actual.double(), expected, atol=atol, rtol=rtol)
+    if loss == "weighted":
+        weights = torch.linspace(-0.4, 0.7, actual.numel(), device="cuda").reshape(actual.shape)
+        objective = (actual * weights).sum()
+    else:
+        objective = actual.sum()
+    actual_grads = torch.autograd.grad(objective, tuple(values.values()), allow_unused=True)
+    for (name, value), grad in zip(values.items(), actual_grads):
+        grad = torch.zeros_like(value) if grad is None else grad
+        torch.testing.assert_close(grad.double(), torch.from_numpy(grads[name]).cuda(),
+                                   atol=gatol, rtol=grtol, msg=name)
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+@pytest.mark.parametrize("packed", [False, True])
+def test_scene_camera_batch_matches_loop(method, packed):
+    """Multiple scenes and cameras give the per-view images and summed derivatives."""
+    values = ordered(small_inputs(method, scenes=2, cameras=3), method)
+    result = maps_from_result(renderer(method)(**values, width=9, height=9, packed=packed))
+    repeated = []
+    for scene in range(2):
+        views = []
+        for camera in range(3):
+            subset = {name: value[scene, camera:camera + 1].contiguous()
+                      if name in {"view_matrices", "intrinsics", "backgrounds"}
+                      else value[scene].contiguous() for name, value in values.items()}
+            views.append(maps_from_result(renderer(method)(**subset, width=9, height=9)))
+        repeated.append(torch.cat(views))
+    repeated = torch.stack(repeated)
+    torch.testing.assert_close(result, repeated)
+    actual = torch.autograd.grad(result.square().sum(), tuple(values.values()), retain_graph=True)
+    expected = torch.autograd.grad(repeated.square().sum(), tuple(values.values()))
+    for name, a, e in zip(values, actual, expected):
+        torch.testing.assert_close(a, e, atol=4e-3, rtol=1e-3, msg=name)
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+@pytest.mark.parametrize("packed", [False, True])
+@pytest.mark.parametrize("empty", [False, True])
+def test_empty_and_invisible_scenes(method, packed, empty):
+    """Background-only images and finite zero primitive gradients when nothing shows."""
+    values = ordered(small_inputs(method, primitives=0 if empty else 3), method)
+    if not empty:
+        with torch.no_grad():
+            values["means"][..., 2] = -2
+    rgb, alpha, meta = renderer(method)(**values, width=9, height=9, packed=packed)
+    torch.testing.assert_close(rgb, values["backgrounds"][:, :, None, None, :].expand_as(rgb))
+    assert alpha.count_nonzero() == 0
+    maps_from_result((rgb, alpha, meta)).sum().backward()
+    for name, value in values.items():
+        assert value.grad is not None and torch.isfinite(value.grad).all(), name
+        if name != "backgrounds":
+            assert value.grad.count_nonzero() == 0, name
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_leading_dimensions_and_stream(method):
+    """Several scene dimensions, on the caller's non-default CUDA stream."""
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        values = ordered(small_inputs(method, scenes=4), method)
+        values = {k: v.detach().reshape(2, 2, *v.shape[1:]).requires_grad_()
+                  for k, v in values.items()}
+        rgb, alpha, _ = renderer(method)(**values, width=9, height=9, packed=True)
+        (rgb.sum() + alpha.sum()).backward()
+        assert rgb.shape == (2, 2, 2, 9, 9, 3)
+    torch.cuda.synchronize()
+    flat = {k: v.detach().reshape(4, *v.shape[2:]).contiguous() for k, v in values.items()}
+    rgb2, _, _ = renderer(method)(**flat, width=9, height=9)
+    torch.testing.assert_close(rgb.detach().reshape(rgb2.shape), rgb2)
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_invalid_contracts(method):
+    """Explicit errors for unsupported dtypes, shapes, layouts and numerical values."""
+    original = ordered(small_inputs(method), method)
+    for name, replacement in [
+        ("means", original["means"].double()),
+        ("scales", -original["scales"]),
+        ("quaternions", torch.zeros_like(original["quaternions"])),
+        ("opacities", torch.full_like(original["opacities"], 2)),
+        ("intrinsics", original["intrinsics"].transpose(-1, -2)),
+    ]:
+        values = dict(original, **{name: replacement})
+        with pytest.raises(ValueError):
+            renderer(method)(**values, width=9, height=9)
+    with pytest.raises(ValueError):
+        renderer(method)(**original, width=0, height=9)
+    with pytest.raises(TypeError):
+        renderer(method)(**original, width=9, height=9, packed=1)
+
+
+@pytest.mark.parametrize("degree", [0, 1, 2, 3])
+def test_classic_sh_batches(degree):
+    """SH colour gradients and camera-specific appearance, dense == packed."""
+    values = ordered(small_inputs("classic", scenes=2), "classic")
+    for name in ["colors", "secondary_colors"]:
+        values[name] = torch.full((2, 3, (degree + 1) ** 2, 3), 0.1, device="cuda",
+                                  requires_grad=True)
+    dense = maps_from_result(rasterize_gabors(**values, width=9, height=9, sh_degree=degree))
+    packed = maps_from_result(rasterize_gabors(**values, width=9, height=9, sh_degree=degree,
+                                               packed=True))
+    torch.testing.assert_close(dense, packed)
+    dense.sum().backward()
+    assert values["colors"].grad.abs().sum() > 0
+    assert values["secondary_colors"].grad.abs().sum() > 0
+
+
+@pytest.mark.parametrize("degree", [0, 3])
+def test_empty_sh_scene(degree):
+    """Empty SH scenes keep valid shapes."""
+    values = ordered(small_inputs("classic", primitives=0), "classic")
+    for name in ["colors", "secondary_colors"]:
+        values[name] = torch.empty((1, 0, (degree + 1) ** 2, 3), device="cuda",
+                                   requires_grad=True)
+    result = rasterize_gabors(**values, width=9, height=9, sh_degree=degree, packed=True)
+    maps_from_result(result).sum().backward()
+    assert values["colors"].grad.shape == values["colors"].shape
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_parameter_finite_differences(method):
+    """Representative derivatives against central differences."""
+    values = ordered(small_inputs(method, cameras=1, primitives=1), method)
+    names = ["means", "scales", "opacities", "phases" if method == "classic" else "input_biases"]
+
+    def objective():
+        maps = maps_from_result(renderer(method)(**values, width=9, height=9))
+        weights = torch.linspace(-0.2, 0.4, maps.numel(), device="cuda").reshape(maps.shape)
+        return (maps.double() * weights).sum()
+
+    gradients = torch.autograd.grad(objective(), [values[name] for name in names])
+    for name, gradient in zip(names, gradients):
+        parameter = values[name]
+        index = (0,) * parameter.ndim
+        step = 5e-4
+        original = parameter[index].item()
+        with torch.no_grad():
+            parameter[index] = original + step
+        plus = objective().item()
+        with torch.no_grad():
+            parameter[index] = original - step
+        minus = objective().item()
+        with torch.no_grad():
+            parameter[index] = original
+        torch.testing.assert_close(gradient[index].double(),
+                                   gradient.new_tensor((plus - minus) / (2 * step)).double(),
+                                   atol=3e-3, rtol=8e-3, msg=name)
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_float32_inputs_ignore_global_default_dtype(method):
+    values = ordered(small_inputs(method, cameras=1, primitives=1), method)
+    previous = torch.get_default_dtype()
+    try:
+        torch.set_default_dtype(torch.float64)
+        rgb, alpha, _ = renderer(method)(**values, width=9, height=9)
+        (rgb.sum() + alpha.sum()).backward()
+        assert rgb.dtype == torch.float32 and alpha.dtype == torch.float32
+    finally:
+        torch.set_default_dtype(previous)
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+@pytest.mark.parametrize("case", ["edge_on", "degenerate_conic"])
+def test_degenerate_surfaces_have_finite_zero_gradients(method, case):
+    """Edge-on and zero-denominator conics are culled without contaminating gradients."""
+    values = ordered(small_inputs(method, cameras=1, primitives=1), method)
+    with torch.no_grad():
+        values["view_matrices"].copy_(torch.eye(4, device="cuda"))
+        values["means"][0, 0] = values["means"].new_tensor([0.0, 0.0, 3.0])
+        values["quaternions"].fill_(0.5)
+        if case == "degenerate_conic":
+            values["scales"].fill_(1.0)
+            values["means"][..., 0] = 0.1
+    rgb, alpha, meta = renderer(method)(**values, width=9, height=9, packed=True)
+    assert alpha.count_nonzero() == 0
+    maps_from_result((rgb, alpha, meta)).sum().backward()
+    for name, value in values.items():
+        assert value.grad is not None and torch.isfinite(value.grad).all(), name
+        if name != "backgrounds":
+            assert value.grad.count_nonzero() == 0, name
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_trusted_input_path_skips_only_value_checks(method, monkeypatch):
+    """validate=False skips only the numerical checks; structure checks remain."""
+    import diff_gabor_splatting_b200.rendering as rendering
+
+    values = ordered(small_inputs(method), method)
+    expected = maps_from_result(renderer(method)(**values, width=9, height=9))
+
+    def unexpected_value_check(*args):
+        raise AssertionError("check_values should not be called")
+
+    monkeypatch.setattr(rendering, "check_values", unexpected_value_check)
+    actual = maps_from_result(renderer(method)(**values, width=9, height=9, validate=False))
+    torch.testing.assert_close(actual, expected)
+    ag = torch.autograd.grad(actual.sum(), tuple(values.values()), retain_graph=True)
+    eg = torch.autograd.grad(expected.sum(), tuple(values.values()))
+    for a, e in zip(ag, eg):
+        torch.testing.assert_close(a, e, atol=2e-3, rtol=1e-3)
+    invalid = dict(values, scales=values["scales"].double())
+    with pytest.raises(ValueError, match="scales must be float32"):
+        renderer(method)(**invalid, width=9, height=9, validate=False)
+
+
+def test_projected_means_receive_screen_gradient():
+    """projected_means is in the graph: retain_grad shows its screen-filter gradient."""
+    values = ordered(small_inputs("classic", primitives=3), "classic")
+    for packed in (False, True):
+        rgb, alpha, meta = rasterize_gabors(**values, width=9, height=9, packed=packed)
+        meta["projected_means"].retain_grad()
+        (rgb.sum() + alpha.sum()).backward()
+        grad = meta["projected_means"].grad
+        assert grad is not None and grad.shape == meta["projected_means"].shape
+        assert torch.isfinite(grad).all()
+        assert np.asarray(meta["radii"].cpu()).size > 0
