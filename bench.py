@@ -57,6 +57,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--cpu-window", type=int, default=64, help="CPU sample window (pixels)")
+    p.add_argument("--surfels", type=int, default=None, help="override N (profiling cases)")
+    p.add_argument("--cameras", type=int, default=None, help="override C (profiling cases)")
+    p.add_argument("--scenes", type=int, default=None, help="override S (profiling cases)")
     return p.parse_args()
 
 
@@ -70,16 +73,16 @@ def dist_setup(args):
     return world, rank, local
 
 
-def shard(workload_config, rank, world):
+def shard(workload_config, rank, world, overrides):
     """This rank's scenes: config 3 splits its 32 scenes, others give each rank a scene."""
     if workload_config in (3,):
-        full = make_workload(workload_config)
+        full = make_workload(workload_config, **overrides)
         S = full.scenes
         lo, hi = rank * S // world, (rank + 1) * S // world
         inputs = {k: v[lo:hi].contiguous() for k, v in full.inputs.items()}
         full.inputs, full.scenes = inputs, hi - lo
         return full, "strong"
-    return make_workload(workload_config, seed=rank), "weak"
+    return make_workload(workload_config, seed=rank, **overrides), "weak"
 
 
 class ClockSampler:
@@ -221,7 +224,7 @@ def run_reference(args, world, rank):
     """CPU arm: the oracle (reference algorithm restated on the CPU), rank 0 only."""
     if rank != 0:
         return
-    w = make_workload(args.config)
+    w = make_workload(args.config, surfels=args.surfels, cameras=args.cameras, scenes=args.scenes)
     cores = os.cpu_count() or 1
     for _ in range(args.warmup):
         cpu_baseline(w, args.cpu_window, cores)
@@ -267,7 +270,8 @@ def main():
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    w, scaling = shard(args.config, rank, world)
+    overrides = dict(surfels=args.surfels, cameras=args.cameras, scenes=args.scenes)
+    w, scaling = shard(args.config, rank, world, overrides)
     fn = rasterize_gabors if w.method == "classic" else rasterize_neural_gabors
     values = device_inputs(w, device)
     for _ in range(max(args.warmup, 3)):
@@ -292,7 +296,8 @@ def main():
     ms = max_over_ranks(start.elapsed_time(end), world, device)
     stage = timer.totals()
     launches = sum(OWN_KERNELS.get(name, 1) * calls for name, (calls, _) in stage.items())
-    pixels_all = w.pixels * world if scaling == "weak" else make_workload_pixels(args.config)
+    pixels_all = w.pixels * world if scaling == "weak" else make_workload_pixels(args.config,
+                                                                                  overrides)
     value = pixels_all * args.steps / (ms * 1e-3) / 1e6
     # end to end: host (pinned) inputs copied in every step, loss read back
     e2e = None
@@ -337,8 +342,8 @@ def main():
         torch.distributed.destroy_process_group()
 
 
-def make_workload_pixels(config):
-    w = make_workload(config, surfels=1)
+def make_workload_pixels(config, overrides):
+    w = make_workload(config, **dict(overrides, surfels=1))
     return w.pixels
 
 

@@ -390,13 +390,11 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
         height, float(near_plane), float(far_plane))
     if sh:
         rows, row_mode = sh_rows, nat.ROWS_PER_RECORD
-    elif neural:
-        rows = torch.cat([t.reshape(S * N, -1) for t in appearance]
-                         + [means.new_zeros((S * N, nat.NEURAL_ROW_FLOATS - 57))], -1)
-        row_mode = nat.ROWS_PER_SURFEL
     else:
-        rows = torch.cat([t.reshape(S * N, -1) for t in appearance]
-                         + [means.new_zeros((S * N, nat.CLASSIC_ROW_FLOATS - 18))], -1)
+        widths = [30, 6, 18, 3] if neural else [3, 3, 4, 4, 4]
+        pad = (nat.NEURAL_ROW_FLOATS if neural else nat.CLASSIC_ROW_FLOATS) - sum(widths)
+        rows = torch.cat([t.reshape(S * N, k) for t, k in zip(appearance, widths)]
+                         + [means.new_zeros((S * N, pad))], -1)
         row_mode = nat.ROWS_PER_SURFEL
     images = S * C
     point_list, ranges = bin_records(records, nat.RECORD_FLOATS, radii, None, max(N, 1), images,

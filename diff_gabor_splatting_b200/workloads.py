@@ -98,12 +98,12 @@ def cameras(rig: str, count: int, width: int, height: int, focal: float, g: torc
 
 
 def make_workload(config: int, seed: int = 0, surfels: int | None = None,
-                  scenes: int | None = None) -> Workload:
-    """Build config ``config`` on the host (optionally with fewer surfels/scenes)."""
+                  scenes: int | None = None, cameras: int | None = None) -> Workload:
+    """Build config ``config`` on the host (optionally fewer surfels/scenes/cameras)."""
     c = dict(CONFIGS[config])
     S = scenes or c["scenes"]
     N = surfels or c["surfels"]
-    C = c["cameras"]
+    C = cameras or c["cameras"]
     g = torch.Generator().manual_seed(seed * 1000 + config)
     if config == 0:
         means = torch.empty(S, N, 3)

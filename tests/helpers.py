@@ -119,3 +119,23 @@ def ordered(values, method):
     names = ["means", "quaternions", "scales", "opacities", *appearance_names(method),
              "view_matrices", "intrinsics", "backgrounds"]
     return {k: values[k] for k in names if k in values}
+
+
+def assert_images_close(actual, expected, rtol, atol, max_bad_pixels=0.01, msg=""):
+    """Image maps [..., H, W, 9] equal within tolerance except at a bounded fraction of
+    pixels.
+
+    Used against the CPU oracle: the kernels (like the reference's CUDA) round the
+    ill-conditioned ray/plane intersection differently from plain CPU float32 (fused
+    multiply-adds), which flips the alpha >= 1/255 acceptance or the T < 1e-4 stop
+    for a few samples; each flip changes one pixel by up to one small contribution.
+    """
+    a = actual.detach().cpu().double()
+    e = expected.detach().cpu().double()
+    assert a.shape == e.shape, (a.shape, e.shape)
+    bad = ((a - e).abs() > atol + rtol * e.abs()).reshape(-1, a.shape[-1]).any(-1)
+    frac = bad.double().mean().item()
+    assert frac <= max_bad_pixels, (
+        f"{msg}: {frac:.3%} of pixels outside rtol={rtol} atol={atol} "
+        f"(max abs diff {(a - e).abs().max().item():.3g})")
+    return frac
