@@ -81,6 +81,15 @@ __device__ __forceinline__ int64_t row_of(const Params& P, int r) {
     return s * P.surfels + n;
 }
 
+// Squared local radius beyond which a sample of opacity o is certainly below the
+// alpha acceptance threshold: o * exp(-rho/2) < 1/255 for every rho > 2 ln(255 o).
+// The 1e-4 margin covers the rounding of expf, of the product and of this logf
+// (each a few 1e-7 relative), so the exact test would reject every sample the early
+// test rejects.  o <= 0 gives -inf (always rejected, as the exact test does).
+__device__ __forceinline__ float reject_threshold(float opacity) {
+    return 2.f * logf(255.f * opacity) + 1e-4f;
+}
+
 template <bool Neural>
 struct Batch {
     static constexpr int kRow = Neural ? kNeuralRow : kClassicRow;
@@ -105,10 +114,14 @@ __device__ __forceinline__ void load_batch(Batch<Neural>& b, const Params& P, in
     __syncthreads();
     for (int i = rank; i < count * kPer; i += kBlock) {
         const int e = i / kPer, part = i % kPer;
-        if (part < kRec / 4)
-            b.geo[e][part] = __ldg(P.records + int64_t(b.ids[e]) * (kRec / 4) + part);
-        else
+        if (part < kRec / 4) {
+            float4 v = __ldg(P.records + int64_t(b.ids[e]) * (kRec / 4) + part);
+            // slot 18 (pad in memory) <- rejection threshold of this record's opacity
+            if (part == 4) v.z = reject_threshold(v.y);
+            b.geo[e][part] = v;
+        } else {
             b.app[e][part - kRec / 4] = __ldg(P.rows + b.rows[e] * (kRow / 4) + (part - kRec / 4));
+        }
     }
     __syncthreads();
 }
@@ -128,11 +141,21 @@ __device__ __forceinline__ bool sample_surface(const float* g, int x, int y, boo
     }
     cross3(v.k, v.l, v.p);
     if (v.p[2] == 0) return false;
+    const float dx = g[9] - x, dy = g[10] - y;
+    const float rho2 = 2 * (dx * dx + dy * dy);
+    // Early rejection (same decision as the exact test below, fewer instructions):
+    // alpha = o exp(-min(rho3, rho2)/2) < 1/255 once both radii exceed g[18].  rho3 is
+    // bounded from below by (p0^2 + p1^2)/p2^2 with a fast divide, shrunk by 1e-5 to
+    // cover its few-ulp error; NaN or an out-of-range p2^2 falls through.
+    if (rho2 > g[18]) {
+        const float q = v.p[2] * v.p[2];
+        if (q >= 1.17549435e-38f && q <= 1e37f &&
+            __fdividef(fmaf(v.p[1], v.p[1], v.p[0] * v.p[0]), q) * (1.f - 1e-5f) > g[18])
+            return false;
+    }
     v.s[0] = v.p[0] / v.p[2];
     v.s[1] = v.p[1] / v.p[2];
     const float rho3 = v.s[0] * v.s[0] + v.s[1] * v.s[1];
-    const float dx = g[9] - x, dy = g[10] - y;
-    const float rho2 = 2 * (dx * dx + dy * dy);
     v.surface = rho3 <= rho2;
     v.depth = (neural || v.surface) ? v.s[0] * g[6] + v.s[1] * g[7] + g[8] : g[8];
     if (v.depth < near_plane || !isfinite(v.depth)) return false;
@@ -369,9 +392,24 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
             float* ga = vals + F::kGeo + 1;    // appearance row fields
             if (active) {
                 float color[3], hidden[6], pre[6], gc[3], gs[2] = {0.f, 0.f};
+                float waves[4], sines[4];
                 T /= 1 - v.alpha;
                 const float w = T * v.alpha;
-                appearance_forward<Neural>(a, g, v, dirs, color, hidden, pre);
+                if constexpr (Neural) {
+                    appearance_forward<Neural>(a, g, v, dirs, color, hidden, pre);
+                } else {
+                    // colour replay with sine and cosine of each wave from one sincosf
+                    float h1 = 0, h2 = 0;
+#pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        const float dot = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
+                        sincosf(2 * kPi * a[10 + f] * dot + a[14 + f], &sines[f], &waves[f]);
+                        h1 += a[6 + f] * 0.5f * (1 + waves[f]);
+                        h2 += a[6 + f] * 0.5f * (1 - waves[f]);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) color[c] = h1 * a[c] + h2 * a[3 + c];
+                }
                 const float m = mscale * (1 - P.near_plane / v.depth);
                 float gw = go[4] * v.depth + go[8] * (m * m * total_a + m2 - 2 * m * m1);
 #pragma unroll
@@ -380,8 +418,9 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                     gc[c] = w * go[c];
                     gg[11 + c] += w * go[5 + c];
                 }
-                const float galpha = T * gw - suffix / (1 - v.alpha) +
-                                     final_t * (go[3] - background_dot) / (1 - v.alpha);
+                const float inv_transmit = __frcp_rn(1 - v.alpha);
+                const float galpha = T * gw - suffix * inv_transmit +
+                                     final_t * (go[3] - background_dot) * inv_transmit;
                 suffix += w * gw;
                 // appearance backward: rasterize.cu:146-197
                 if constexpr (Neural) {
@@ -417,8 +456,7 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                         const float dx = dirs.c[f], dy = dirs.s[f];
                         const float dot = dx * v.s[0] + dy * v.s[1];
                         const float angle = 2 * kPi * a[10 + f] * dot + a[14 + f];
-                        const float wave = cosf(angle);
-                        const float sine = sinf(angle);
+                        const float wave = waves[f], sine = sines[f];
                         float gwf = 0, gt = 0;
 #pragma unroll
                         for (int c = 0; c < 3; ++c) {
@@ -436,7 +474,7 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                 }
                 // geometry: rasterize.cu:359-385
                 const float gz = w * go[4] + go[8] * 2 * w * (m * total_a - m1) * mscale *
-                                                 P.near_plane / (v.depth * v.depth);
+                                                 P.near_plane * __frcp_rn(v.depth * v.depth);
                 if (Neural || v.surface) {
                     gs[0] += gz * g[6];
                     gs[1] += gz * g[7];
@@ -456,8 +494,9 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                     gg[9] += 4 * (g[9] - x) * grho;
                     gg[10] += 4 * (g[10] - y) * grho;
                 }
-                const float gp[3] = {gs[0] / v.p[2], gs[1] / v.p[2],
-                                     -(gs[0] * v.s[0] + gs[1] * v.s[1]) / v.p[2]};
+                const float inv_p2 = __frcp_rn(v.p[2]);
+                const float gp[3] = {gs[0] * inv_p2, gs[1] * inv_p2,
+                                     -(gs[0] * v.s[0] + gs[1] * v.s[1]) * inv_p2};
                 float gk[3], gl[3];
                 cross3(v.l, gp, gk);
                 cross3(gp, v.k, gl);

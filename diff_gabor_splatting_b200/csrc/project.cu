@@ -25,6 +25,15 @@ namespace {
 constexpr int kProjThreads = 256;
 constexpr float kMinRadius = 3 * 0.707106f;   // rendering.py:208
 
+// Sums in the order PyTorch's CUDA reduction over a last dimension of 3 or 4 uses:
+// (a0 + a2) + a1 and (a0 + a2) + (a1 + a3), each add rounded.
+__device__ __forceinline__ float sum3(float a0, float a1, float a2) {
+    return __fadd_rn(__fadd_rn(a0, a2), a1);
+}
+__device__ __forceinline__ float sum4(float a0, float a1, float a2, float a3) {
+    return __fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3));
+}
+
 struct Surfel {
     float mean[3], q[4], qn[4], qnorm, scale[2], R[3][3], tangent[3][2];
 };
@@ -42,14 +51,13 @@ __device__ __forceinline__ void load_surfel(Surfel& v, const float* means, const
     float2 sc = reinterpret_cast<const float2*>(scales)[sn];
     v.scale[0] = sc.x; v.scale[1] = sc.y;
     // q / ||q|| (rendering.py:158)
-    float ss = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(q.x, q.x), __fmul_rn(q.y, q.y)),
-                                   __fmul_rn(q.z, q.z)), __fmul_rn(q.w, q.w));
+    float ss = sum4(__fmul_rn(q.x, q.x), __fmul_rn(q.y, q.y), __fmul_rn(q.z, q.z),
+                    __fmul_rn(q.w, q.w));
     v.qnorm = sqrtf(ss);
 #pragma unroll
     for (int i = 0; i < 4; ++i) v.qn[i] = __fdiv_rn(v.q[i], v.qnorm);
     const float w = v.qn[0], x = v.qn[1], y = v.qn[2], z = v.qn[3];
     // rendering.py:160-172, each product and sum rounded like the element-wise ops
-    auto m2 = [](float a, float b) { return __fmul_rn(2.f, __fmul_rn(a, b)); };
     v.R[0][0] = __fsub_rn(1.f, __fmul_rn(2.f, __fadd_rn(__fmul_rn(y, y), __fmul_rn(z, z))));
     v.R[0][1] = __fmul_rn(2.f, __fsub_rn(__fmul_rn(x, y), __fmul_rn(w, z)));
     v.R[0][2] = __fmul_rn(2.f, __fadd_rn(__fmul_rn(x, z), __fmul_rn(w, y)));
@@ -59,7 +67,6 @@ __device__ __forceinline__ void load_surfel(Surfel& v, const float* means, const
     v.R[2][0] = __fmul_rn(2.f, __fsub_rn(__fmul_rn(x, z), __fmul_rn(w, y)));
     v.R[2][1] = __fmul_rn(2.f, __fadd_rn(__fmul_rn(y, z), __fmul_rn(w, x)));
     v.R[2][2] = __fsub_rn(1.f, __fmul_rn(2.f, __fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y))));
-    (void)m2;
 #pragma unroll
     for (int i = 0; i < 3; ++i)
 #pragma unroll
@@ -111,9 +118,10 @@ __device__ __forceinline__ void setup_pair(Pair& p, const Surfel& v, const Camer
             p.T[i][j] = dot3(c.K[i][0], p.plane[0][j], c.K[i][1], p.plane[1][j], c.K[i][2],
                              p.plane[2][j]);
     const float t[3] = {9.f, 9.f, -1.f};
-    float d = 0.f;
+    float dt[3];
 #pragma unroll
-    for (int j = 0; j < 3; ++j) d = __fadd_rn(d, __fmul_rn(t[j], __fmul_rn(p.T[2][j], p.T[2][j])));
+    for (int j = 0; j < 3; ++j) dt[j] = __fmul_rn(t[j], __fmul_rn(p.T[2][j], p.T[2][j]));
+    const float d = sum3(dt[0], dt[1], dt[2]);
     p.denom = d;
     p.valid = d != 0.f;
     float safe = p.valid ? d : 1.f;
@@ -121,30 +129,28 @@ __device__ __forceinline__ void setup_pair(Pair& p, const Surfel& v, const Camer
     for (int j = 0; j < 3; ++j) p.f[j] = __fdiv_rn(t[j], safe);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-        float acc = 0.f;
+        float term[3];
 #pragma unroll
-        for (int j = 0; j < 3; ++j)
-            acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(p.f[j], p.T[i][j]), p.T[2][j]));
-        p.xy[i] = acc;
+        for (int j = 0; j < 3; ++j) term[j] = __fmul_rn(__fmul_rn(p.f[j], p.T[i][j]), p.T[2][j]);
+        p.xy[i] = sum3(term[0], term[1], term[2]);
     }
     float n[3];
 #pragma unroll
     for (int i = 0; i < 3; ++i)
         n[i] = dot3(c.Rc[i][0], v.R[0][2], c.Rc[i][1], v.R[1][2], c.Rc[i][2], v.R[2][2]);
-    float facing = -__fadd_rn(__fadd_rn(__fmul_rn(p.cm[0], n[0]), __fmul_rn(p.cm[1], n[1])),
-                              __fmul_rn(p.cm[2], n[2]));
+    float facing = -sum3(__fmul_rn(p.cm[0], n[0]), __fmul_rn(p.cm[1], n[1]),
+                         __fmul_rn(p.cm[2], n[2]));
     p.sign = facing > 0.f ? 1.f : -1.f;
 #pragma unroll
     for (int i = 0; i < 3; ++i) p.normal[i] = __fmul_rn(n[i], p.sign);
     // camera centre -Rc^T t and the unit world direction centre -> mean
-    float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
         float center = -dot3(c.Rc[0][i], c.tc[0], c.Rc[1][i], c.tc[1], c.Rc[2][i], c.tc[2]);
         p.dvec[i] = __fsub_rn(v.mean[i], center);
-        ss = __fadd_rn(ss, __fmul_rn(p.dvec[i], p.dvec[i]));
     }
-    p.dnorm = fmaxf(sqrtf(ss), 1e-12f);
+    p.dnorm = fmaxf(sqrtf(sum3(__fmul_rn(p.dvec[0], p.dvec[0]), __fmul_rn(p.dvec[1], p.dvec[1]),
+                               __fmul_rn(p.dvec[2], p.dvec[2]))), 1e-12f);
 #pragma unroll
     for (int i = 0; i < 3; ++i) p.dir[i] = __fdiv_rn(p.dvec[i], p.dnorm);
     // facing is kept in sign; culling needs it non-zero
@@ -154,14 +160,14 @@ __device__ __forceinline__ void setup_pair(Pair& p, const Surfel& v, const Camer
 // Unit world direction from the camera centre -Rc^T t to the surfel mean
 // (rendering.py:202-206), rounded like setup_pair.
 __device__ __forceinline__ void view_direction(const Surfel& v, const Camera& c, float* dir) {
-    float d[3], ss = 0.f;
+    float d[3];
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
         float center = -dot3(c.Rc[0][i], c.tc[0], c.Rc[1][i], c.tc[1], c.Rc[2][i], c.tc[2]);
         d[i] = __fsub_rn(v.mean[i], center);
-        ss = __fadd_rn(ss, __fmul_rn(d[i], d[i]));
     }
-    const float norm = fmaxf(sqrtf(ss), 1e-12f);
+    const float norm = fmaxf(sqrtf(sum3(__fmul_rn(d[0], d[0]), __fmul_rn(d[1], d[1]),
+                                        __fmul_rn(d[2], d[2]))), 1e-12f);
 #pragma unroll
     for (int i = 0; i < 3; ++i) dir[i] = __fdiv_rn(d[i], norm);
 }
@@ -172,11 +178,10 @@ __device__ __forceinline__ int pair_radius(const Pair& p, int tw, int th, float 
     float extent[2];
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-        float acc = 0.f;
+        float term[3];
 #pragma unroll
-        for (int j = 0; j < 3; ++j)
-            acc = __fadd_rn(acc, __fmul_rn(p.f[j], __fmul_rn(p.T[i][j], p.T[i][j])));
-        float e2 = __fsub_rn(__fmul_rn(p.xy[i], p.xy[i]), acc);
+        for (int j = 0; j < 3; ++j) term[j] = __fmul_rn(p.f[j], __fmul_rn(p.T[i][j], p.T[i][j]));
+        float e2 = __fsub_rn(__fmul_rn(p.xy[i], p.xy[i]), sum3(term[0], term[1], term[2]));
         extent[i] = sqrtf(fmaxf(e2, 1e-4f));
     }
     float radius = ceilf(fmaxf(fmaxf(extent[0], extent[1]), kMinRadius));

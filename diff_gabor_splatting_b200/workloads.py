@@ -77,7 +77,8 @@ def look_at(eye: torch.Tensor) -> torch.Tensor:
     return V
 
 
-def cameras(rig: str, count: int, width: int, height: int, focal: float, g: torch.Generator):
+def camera_rig(rig: str, count: int, width: int, height: int, focal: float,
+               g: torch.Generator):
     """View matrices [count,4,4] and intrinsics [count,3,3] (float32)."""
     if rig == "identity":
         views = torch.eye(4, dtype=torch.float64).expand(count, 4, 4).clone()
@@ -140,7 +141,7 @@ def make_workload(config: int, seed: int = 0, surfels: int | None = None,
         inputs["output_biases"] = torch.zeros(S, N, 3)
     views, Ks = [], []
     for _ in range(S):
-        v, k = cameras(c["rig"], C, c["width"], c["height"], c["focal"], g)
+        v, k = camera_rig(c["rig"], C, c["width"], c["height"], c["focal"], g)
         views.append(v)
         Ks.append(k)
     inputs["view_matrices"] = torch.stack(views)

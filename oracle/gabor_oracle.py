@@ -158,19 +158,20 @@ def pack(transform, xy, normals, directions, radii, opacities, appearance,
     scene dims flattened to one ([S,N,...]).
     """
     S, C, N = radii.shape
+    dev = radii.device
     if sh_degree is not None:
         colors = evaluate_sh(appearance[0], appearance[1], directions, sh_degree)
         rest = [t.reshape(S, 1, N, 4).expand(S, C, N, 4) for t in appearance[2:]]
         parameters = torch.cat((colors, *rest), -1).reshape(-1, 18)
         opacity_parameters = opacities.reshape(S, 1, N).expand(S, C, N).reshape(-1)
-        primitive_ids = torch.arange(S * C * N)
+        primitive_ids = torch.arange(S * C * N, device=dev)
     else:
         width = 57 if neural else 18
         parameters = torch.cat([t.reshape(S, N, -1) for t in appearance], -1).reshape(S * N, width)
         opacity_parameters = opacities.reshape(S * N)
-        primitive_ids = torch.arange(S * N).reshape(S, 1, N).expand(S, C, N).reshape(-1)
-    image_ids = torch.arange(S * C).reshape(S, C, 1).expand(S, C, N).reshape(-1)
-    selected = torch.arange(S * C * N)
+        primitive_ids = torch.arange(S * N, device=dev).reshape(S, 1, N).expand(S, C, N).reshape(-1)
+    image_ids = torch.arange(S * C, device=dev).reshape(S, C, 1).expand(S, C, N).reshape(-1)
+    selected = torch.arange(S * C * N, device=dev)
     if packed:
         selected = selected[radii.reshape(-1) > 0]
     projected_means = xy.reshape(-1, 2)[selected]

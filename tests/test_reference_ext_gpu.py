@@ -95,7 +95,13 @@ def test_native_layer_matches_reference(method, packed):
 @pytest.mark.parametrize("method,sh_degree", [("classic", None), ("classic", 3), ("neural", None)])
 @pytest.mark.parametrize("packed", [False, True])
 def test_public_api_matches_reference(method, sh_degree, packed):
-    v = random_scene(method, scenes=1, cameras=3, n=500, width=W, height=H, sh_degree=sh_degree)
+    """Whole public call vs the reference on a 2-scene batch.
+
+    The fused projection reproduces PyTorch's CUDA rounding (reduction and GEMM
+    accumulation orders), so records, radii and images agree bit for bit here; see
+    test_reference_varies_with_batch_shape for the one case where it cannot.
+    """
+    v = random_scene(method, scenes=2, cameras=3, n=500, width=W, height=H, sh_degree=sh_degree)
     mine = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
     theirs = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
     kw = dict(width=W, height=H, packed=packed)
@@ -112,14 +118,35 @@ def test_public_api_matches_reference(method, sh_degree, packed):
     torch.testing.assert_close(a_res[2]["projected_means"], e_res[2]["projected_means"],
                                rtol=1e-5, atol=1e-4)
     a_maps, e_maps = maps_from_result(a_res), maps_from_result(e_res)
-    assert_images_close(a_maps, e_maps, rtol=1e-5, atol=1e-6, max_bad_pixels=5e-3, msg="maps")
+    assert_images_close(a_maps, e_maps, rtol=1e-5, atol=1e-6, max_bad_pixels=1e-3, msg="maps")
     weights = torch.linspace(-0.4, 0.7, a_maps.numel(), device="cuda").reshape(a_maps.shape)
     ag = torch.autograd.grad((a_maps * weights).sum(), tuple(mine.values()))
     eg = torch.autograd.grad((e_maps * weights).sum(), tuple(theirs.values()))
     for name, a, e in zip(mine, ag, eg):
-        # relative 1e-3 of scale here: projection rounding differs (torch einsum vs the
-        # fused kernel) and is amplified by near-grazing samples
-        grads_close(a, e, name, rel=1e-3)
+        grads_close(a, e, name, rel=1e-4)
+
+
+def test_reference_varies_with_batch_shape():
+    """The reference's own images of one scene change with the batch it is rendered in.
+
+    For a single small scene PyTorch's einsum (inside the reference's projection) takes
+    a path with separately rounded products instead of the fused-multiply-add GEMM it
+    uses for larger or batched problems.  One-ulp differences in the plane transform
+    are then amplified by the Gabor waves (cos(2 pi f u) with f up to 8 and |u| large
+    near grazing angles).  This build follows the GEMM order, so rendering the scene
+    alone it differs from the reference-alone result exactly as the reference differs
+    from itself between the two batch shapes, and equals the reference-batched result.
+    """
+    v = random_scene("classic", scenes=1, cameras=3, n=500, width=W, height=H)
+    vals = ordered(v, "classic")
+    ref_alone = maps_from_result(ref.rasterize_gabors(**vals, width=W, height=H))
+    two = {k: torch.cat([t, t], 0).contiguous() for k, t in vals.items()}
+    ref_batched = maps_from_result(ref.rasterize_gabors(**two, width=W, height=H))[:1]
+    mine_alone = maps_from_result(rasterize_gabors(**vals, width=W, height=H))
+    assert torch.equal(mine_alone, ref_batched)
+    self_gap = (ref_alone - ref_batched).abs().max().item()
+    our_gap = (mine_alone - ref_alone).abs().max().item()
+    assert our_gap <= self_gap
 
 
 @pytest.mark.parametrize("degree", [0, 1, 2, 3])
