@@ -101,7 +101,8 @@ def test_public_api_matches_reference(method, sh_degree, packed):
     accumulation orders), so records, radii and images agree bit for bit here; see
     test_reference_varies_with_batch_shape for the one case where it cannot.
     """
-    v = random_scene(method, scenes=2, cameras=3, n=500, width=W, height=H, sh_degree=sh_degree)
+    v = random_scene(method, scenes=2, cameras=3, n=500, width=W, height=H, sh_degree=sh_degree,
+                     conditioned=True)
     mine = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
     theirs = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
     kw = dict(width=W, height=H, packed=packed)
@@ -124,6 +125,30 @@ def test_public_api_matches_reference(method, sh_degree, packed):
     eg = torch.autograd.grad((e_maps * weights).sum(), tuple(theirs.values()))
     for name, a, e in zip(mine, ag, eg):
         grads_close(a, e, name, rel=1e-4)
+
+
+@pytest.mark.parametrize("method,sh_degree", [("classic", None), ("classic", 3), ("neural", None)])
+def test_public_api_benchmark_like_scene(method, sh_degree):
+    """Benchmark distributions (arbitrary tilts, Gabor frequencies up to 8): images bit
+    for bit on a batched call; gradients in relative L2 norm (near-grazing samples give
+    a few large, rounding-sensitive per-surfel gradients on both sides)."""
+    v = random_scene(method, scenes=2, cameras=3, n=500, width=W, height=H, sh_degree=sh_degree)
+    mine = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    theirs = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    kw = dict(width=W, height=H)
+    if method == "classic":
+        kw["sh_degree"] = sh_degree
+        a_maps = maps_from_result(rasterize_gabors(**mine, **kw))
+        e_maps = maps_from_result(ref.rasterize_gabors(**theirs, **kw))
+    else:
+        a_maps = maps_from_result(rasterize_neural_gabors(**mine, **kw))
+        e_maps = maps_from_result(ref.rasterize_neural_gabors(**theirs, **kw))
+    assert_images_close(a_maps, e_maps, rtol=1e-5, atol=1e-6, max_bad_pixels=1e-3, msg="maps")
+    ag = torch.autograd.grad(a_maps.sum(), tuple(mine.values()))
+    eg = torch.autograd.grad(e_maps.sum(), tuple(theirs.values()))
+    for name, a, e in zip(mine, ag, eg):
+        rel = (a - e).double().norm().item() / (e.double().norm().item() + 1e-12)
+        assert rel <= 1e-3, f"{name}: relative L2 error {rel:.2e}"
 
 
 def test_reference_varies_with_batch_shape():
