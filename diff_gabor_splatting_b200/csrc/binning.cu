@@ -19,6 +19,8 @@
 // Result: point_list and ranges identical to the reference's.
 #include <cub/cub.cuh>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace gs {
@@ -319,4 +321,92 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
     ranges_kernel<<<blocks_for(I), kBinThreads, 0, s>>>(I, keys_out, reinterpret_cast<int2*>(ranges));
     GS_CHECK_LAUNCH("ranges_kernel");
     return GS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// gs_bin_static: binning without any allocation.
+//
+// Some callers cannot allocate device memory at the moment they need binning: a
+// renderer embedded in a host application whose allocator owns every device byte
+// (game-engine or DCC plugins with a fixed memory budget), code that runs while a
+// CUDA stream is being captured into a graph (cudaMalloc is not permitted during
+// capture), or real-time loops that forbid allocation after start-up.  For them the
+// two workspaces of gs_bin_count/gs_bin_sort live in one file-scope device array,
+// which every GPU that loads this library holds (32 MiB) until the process exits.
+// ------------------------------------------------------------------------------
+namespace gs {
+namespace {
+
+constexpr int64_t kStaticMaxRecords = 65536;
+constexpr int64_t kStaticMaxIntersections = int64_t(1) << 20;
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;
+
+static __device__ __align__(256) unsigned char g_bin_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_address[kMaxDevices] = {};
+
+// Device address of g_bin_scratch on the current device, looked up once per device.
+int static_scratch(void** out) {
+    int device = 0;
+    GS_CUDA(cudaGetDevice(&device));
+    if (device < 0 || device >= kMaxDevices)
+        return fail(GS_ERR_LIMIT, "gs_bin_static: device ordinal beyond 63");
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_address[device]) {
+        void* address = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&address, g_bin_scratch);
+        if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(g_bin_scratch)");
+        g_scratch_address[device] = address;
+    }
+    *out = g_scratch_address[device];
+    return GS_OK;
+}
+
+}  // namespace
+}  // namespace gs
+
+extern "C" int gs_bin_static(const float* records, int record_stride, const int32_t* radii,
+                             const int64_t* image_ids, int64_t records_count,
+                             int64_t records_per_image, int64_t images, int width, int height,
+                             int32_t* point_list, int64_t point_list_capacity, int32_t* ranges,
+                             int64_t* intersections, void* stream) {
+    if (!intersections) return fail(GS_ERR_ARGUMENT, "gs_bin_static: intersections is NULL");
+    *intersections = 0;
+    if (records_count > kStaticMaxRecords)
+        return fail(GS_ERR_LIMIT, "gs_bin_static: more than 65536 records (the static scratch "
+                                  "limit); use gs_bin_count/gs_bin_sort with caller workspaces");
+    int st = check_common("gs_bin_static", records, record_stride, radii, records_count,
+                          records_per_image, images, width, height);
+    if (st) return st;
+    void* scratch = nullptr;
+    st = static_scratch(&scratch);
+    if (st) return st;
+    size_t bytes1 = 0;
+    st = gs_bin_count_workspace(records_count, &bytes1);
+    if (st) return st;
+    bytes1 = align_up(bytes1);
+    if (bytes1 > kStaticScratchBytes)
+        return fail(GS_ERR_LIMIT, "gs_bin_static: count workspace exceeds the static scratch");
+    int64_t total = 0;
+    st = gs_bin_count(records, record_stride, radii, image_ids, records_count, records_per_image,
+                      images, width, height, scratch, bytes1, &total, stream);
+    if (st) return st;
+    *intersections = total;
+    if (total > kStaticMaxIntersections)
+        return fail(GS_ERR_LIMIT, "gs_bin_static: more than 1048576 tile intersections (the "
+                                  "static scratch limit)");
+    if (total > point_list_capacity)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_static: point_list capacity is below the "
+                                     "intersection count returned in *intersections");
+    size_t bytes2 = 0;
+    st = gs_bin_sort_workspace(records_count, total, images, width, height, &bytes2);
+    if (st) return st;
+    if (bytes1 + bytes2 > kStaticScratchBytes)
+        return fail(GS_ERR_LIMIT, "gs_bin_static: sort workspace exceeds the static scratch");
+    return gs_bin_sort(records, record_stride, radii, image_ids, records_count, records_per_image,
+                       images, width, height, scratch, bytes1,
+                       static_cast<char*>(scratch) + bytes1, bytes2, total, point_list, ranges,
+                       stream);
 }

@@ -120,6 +120,23 @@ int gs_bin_sort(const float* records, int record_stride, const int32_t* radii,
                 size_t workspace1_bytes, void* workspace2, size_t workspace2_bytes,
                 int64_t intersections, int32_t* point_list, int32_t* ranges, void* stream);
 
+/* No-allocation binning: gs_bin_count followed by gs_bin_sort with both workspaces
+ * taken from a 32 MiB array compiled into the library (one per GPU, held until
+ * exit), for callers that cannot allocate device memory (a host application that
+ * owns all device memory, code running during CUDA graph capture, allocation-free
+ * real-time loops).  No counterpart in the reference.  Limits: at most 65536 records
+ * and 1048576 tile intersections (GS_ERR_LIMIT beyond; *intersections still reports
+ * the count when that is the cause).  point_list must hold point_list_capacity
+ * entries.  The first call on a device looks the array up on the current device
+ * (make that call before any stream capture).  All calls share the array: calls that
+ * overlap on the GPU race, so serialise them (one stream, or events).  Waits on the
+ * stream once, like gs_bin_count. */
+int gs_bin_static(const float* records, int record_stride, const int32_t* radii,
+                  const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
+                  int64_t images, int width, int height, int32_t* point_list,
+                  int64_t point_list_capacity, int32_t* ranges, int64_t* intersections,
+                  void* stream);
+
 /* ---------------------------------------------------------------------------
  * Tile compositor.  Forward: renderForward (rasterize.cu:229-281); backward:
  * renderBackward (rasterize.cu:283-399).  One CTA per 16x16 tile.
