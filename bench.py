@@ -60,6 +60,11 @@ def parse():
     p.add_argument("--surfels", type=int, default=None, help="override N (profiling cases)")
     p.add_argument("--cameras", type=int, default=None, help="override C (profiling cases)")
     p.add_argument("--scenes", type=int, default=None, help="override S (profiling cases)")
+    p.add_argument("--split-cameras", action="store_true",
+                   help="shard one workload over the ranks, splitting a scene's cameras "
+                        "(gradient all-reduce) when there are more ranks than scenes")
+    p.add_argument("--scenes-per-call", type=int, default=None,
+                   help="scenes per render call (config 4 defaults to 1)")
     return p.parse_args()
 
 
@@ -73,16 +78,42 @@ def dist_setup(args):
     return world, rank, local
 
 
-def shard(workload_config, rank, world, overrides):
-    """This rank's scenes: config 3 splits its 32 scenes, others give each rank a scene."""
-    if workload_config in (3,):
-        full = make_workload(workload_config, **overrides)
-        S = full.scenes
-        lo, hi = rank * S // world, (rank + 1) * S // world
-        inputs = {k: v[lo:hi].contiguous() for k, v in full.inputs.items()}
-        full.inputs, full.scenes = inputs, hi - lo
-        return full, "strong"
-    return make_workload(workload_config, seed=rank, **overrides), "weak"
+class Job:
+    """This rank's share of one step: render calls (each a scene block) + collectives."""
+
+    def __init__(self, args, rank, world):
+        from diff_gabor_splatting_b200 import sharding
+
+        overrides = dict(surfels=args.surfels, cameras=args.cameras, scenes=args.scenes)
+        self.sharding = sharding
+        if args.config in (3, 4) or args.split_cameras:
+            # one workload sharded over the ranks (strong scaling)
+            full = make_workload(args.config, **overrides)
+            self.scaling = "strong"
+            self.total_pixels = full.pixels
+            shards = sharding.plan(full.scenes, full.cameras, world)
+            self.groups = sharding.groups_for(shards) if world > 1 else {}
+            self.shard = shards[rank]
+            part = sharding.take(full.inputs, self.shard)
+            self.workload = full
+        else:
+            # every rank renders its own independent scene of the config (weak scaling)
+            full = make_workload(args.config, seed=rank, **overrides)
+            self.scaling = "weak"
+            self.total_pixels = full.pixels * world
+            self.groups, self.shard = {}, None
+            part = full.inputs
+            self.workload = full
+        per_call = args.scenes_per_call or (1 if args.config == 4 else None)
+        S = next(iter(part.values())).shape[0]
+        step = per_call or S
+        self.calls = [{k: v[s:s + step] for k, v in part.items()} for s in range(0, S, step)]
+        self.local_pixels = sum(c["view_matrices"].shape[0] * c["view_matrices"].shape[1]
+                                for c in self.calls) * full.width * full.height
+
+    def inputs_on(self, device):
+        return [{k: v.to(device).contiguous().requires_grad_() for k, v in c.items()}
+                for c in self.calls]
 
 
 class ClockSampler:
@@ -139,15 +170,24 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def device_inputs(w, device):
-    return {k: v.to(device).requires_grad_() for k, v in w.inputs.items()}
-
-
-def step(fn, w, values):
-    rgb, alpha, meta = fn(**values, **w.kwargs(), validate=False)
-    loss = loss_of(rgb, alpha, meta, w.depth_normal_loss)
-    loss.backward()
-    return loss
+def step(fn, job, calls):
+    """Render every call of this rank, backward with the batch-mean loss, and sum
+    parameter gradients over the camera-split group when the scene is split."""
+    w = job.workload
+    total = None
+    for values in calls:
+        for v in values.values():
+            v.grad = None
+        rgb, alpha, meta = fn(**values, **w.kwargs(), validate=False)
+        pixels = rgb.shape[:-1].numel()
+        loss = loss_of(rgb, alpha, meta, w.depth_normal_loss) * (pixels / job.total_pixels)
+        loss.backward()
+        total = loss.detach() if total is None else total + loss.detach()
+    if job.shard is not None and job.shard.split:
+        for values in calls:
+            params = [t for k, t in values.items() if k not in job.sharding.PER_CAMERA]
+            job.sharding.allreduce_gradients(params, job.groups[job.shard.group_ranks])
+    return total
 
 
 def max_over_ranks(value, world, device):
@@ -170,25 +210,32 @@ def peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def roofline(stage_ms, counts, w, steps):
-    """Roofline of the dominant stage (largest total device time)."""
+def roofline(stage_ms, counts, w, steps, calls_per_step):
+    """Roofline of the dominant stage (largest total device time in the timed region).
+
+    achieved = algorithmic work of every launch of that stage in the timed region
+    (the counted work of one render call x calls per step x steps) / their summed
+    CUDA-event time.
+    """
     from diff_gabor_splatting_b200 import perfmodel
 
-    name, (calls, total) = max(stage_ms.items(), key=lambda kv: kv[1][1])
-    per_launch_ms = total / max(calls, 1)
+    name, (launches, total_ms) = max(stage_ms.items(), key=lambda kv: kv[1][1])
     model = perfmodel.stage_model(name, counts, w)
+    work = model["work"] * calls_per_step * steps
     data, source = peaks()
-    out = {"kernel": name, "launches": calls, "ms_per_launch": per_launch_ms,
+    out = {"kernel": name, "launches": launches, "ms_per_launch": total_ms / max(launches, 1),
            "bound": model["bound"], "unit": model["unit"], "traffic": None}
     if model["bound"] == "hbm":
-        achieved = model["work"] / (per_launch_ms * 1e-3) / 1e9
+        achieved = work / (total_ms * 1e-3) / 1e9
         peak = data["hbm_gbs"]
         out["peak_source"] = f"hbm_gbs of {source}"
     else:
-        achieved = model["work"] / (per_launch_ms * 1e-3) / 1e12
+        achieved = work / (total_ms * 1e-3) / 1e12
         peak = perfmodel.FP32_NOMINAL_TFLOPS
-        out["peak_source"] = "nominal FP32 (148 SM x 128 lanes x 2 x 1.965 GHz); no measured FP32 peak"
-    out.update(achieved=achieved, peak=peak, frac=achieved / peak, work_per_launch=model["work"],
+        out["peak_source"] = ("nominal FP32 (148 SM x 128 lanes x 2 flop x 1.965 GHz); "
+                              "no measured FP32 peak exists for this pool")
+    out.update(achieved=achieved, peak=peak, frac=achieved / peak,
+               work_per_launch=model["work"] * calls_per_step * steps / max(launches, 1),
                work_basis=model["basis"])
     return out
 
@@ -270,16 +317,14 @@ def main():
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    overrides = dict(surfels=args.surfels, cameras=args.cameras, scenes=args.scenes)
-    w, scaling = shard(args.config, rank, world, overrides)
+    job = Job(args, rank, world)
+    w = job.workload
     fn = rasterize_gabors if w.method == "classic" else rasterize_neural_gabors
-    values = device_inputs(w, device)
+    calls = job.inputs_on(device)
     for _ in range(max(args.warmup, 3)):
-        for v in values.values():
-            v.grad = None
-        step(fn, w, values)
+        step(fn, job, calls)
     torch.cuda.synchronize()
-    counts = perfmodel.count_work(fn, w, values)
+    counts = perfmodel.count_work(fn, w, calls[0])
     # timed region: K steps, inputs resident in HBM
     barrier(world)
     torch.cuda.synchronize()
@@ -287,33 +332,35 @@ def main():
     with ClockSampler(local) as clocks, nat.StageTimer() as timer:
         start.record()
         for _ in range(args.steps):
-            for v in values.values():
-                v.grad = None
-            step(fn, w, values)
+            step(fn, job, calls)
         end.record()
         torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world, device)
     stage = timer.totals()
-    launches = sum(OWN_KERNELS.get(name, 1) * calls for name, (calls, _) in stage.items())
-    pixels_all = w.pixels * world if scaling == "weak" else make_workload_pixels(args.config,
-                                                                                  overrides)
+    launches = sum(OWN_KERNELS.get(name, 1) * n for name, (n, _) in stage.items()
+                   if name in OWN_KERNELS)
+    pixels_all = job.total_pixels
     value = pixels_all * args.steps / (ms * 1e-3) / 1e6
     # end to end: host (pinned) inputs copied in every step, loss read back
     e2e = None
     if not args.no_e2e:
-        host = {k: v.pin_memory() for k, v in w.inputs.items()}
-        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        host = [{k: v.pin_memory() for k, v in c.items()} for c in job.calls]
+        h2d = sum(v.numel() * v.element_size() for c in host for v in c.values())
+
+        def e2e_step():
+            dev = [{k: v.to(device, non_blocking=True).requires_grad_() for k, v in c.items()}
+                   for c in host]
+            return step(fn, job, dev).item()
+
         for _ in range(2):
-            dev = {k: v.to(device, non_blocking=True).requires_grad_() for k, v in host.items()}
-            step(fn, w, dev).item()
+            e2e_step()
         barrier(world)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
-            dev = {k: v.to(device, non_blocking=True).requires_grad_() for k, v in host.items()}
-            step(fn, w, dev).item()
+            e2e_step()
         e1.record()
         torch.cuda.synchronize()
         barrier(world)
@@ -330,11 +377,12 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "Mpix/s", "n_gpus": world,
                 "steps": args.steps, "warmup": max(args.warmup, 3),
-                "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": scaling,
+                "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": job.scaling,
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config shapes)",
-                "config": config_desc(w, f"scene-sharded x{world}" if world > 1 else "single"),
+                "config": config_desc(w, parallelism(job, world)),
                 "gpu_launches": launches,
-                "roofline": roofline(stage, counts, w, args.steps),
+                "roofline": roofline(stage, counts, w, args.steps, len(job.calls)),
                 "stages_ms_per_step": {k: v[1] / args.steps for k, v in stage.items()},
                 "work": counts, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
@@ -342,9 +390,16 @@ def main():
         torch.distributed.destroy_process_group()
 
 
-def make_workload_pixels(config, overrides):
-    w = make_workload(config, **dict(overrides, surfels=1))
-    return w.pixels
+def parallelism(job, world):
+    if world == 1:
+        return "single GPU" + (f", {len(job.calls)} render calls per step"
+                               if len(job.calls) > 1 else "")
+    if job.scaling == "weak":
+        return f"scene replicas x{world} (one independent scene per GPU, no collective)"
+    if job.shard.split:
+        return (f"camera split x{world} (ranks per scene {len(job.shard.group_ranks)}, "
+                "NCCL all-reduce of parameter gradients)")
+    return f"scene sharded x{world} (contiguous scene blocks, no collective)"
 
 
 if __name__ == "__main__":

@@ -115,9 +115,9 @@ def rasterize_backward(geometry, appearance, opacities, primitive_ids, backgroun
         stream = nat.stream_of(device)
         images = backgrounds.shape[0]
         records, rows = _pack(geometry, appearance, opacities, primitive_ids, neural)
-        g_records = torch.empty_like(records)
-        g_rows = torch.empty_like(rows)
-        g_bg = torch.empty_like(backgrounds)
+        g_records = torch.zeros_like(records)
+        g_rows = torch.zeros_like(rows)
+        g_bg = torch.zeros_like(backgrounds)
         nat.call("gs_composite_backward", nat.ptr(records), nat.ptr(rows), nat.ROWS_EXPLICIT,
                  nat.ptr(primitive_ids), 1, 1, records.shape[0], rows.shape[0],
                  nat.ptr(backgrounds), nat.ptr(point_list), nat.ptr(ranges), nat.ptr(state),

@@ -626,13 +626,7 @@ extern "C" int gs_composite_backward(const float* records, const float* rows, in
         (records_count > 0 && (!grad_records || !grad_rows)))
         return fail(GS_ERR_ARGUMENT, "gs_composite_backward: NULL buffer");
     auto s = as_stream(stream);
-    const int row = neural ? kNeuralRow : kClassicRow;
-    if (records_count > 0) {
-        GS_CUDA(cudaMemsetAsync(grad_records, 0, sizeof(float) * kRec * records_count, s));
-        GS_CUDA(cudaMemsetAsync(grad_rows, 0, sizeof(float) * row * rows_count, s));
-        if (grad_xy) GS_CUDA(cudaMemsetAsync(grad_xy, 0, sizeof(float) * 2 * records_count, s));
-    }
-    GS_CUDA(cudaMemsetAsync(grad_backgrounds, 0, sizeof(float) * 3 * images, s));
+    (void)rows_count;
     Params P{};
     P.records = reinterpret_cast<const float4*>(records);
     P.rows = reinterpret_cast<const float4*>(rows);

@@ -123,25 +123,32 @@ class Projection(torch.autograd.Function):
 class Composite(torch.autograd.Function):
     """Tile compositor forward/backward (rasterize.cu:229-399) over binned records.
 
-    ``projected_means`` receives the screen-centre gradient (record slots 9-10), so it
-    can be inspected with ``retain_grad`` like the reference's.
+    ``chunks`` is the list of image chunks from ``bin_chunks``; each is composited
+    with its own point list and ranges, and the backward adds every chunk into the
+    same gradient buffers.  ``projected_means`` receives the screen-centre gradient
+    (record slots 9-10), so it can be inspected with ``retain_grad`` like the
+    reference's.
     """
 
     @staticmethod
-    def forward(ctx, records, projected_means, rows, backgrounds, selected, point_list, ranges,
-                row_mode, cameras, surfels, images, width, height, neural, near_plane,
-                far_plane):
+    def forward(ctx, records, projected_means, rows, backgrounds, selected, chunks, row_mode,
+                cameras, surfels, images, width, height, neural, near_plane, far_plane):
         device = records.device
         maps = torch.empty((images, height, width, 9), device=device, dtype=torch.float32)
         state = torch.empty((images, height, width, 3), device=device, dtype=torch.float32)
         contributors = torch.empty((images, height, width), device=device, dtype=torch.int32)
-        nat.call("gs_composite_forward", nat.ptr(records), nat.ptr(rows), row_mode, None,
-                 cameras, surfels, records.shape[0], rows.shape[0], nat.ptr(backgrounds),
-                 nat.ptr(point_list), nat.ptr(ranges), images, width, height, int(neural),
-                 near_plane, far_plane, nat.ptr(maps), nat.ptr(state), nat.ptr(contributors),
-                 nat.ptr(_counters("forward", device)), nat.stream_of(device))
-        ctx.save_for_backward(records, rows, backgrounds, selected, point_list, ranges, state,
-                              contributors)
+        stream = nat.stream_of(device)
+        for ch in chunks:
+            a = _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height)
+            nat.call("gs_composite_forward", a["records"], a["rows"], row_mode, None,
+                     a["cameras"], surfels, ch.record_count, a["rows_count"],
+                     _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
+                     nat.ptr(ch.ranges), ch.images, width, height, int(neural), near_plane,
+                     far_plane, _at(maps, a["pixel0"] * 9), _at(state, a["pixel0"] * 3),
+                     _at(contributors, a["pixel0"]), nat.ptr(_counters("forward", device)),
+                     stream)
+        ctx.save_for_backward(records, rows, backgrounds, selected, state, contributors)
+        ctx.chunks = chunks
         ctx.options = (row_mode, cameras, surfels, images, width, height, neural, near_plane,
                        far_plane)
         return maps
@@ -149,31 +156,176 @@ class Composite(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx, grad_maps):
-        records, rows, backgrounds, selected, point_list, ranges, state, contributors = \
-            ctx.saved_tensors
+        records, rows, backgrounds, selected, state, contributors = ctx.saved_tensors
         row_mode, cameras, surfels, images, width, height, neural, near_plane, far_plane = \
             ctx.options
         device = records.device
         grad_maps = grad_maps.contiguous()
-        g_records = torch.empty_like(records)
-        g_xy = torch.empty((records.shape[0], 2), device=device, dtype=torch.float32)
-        g_rows = torch.empty_like(rows)
-        g_bg = torch.empty_like(backgrounds)
-        nat.call("gs_composite_backward", nat.ptr(records), nat.ptr(rows), row_mode, None,
-                 cameras, surfels, records.shape[0], rows.shape[0], nat.ptr(backgrounds),
-                 nat.ptr(point_list), nat.ptr(ranges), nat.ptr(state), nat.ptr(contributors),
-                 nat.ptr(grad_maps), images, width, height, int(neural), near_plane, far_plane,
-                 nat.ptr(g_records), nat.ptr(g_xy), nat.ptr(g_rows), nat.ptr(g_bg),
-                 nat.ptr(_counters("backward", device)), nat.stream_of(device))
-        if records.shape[0] == 0:
-            g_records.zero_(), g_xy.zero_(), g_rows.zero_()
+        g_records = torch.zeros_like(records)
+        g_xy = torch.zeros((records.shape[0], 2), device=device, dtype=torch.float32)
+        g_rows = torch.zeros_like(rows)
+        g_bg = torch.zeros_like(backgrounds)
+        stream = nat.stream_of(device)
+        for ch in ctx.chunks:
+            a = _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height)
+            nat.call("gs_composite_backward", a["records"], a["rows"], row_mode, None,
+                     a["cameras"], surfels, ch.record_count, a["rows_count"],
+                     _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
+                     nat.ptr(ch.ranges), _at(state, a["pixel0"] * 3),
+                     _at(contributors, a["pixel0"]), _at(grad_maps, a["pixel0"] * 9),
+                     ch.images, width, height, int(neural), near_plane, far_plane,
+                     _at(g_records, ch.record0 * nat.RECORD_FLOATS), _at(g_xy, ch.record0 * 2),
+                     _at(g_rows, a["row0"] * rows.shape[1]), _at(g_bg, ch.image0 * 3),
+                     nat.ptr(_counters("backward", device)), stream)
         g_pm = g_xy if selected is None else g_xy[selected]
-        return (g_records, g_pm, g_rows, g_bg) + (None,) * 12
+        return (g_records, g_pm, g_rows, g_bg) + (None,) * 11
+
+
+def _at(t: torch.Tensor, offset: int) -> int | None:
+    """Device address of element ``offset`` of a contiguous tensor."""
+    if t is None or t.numel() == 0:
+        return None
+    return t.data_ptr() + offset * t.element_size()
+
+
+def _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height):
+    """Pointers and appearance-row addressing of one image chunk.
+
+    Chunks are either whole scenes or a camera range of one scene, so with rows
+    addressed per surfel the chunk's rows start at its first scene and the per-chunk
+    camera count keeps the kernel's record -> row arithmetic local.
+    """
+    if row_mode == nat.ROWS_PER_SURFEL:
+        row0 = (ch.image0 // cameras) * surfels
+        cams = cameras if ch.whole_scenes else ch.images
+        rows_count = (ch.images // cameras if ch.whole_scenes else 1) * surfels
+    else:
+        row0, cams, rows_count = ch.record0, cameras, ch.record_count
+    return dict(records=_at(records, ch.record0 * nat.RECORD_FLOATS),
+                rows=_at(rows, row0 * rows.shape[1]), cameras=cams, rows_count=rows_count,
+                row0=row0, pixel0=ch.image0 * height * width)
+
+
+# Largest number of tile intersections binned in one pass.  Larger batches are split
+# into image chunks (whole scenes, or camera ranges of one scene), each binned and
+# composited on its own; this bounds the sort workspace (~20 bytes per intersection)
+# and keeps indices within int32.
+MAX_CHUNK_INTERSECTIONS = 1 << 30
+GS_ERR_LIMIT = 2
+INT32_MAX = 2**31 - 1
+
+
+class Chunk:
+    """One image chunk: images [image0, image0 + images), records likewise."""
+
+    def __init__(self, image0, images, surfels, whole_scenes):
+        self.image0, self.images, self.whole_scenes = image0, images, whole_scenes
+        self.record0, self.record_count = image0 * surfels, images * surfels
+        self.point_list = self.ranges = None
+
+
+def _count(records, radii, R, per_image, images, width, height):
+    """gs_bin_count on a record range (``_Ptr`` addresses); returns (workspace, bytes,
+    intersections); the count is returned even when it exceeds int32."""
+    device = records.device
+    bytes1 = ctypes.c_size_t()
+    nat.call("gs_bin_count_workspace", R, ctypes.byref(bytes1))
+    ws1 = torch.empty((max(bytes1.value, 1),), device=device, dtype=torch.uint8)
+    total = ctypes.c_int64()
+    status = nat.lib.gs_bin_count(records.address, nat.RECORD_FLOATS, radii.address, None, R,
+                                  per_image, images,
+                                  width, height, nat.ptr(ws1), bytes1.value, ctypes.byref(total),
+                                  nat.stream_of(device))
+    if status not in (0, GS_ERR_LIMIT) or (status == GS_ERR_LIMIT and total.value <= INT32_MAX):
+        nat.check(status, "gs_bin_count")
+    return ws1, bytes1.value, total.value
+
+
+def _bin_chunk(ch, records, radii, surfels, width, height):
+    device = records.device
+    rec = _at(records, ch.record0 * nat.RECORD_FLOATS)
+    rad = _at(radii, ch.record0)
+    ws1, bytes1, total = _count(_Ptr(rec, device), _Ptr(rad, device), ch.record_count, surfels,
+                                ch.images, width, height)
+    tw, th = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
+    bytes2 = ctypes.c_size_t()
+    nat.call("gs_bin_sort_workspace", ch.record_count, total, ch.images, width, height,
+             ctypes.byref(bytes2))
+    ws2 = torch.empty((max(bytes2.value, 1),), device=device, dtype=torch.uint8)
+    ch.point_list = torch.empty((total,), device=device, dtype=torch.int32)
+    ch.ranges = torch.empty((ch.images * tw * th, 2), device=device, dtype=torch.int32)
+    nat.call("gs_bin_sort", rec, nat.RECORD_FLOATS, rad, None, ch.record_count, surfels,
+             ch.images, width, height, nat.ptr(ws1), bytes1, nat.ptr(ws2), bytes2.value, total,
+             nat.ptr(ch.point_list), nat.ptr(ch.ranges), nat.stream_of(device))
+    if WORK is not None:
+        WORK["records"] = WORK.get("records", 0) + ch.record_count
+        WORK["intersections"] = WORK.get("intersections", 0) + total
+        WORK["tiles"] = WORK.get("tiles", 0) + ch.images * tw * th
+    return ch
+
+
+class _Ptr:
+    """A raw device address standing in for a tensor argument of ``_count``."""
+
+    def __init__(self, address, device):
+        self.address, self.device = address, device
+
+
+def bin_chunks(records, radii, scenes, cameras, surfels, width, height):
+    """Bin the dense records of S scenes x C cameras x N surfels in image chunks."""
+    device = records.device
+    images = scenes * cameras
+    whole = Chunk(0, images, surfels, True)
+    if records.shape[0] == 0:
+        whole.record_count = 0
+        whole.point_list = torch.empty((0,), device=device, dtype=torch.int32)
+        tw, th = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
+        whole.ranges = torch.zeros((images * tw * th, 2), device=device, dtype=torch.int32)
+        return [whole]
+
+    def count_of(image0, count):
+        rec = _Ptr(_at(records, image0 * surfels * nat.RECORD_FLOATS), device)
+        rad = _Ptr(_at(radii, image0 * surfels), device)
+        return _count(rec, rad, count * surfels, surfels, count, width, height)[2]
+
+    if count_of(0, images) <= MAX_CHUNK_INTERSECTIONS:
+        return [_bin_chunk(whole, records, radii, surfels, width, height)]
+    chunks, group, group_total = [], [], 0
+
+    def flush():
+        nonlocal group, group_total
+        if group:
+            chunks.append(Chunk(group[0] * cameras, len(group) * cameras, surfels, True))
+        group, group_total = [], 0
+
+    for s in range(scenes):
+        total = count_of(s * cameras, cameras)
+        if total > MAX_CHUNK_INTERSECTIONS:
+            flush()
+            pending = [(s * cameras, cameras)]
+            while pending:   # split the scene's cameras until each range fits
+                image0, count = pending.pop(0)
+                if count > 1 and count_of(image0, count) > MAX_CHUNK_INTERSECTIONS:
+                    half = count // 2
+                    pending[:0] = [(image0, half), (image0 + half, count - half)]
+                else:
+                    chunks.append(Chunk(image0, count, surfels, count == cameras))
+        elif group_total + total > MAX_CHUNK_INTERSECTIONS:
+            flush()
+            group, group_total = [s], total
+        else:
+            group.append(s)
+            group_total += total
+    flush()
+    return [_bin_chunk(ch, records, radii, surfels, width, height) for ch in chunks]
 
 
 def bin_records(records, record_stride, radii, image_ids, records_per_image, images, width,
                 height):
-    """Depth-ordered per-tile record lists (rasterize.cu:454-493): point_list, ranges."""
+    """Depth-ordered per-tile record lists (rasterize.cu:454-493): point_list, ranges.
+
+    One pass (no chunking): used by the reference-layout entry points and the tests.
+    """
     device = records.device
     stream = nat.stream_of(device)
     R = records.shape[0]
@@ -186,10 +338,6 @@ def bin_records(records, record_stride, radii, image_ids, records_per_image, ima
              R, records_per_image, images, width, height, nat.ptr(ws1), bytes1.value,
              ctypes.byref(total), stream)
     intersections = total.value
-    if WORK is not None:
-        WORK["records"] = WORK.get("records", 0) + R
-        WORK["intersections"] = WORK.get("intersections", 0) + intersections
-        WORK["tiles"] = WORK.get("tiles", 0) + images * tw * th
     bytes2 = ctypes.c_size_t()
     nat.call("gs_bin_sort_workspace", R, intersections, images, width, height,
              ctypes.byref(bytes2))
@@ -397,16 +545,15 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
                          + [means.new_zeros((S * N, pad))], -1)
         row_mode = nat.ROWS_PER_SURFEL
     images = S * C
-    point_list, ranges = bin_records(records, nat.RECORD_FLOATS, radii, None, max(N, 1), images,
-                                     width, height)
+    chunks = bin_chunks(records, radii, S, C, max(N, 1), width, height)
     selected = None
     projected_means = xy
     if packed:
         selected = torch.nonzero(radii > 0).reshape(-1)
         projected_means = xy[selected]
     maps = Composite.apply(records, projected_means, rows, backgrounds.reshape(-1, 3), selected,
-                           point_list, ranges, row_mode, C, max(N, 1), images, width, height,
-                           neural, float(near_plane), float(far_plane))
+                           chunks, row_mode, C, max(N, 1), images, width, height, neural,
+                           float(near_plane), float(far_plane))
     maps = maps.reshape(batch + (C, height, width, 9))
     ids = selected if packed else torch.arange(P, device=device)
     meta = {

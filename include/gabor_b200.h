@@ -142,9 +142,10 @@ int gs_bin_static(const float* records, int record_stride, const int32_t* radii,
  * renderBackward (rasterize.cu:283-399).  One CTA per 16x16 tile.
  * row_mode selects the appearance row of a record (GS_ROWS_*); `cameras`,
  * `surfels` are used by GS_ROWS_PER_SURFEL, primitive_ids by GS_ROWS_EXPLICIT.
- * Backward adds into grad_records / grad_rows / grad_backgrounds, which it zeroes
- * first; grad_xy (nullable, [R][2]) receives the slot 9-10 (screen-centre)
- * gradients instead of grad_records when given.
+ * Backward adds into grad_records / grad_rows / grad_backgrounds (the caller
+ * zeroes them, so several calls over image chunks can accumulate into shared
+ * appearance rows); grad_xy (nullable, [R][2]) receives the slot 9-10
+ * (screen-centre) gradients instead of grad_records when given.
  * counters (nullable, uint64[2], zeroed by the caller) receives the work done:
  * [0] ray/splat samples tested, [1] contributions accepted (blended forward,
  * differentiated backward).  A NULL pointer selects kernels without counting.

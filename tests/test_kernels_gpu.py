@@ -232,3 +232,50 @@ def test_benchmark_like_scene_gradients_in_norm(method):
         per_item = ((a - e).abs().amax(-1) / scale).reshape(-1)
         frac = (per_item <= 1e-3).double().mean().item()
         assert frac >= 0.97, f"{name}: only {frac:.2%} of entries within 1e-3 of scale"
+
+
+@pytest.mark.parametrize("method,sh_degree", [("classic", None), ("classic", 2), ("neural", None)])
+def test_image_chunks_match_single_pass(method, sh_degree, monkeypatch):
+    """Batches too large to bin at once are split into image chunks (groups of whole
+    scenes, or camera ranges of one scene); images are identical and gradients equal
+    to float-atomic order."""
+    v = random_scene(method, scenes=3, cameras=3, n=300, width=W, height=H, sh_degree=sh_degree)
+    fn = rasterize_gabors if method == "classic" else rasterize_neural_gabors
+    kw = {"sh_degree": sh_degree} if method == "classic" else {}
+    one = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    maps_one = maps_from_result(fn(**one, width=W, height=H, **kw))
+    g_one = torch.autograd.grad(maps_one.sum(), tuple(one.values()))
+    per_camera = []
+    monkeypatch.setattr(rendering, "MAX_CHUNK_INTERSECTIONS", 1)   # forces per-camera chunks
+    original = rendering._bin_chunk
+    monkeypatch.setattr(rendering, "_bin_chunk",
+                        lambda ch, *a: per_camera.append(ch.images) or original(ch, *a))
+    many = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    maps_many = maps_from_result(fn(**many, width=W, height=H, **kw))
+    assert per_camera == [1] * 9
+    assert torch.equal(maps_many, maps_one)
+    g_many = torch.autograd.grad(maps_many.sum(), tuple(many.values()))
+    for name, a, e in zip(one, g_many, g_one):
+        assert_grads_close(a, e, name, elementwise=1e-4)
+
+
+def test_scene_grouped_chunks(monkeypatch):
+    """A limit between one and two scenes' intersections groups whole scenes."""
+    v = random_scene("classic", scenes=4, cameras=2, n=200, width=W, height=H)
+    values = ordered(v, "classic")
+    base = maps_from_result(rasterize_gabors(**values, width=W, height=H))
+    rendering.WORK = {}
+    try:
+        rasterize_gabors(**values, width=W, height=H)
+        total = rendering.WORK["intersections"]
+    finally:
+        rendering.WORK = None
+    seen = []
+    original = rendering._bin_chunk
+    monkeypatch.setattr(rendering, "MAX_CHUNK_INTERSECTIONS", total // 2 + total // 8)
+    monkeypatch.setattr(rendering, "_bin_chunk",
+                        lambda ch, *a: seen.append((ch.image0, ch.images)) or original(ch, *a))
+    grouped = maps_from_result(rasterize_gabors(**values, width=W, height=H))
+    assert len(seen) >= 2 and all(images % 2 == 0 for _, images in seen)
+    assert sum(images for _, images in seen) == 8
+    assert torch.equal(grouped, base)
