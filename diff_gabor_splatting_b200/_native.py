@@ -81,15 +81,20 @@ TIMER = None
 
 def call(name: str, *args) -> None:
     """Call one C entry point and check its status."""
+    check(call_status(name, *args), name)
+
+
+def call_status(name: str, *args) -> int:
+    """Call one C entry point and return its status (timed when a timer is set)."""
     if TIMER is None:
-        check(getattr(lib, name)(*args), name)
-        return
+        return getattr(lib, name)(*args)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record()
-    check(getattr(lib, name)(*args), name)
+    status = getattr(lib, name)(*args)
     end.record()
     TIMER.add(name, start, end)
+    return status
 
 
 class StageTimer:

@@ -232,8 +232,8 @@ def _count(records, radii, R, per_image, images, width, height):
     nat.call("gs_bin_count_workspace", R, ctypes.byref(bytes1))
     ws1 = torch.empty((max(bytes1.value, 1),), device=device, dtype=torch.uint8)
     total = ctypes.c_int64()
-    status = nat.lib.gs_bin_count(records.address, nat.RECORD_FLOATS, radii.address, None, R,
-                                  per_image, images,
+    status = nat.call_status("gs_bin_count", records.address, nat.RECORD_FLOATS, radii.address,
+                             None, R, per_image, images,
                                   width, height, nat.ptr(ws1), bytes1.value, ctypes.byref(total),
                                   nat.stream_of(device))
     if status not in (0, GS_ERR_LIMIT) or (status == GS_ERR_LIMIT and total.value <= INT32_MAX):
