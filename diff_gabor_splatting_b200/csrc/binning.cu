@@ -188,12 +188,35 @@ __global__ __launch_bounds__(kBinThreads) void expand_kernel(
     }
 }
 
+// Tile ranges from the sorted tile ids: a range starts where the id changes.  Each
+// thread reads four consecutive ids with one 16-byte load plus the id before them.
+constexpr int kRangeItems = 4;
+
 __global__ void ranges_kernel(int64_t I, const uint32_t* __restrict__ keys, int2* __restrict__ ranges) {
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= I) return;
-    const uint32_t t = keys[i];
-    if (i == 0 || keys[i - 1] != t) ranges[t].x = int(i);
-    if (i == I - 1 || keys[i + 1] != t) ranges[t].y = int(i + 1);
+    const int64_t i0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * kRangeItems;
+    if (i0 >= I) return;
+    uint32_t t[kRangeItems + 1];
+    t[0] = i0 ? keys[i0 - 1] : 0xffffffffu;
+    if (i0 + kRangeItems <= I) {
+        const uint4 v = *reinterpret_cast<const uint4*>(keys + i0);
+        t[1] = v.x; t[2] = v.y; t[3] = v.z; t[4] = v.w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < kRangeItems; ++k) t[k + 1] = i0 + k < I ? keys[i0 + k] : 0xffffffffu;
+    }
+#pragma unroll
+    for (int k = 0; k < kRangeItems; ++k) {
+        const int64_t i = i0 + k;
+        if (i >= I) break;
+        if (t[k + 1] != t[k]) {
+            ranges[t[k + 1]].x = int(i);
+            if (i0 + k > 0) ranges[t[k]].y = int(i);
+        }
+    }
+    if (i0 + kRangeItems >= I) {   // the thread holding the last id closes its range
+        const int64_t last = I - 1;
+        ranges[keys[last]].y = int(I);
+    }
 }
 
 unsigned blocks_for(int64_t n) { return unsigned((n + kBinThreads - 1) / kBinThreads); }
@@ -318,7 +341,8 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
     size_t temp_bytes = L.temp_bytes;
     GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, point_list,
                                             int(I), 0, tile_bits(n_tiles), s));
-    ranges_kernel<<<blocks_for(I), kBinThreads, 0, s>>>(I, keys_out, reinterpret_cast<int2*>(ranges));
+    ranges_kernel<<<blocks_for((I + kRangeItems - 1) / kRangeItems), kBinThreads, 0, s>>>(
+        I, keys_out, reinterpret_cast<int2*>(ranges));
     GS_CHECK_LAUNCH("ranges_kernel");
     return GS_OK;
 }

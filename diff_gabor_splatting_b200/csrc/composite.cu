@@ -90,20 +90,25 @@ __device__ __forceinline__ float reject_threshold(float opacity) {
     return 2.f * logf(255.f * opacity) + 1e-4f;
 }
 
-template <bool Neural>
+template <bool Neural, int kSize = kBatch>
 struct Batch {
     static constexpr int kRow = Neural ? kNeuralRow : kClassicRow;
-    int ids[kBatch];
-    int64_t rows[kBatch];
-    float4 geo[kBatch][kRec / 4];
-    float4 app[kBatch][kRow / 4];
+    static constexpr bool kNeural = Neural;
+    int ids[kSize];
+    int64_t rows[kSize];
+    float4 geo[kSize][kRec / 4];
+    float4 app[kSize][kRow / 4];
 };
 
-// Stage `count` records (list positions first + stride*e) and their rows.
-template <bool Neural>
-__device__ __forceinline__ void load_batch(Batch<Neural>& b, const Params& P, int first, int stride,
+// Stage `count` records (list positions first + stride*e) and their rows.  Per record
+// it also stores the early-rejection threshold in record slot 18 (memory pad) and,
+// for classic rows, 2*pi*magnitude in place of each magnitude: the factor every wave
+// argument uses, computed once per record instead of once per sample (the same
+// float product the per-sample expression 2 * pi * magnitude rounds to).
+template <class B>
+__device__ __forceinline__ void load_batch(B& b, const Params& P, int first, int stride,
                                            int count, int rank) {
-    constexpr int kRow = Batch<Neural>::kRow;
+    constexpr int kRow = B::kRow;
     constexpr int kPer = kRec / 4 + kRow / 4;
     __syncthreads();
     if (rank < count) {
@@ -120,7 +125,14 @@ __device__ __forceinline__ void load_batch(Batch<Neural>& b, const Params& P, in
             if (part == 4) v.z = reject_threshold(v.y);
             b.geo[e][part] = v;
         } else {
-            b.app[e][part - kRec / 4] = __ldg(P.rows + b.rows[e] * (kRow / 4) + (part - kRec / 4));
+            const int q = part - kRec / 4;
+            float4 v = __ldg(P.rows + b.rows[e] * (kRow / 4) + q);
+            if constexpr (!B::kNeural) {
+                constexpr float kTwoPi = 2 * kPi;
+                if (q == 2) { v.z = kTwoPi * v.z; v.w = kTwoPi * v.w; }   // magnitudes 0-1
+                if (q == 3) { v.x = kTwoPi * v.x; v.y = kTwoPi * v.y; }   // magnitudes 2-3
+            }
+            b.app[e][q] = v;
         }
     }
     __syncthreads();
@@ -177,6 +189,17 @@ struct Directions {
     }
 };
 
+// Sine and cosine for gradient arithmetic only (images use the exact cosf/sinf):
+// Cody-Waite reduction of x by 2*pi with a two-term constant (2*pi = hi + lo,
+// hi = float(2*pi)), then the SFU approximations on [-pi, pi].  Absolute error below
+// 1e-6 for |x| < 1e4, far inside the gradients' 1e-4 tolerance.
+__device__ __forceinline__ void grad_sincos(float x, float* s, float* c) {
+    const float k = rintf(x * 0.159154943091895336f);
+    float r = fmaf(-k, 6.28318548202514648f, x);
+    r = fmaf(-k, -1.74845553e-07f, r);
+    __sincosf(r, s, c);
+}
+
 // Appearance: rasterize.cu:105-138.
 template <bool Neural>
 __device__ __forceinline__ void appearance_forward(const float* a, const float* g, const Sample& v,
@@ -204,7 +227,7 @@ __device__ __forceinline__ void appearance_forward(const float* a, const float* 
 #pragma unroll
         for (int f = 0; f < 4; ++f) {
             const float dot = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
-            const float wave = cosf(2 * kPi * a[10 + f] * dot + a[14 + f]);
+            const float wave = cosf(a[10 + f] * dot + a[14 + f]);   // a[10+f] = 2 pi mag_f
             h1 += a[6 + f] * 0.5f * (1 + wave);
             h2 += a[6 + f] * 0.5f * (1 - wave);
         }
@@ -233,7 +256,7 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
     for (int start = range.x; start < range.y; start += kBatch) {
         if (__syncthreads_count(done) == kBlock) break;
         const int count = min(kBatch, range.y - start);
-        load_batch<Neural>(batch, P, start, 1, count, rank);
+        load_batch(batch, P, start, 1, count, rank);
         for (int j = 0; j < count && !done; ++j) {
             const float* g = reinterpret_cast<const float*>(batch.geo[j]);
             Sample v;
@@ -292,9 +315,15 @@ struct Fields {
     }
 };
 
-// Reduce `vals` across the warp and add each field's warp sum to acc[slot].
+constexpr int kBackBatch = 32;
+constexpr int kWarps = kBlock / 32;
+
+// Reduce `vals` across the warp (lane i ends up owning packed field i) and store the
+// warp's sums in its own shared row; `mask` records which warps stored for the record.
+// Plain stores, no shared atomics: the CTA's eight rows are summed at the flush.
 template <bool Neural>
-__device__ __forceinline__ void warp_accumulate(float* vals, float* acc, int lane) {
+__device__ __forceinline__ void warp_store(float* vals, float* row, unsigned* mask, int warp,
+                                           int lane) {
     using F = Fields<Neural>;
     constexpr int kFull = F::kCount / 32;
     constexpr int kRest = F::kCount - kFull * 32;
@@ -304,7 +333,7 @@ __device__ __forceinline__ void warp_accumulate(float* vals, float* acc, int lan
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = vals[chunk * 32 + i];
         warp_reduce_scatter<32>(v, lane);
-        if (v[0] != 0.f) atomicAdd(acc + F::slot(chunk * 32 + lane), v[0]);
+        row[chunk * 32 + lane] = v[0];
     }
     if constexpr (kRest > 0) {
         constexpr int kPad = kRest <= 1 ? 1 : kRest <= 2 ? 2 : kRest <= 4 ? 4 : kRest <= 8 ? 8
@@ -316,20 +345,35 @@ __device__ __forceinline__ void warp_accumulate(float* vals, float* acc, int lan
         for (int i = 0; i < kPad; ++i) v[i] = i < kRest ? vals[kFull * 32 + i] : 0.f;
         warp_reduce_scatter<kPad>(v, lane);
         const int field = lane >> kShift;
-        if ((lane & ((1 << kShift) - 1)) == 0 && field < kRest && v[0] != 0.f)
-            atomicAdd(acc + F::slot(kFull * 32 + field), v[0]);
+        if ((lane & ((1 << kShift) - 1)) == 0 && field < kRest) row[kFull * 32 + field] = v[0];
     }
+    if (lane == 0) atomicOr(mask, 1u << warp);
 }
+
+// Shared memory of the backward kernel: the record batch, one partial-sum row per
+// (warp, record), and the per-record masks of warps that stored.
+template <bool Neural>
+struct BackShared {
+    using F = Fields<Neural>;
+    static constexpr int kStride = (F::kCount + 3) / 4 * 4;   // 36 classic, 76 neural
+    Batch<Neural, kBackBatch> batch;
+    float rows[kWarps][kBackBatch][kStride];
+    unsigned mask[kBackBatch];
+    int warp_max[kWarps];
+    float bg[3];
+};
 
 template <bool Neural, bool Count>
 __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params P) {
     unsigned tests = 0, accepts = 0;
     using F = Fields<Neural>;
+    using S = BackShared<Neural>;
     constexpr int kRow = Batch<Neural>::kRow;
-    __shared__ Batch<Neural> batch;
-    __shared__ float acc[kBatch * F::kSlots];
-    __shared__ int warp_max[kBlock / 32];
-    __shared__ float bg_acc[3];
+    extern __shared__ float4 dynamic_smem[];
+    S& sh = *reinterpret_cast<S*>(dynamic_smem);
+    auto& batch = sh.batch;
+    int* warp_max = sh.warp_max;
+    float* bg_acc = sh.bg;
     const int lane = (threadIdx.y * kTile + threadIdx.x) & 31;
     const int warp = (threadIdx.y * kTile + threadIdx.x) >> 5;
     const int tiles_per_image = P.tw * P.th;
@@ -340,7 +384,6 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
     const bool inside = x < P.width && y < P.height;
     const int64_t pixel = (int64_t(image) * P.height + y) * P.width + x;
     const int last = inside ? P.contributors[pixel] : 0;
-    for (int i = rank; i < kBatch * F::kSlots; i += kBlock) acc[i] = 0.f;
     if (rank < 3) bg_acc[rank] = 0.f;
     int wmax = last;
 #pragma unroll
@@ -363,7 +406,7 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
             bgv[c] = final_t * go[c];
         }
         warp_reduce_scatter<4>(bgv, lane);
-        __syncthreads();   // bg_acc and acc initialised
+        __syncthreads();   // bg_acc initialised
         if ((lane & 7) == 0 && (lane >> 3) < 3 && bgv[0] != 0.f) atomicAdd(bg_acc + (lane >> 3), bgv[0]);
     }
     int block_last = 0;
@@ -372,9 +415,11 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
     const int2 range = P.ranges[tile];
     const Directions dirs;
     const float mscale = P.far_plane / (P.far_plane - P.near_plane);
-    for (int start = block_last; start > 0; start -= kBatch) {
-        const int count = min(kBatch, start);
-        load_batch<Neural>(batch, P, range.x + start - 1, -1, count, rank);
+    for (int start = block_last; start > 0; start -= kBackBatch) {
+        const int count = min(kBackBatch, start);
+        __syncthreads();   // every thread has finished the previous batch's flush
+        if (rank < kBackBatch) sh.mask[rank] = 0u;
+        load_batch(batch, P, range.x + start - 1, -1, count, rank);
         for (int j = 0; j < count; ++j) {
             const float* g = reinterpret_cast<const float*>(batch.geo[j]);
             const float* a = reinterpret_cast<const float*>(batch.app[j]);
@@ -395,22 +440,39 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                 float waves[4], sines[4];
                 T /= 1 - v.alpha;
                 const float w = T * v.alpha;
+                // colour replay: feeds only gradients, so the waves, the SIREN's sines
+                // and its sigmoid use the fast forms (cosines kept for the adjoint)
+                float coss[6];
                 if constexpr (Neural) {
-                    appearance_forward<Neural>(a, g, v, dirs, color, hidden, pre);
+                    const float input[5] = {v.s[0] / 3, v.s[1] / 3, g[14], g[15], g[16]};
+#pragma unroll
+                    for (int h = 0; h < 6; ++h) {
+                        float z = a[30 + h];
+#pragma unroll
+                        for (int k = 0; k < 5; ++k) z += a[h * 5 + k] * input[k];
+                        pre[h] = z;
+                        grad_sincos(30 * z, &hidden[h], &coss[h]);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) {
+                        float z = a[54 + c];
+#pragma unroll
+                        for (int h = 0; h < 6; ++h) z += a[36 + c * 6 + h] * hidden[h];
+                        color[c] = __frcp_rn(1.f + __expf(-z));
+                    }
                 } else {
-                    // colour replay with sine and cosine of each wave from one sincosf
                     float h1 = 0, h2 = 0;
 #pragma unroll
                     for (int f = 0; f < 4; ++f) {
                         const float dot = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
-                        sincosf(2 * kPi * a[10 + f] * dot + a[14 + f], &sines[f], &waves[f]);
+                        grad_sincos(a[10 + f] * dot + a[14 + f], &sines[f], &waves[f]);
                         h1 += a[6 + f] * 0.5f * (1 + waves[f]);
                         h2 += a[6 + f] * 0.5f * (1 - waves[f]);
                     }
 #pragma unroll
                     for (int c = 0; c < 3; ++c) color[c] = h1 * a[c] + h2 * a[3 + c];
                 }
-                const float m = mscale * (1 - P.near_plane / v.depth);
+                const float m = mscale * (1 - __fdividef(P.near_plane, v.depth));
                 float gw = go[4] * v.depth + go[8] * (m * m * total_a + m2 - 2 * m * m1);
 #pragma unroll
                 for (int c = 0; c < 3; ++c) {
@@ -438,7 +500,7 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                     }
 #pragma unroll
                     for (int h = 0; h < 6; ++h) {
-                        const float gz = gh[h] * 30 * cosf(30 * pre[h]);
+                        const float gz = gh[h] * 30 * coss[h];
                         ga[30 + h] += gz;
 #pragma unroll
                         for (int k = 0; k < 5; ++k) {
@@ -455,7 +517,6 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                     for (int f = 0; f < 4; ++f) {
                         const float dx = dirs.c[f], dy = dirs.s[f];
                         const float dot = dx * v.s[0] + dy * v.s[1];
-                        const float angle = 2 * kPi * a[10 + f] * dot + a[14 + f];
                         const float wave = waves[f], sine = sines[f];
                         float gwf = 0, gt = 0;
 #pragma unroll
@@ -468,8 +529,8 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                         ga[6 + f] += gwf;
                         ga[10 + f] += gt * 2 * kPi * dot;
                         ga[14 + f] += gt;
-                        gs[0] += gt * 2 * kPi * a[10 + f] * dx;
-                        gs[1] += gt * 2 * kPi * a[10 + f] * dy;
+                        gs[0] += gt * a[10 + f] * dx;   // a[10+f] = 2 pi mag_f
+                        gs[1] += gt * a[10 + f] * dy;
                     }
                 }
                 // geometry: rasterize.cu:359-385
@@ -507,15 +568,20 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                     gg[6 + k] += x * gk[k] + y * gl[k];
                 }
             }
-            warp_accumulate<Neural>(vals, acc + j * F::kSlots, lane);
+            warp_store<Neural>(vals, sh.rows[warp][j], &sh.mask[j], warp, lane);
         }
-        // flush this batch's per-record sums: one global atomic per (tile, record, field)
+        // flush: sum the warps' rows of each record in warp order, one global atomic per
+        // (tile, record, field)
         __syncthreads();
-        for (int i = rank; i < count * F::kSlots; i += kBlock) {
-            const float val = acc[i];
+        for (int i = rank; i < count * F::kCount; i += kBlock) {
+            const int e = i / F::kCount, field = i % F::kCount;
+            const unsigned mask = sh.mask[e];
+            float val = 0.f;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w)
+                if (mask & (1u << w)) val += sh.rows[w][e][field];
             if (val == 0.f) continue;
-            acc[i] = 0.f;
-            const int e = i / F::kSlots, slot = i % F::kSlots;
+            const int slot = F::slot(field);
             if (slot < kRec) {
                 const int64_t r = batch.ids[e];
                 if (P.grad_xy && (slot == 9 || slot == 10))
@@ -653,14 +719,21 @@ extern "C" int gs_composite_backward(const float* records, const float* rows, in
     const int64_t tiles = images * P.tw * P.th;
     P.counters = reinterpret_cast<unsigned long long*>(counters);
     const dim3 block(kTile, kTile);
+    auto launch = [&](auto kernel, size_t smem) -> int {
+        GS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     int(smem)));
+        kernel<<<unsigned(tiles), block, smem, s>>>(P);
+        return GS_OK;
+    };
     if (neural && counters)
-        composite_backward_kernel<true, true><<<unsigned(tiles), block, 0, s>>>(P);
+        st = launch(composite_backward_kernel<true, true>, sizeof(BackShared<true>));
     else if (neural)
-        composite_backward_kernel<true, false><<<unsigned(tiles), block, 0, s>>>(P);
+        st = launch(composite_backward_kernel<true, false>, sizeof(BackShared<true>));
     else if (counters)
-        composite_backward_kernel<false, true><<<unsigned(tiles), block, 0, s>>>(P);
+        st = launch(composite_backward_kernel<false, true>, sizeof(BackShared<false>));
     else
-        composite_backward_kernel<false, false><<<unsigned(tiles), block, 0, s>>>(P);
+        st = launch(composite_backward_kernel<false, false>, sizeof(BackShared<false>));
+    if (st) return st;
     GS_CHECK_LAUNCH("composite_backward_kernel");
     return GS_OK;
 }

@@ -241,12 +241,15 @@ def _count(records, radii, R, per_image, images, width, height):
     return ws1, bytes1.value, total.value
 
 
-def _bin_chunk(ch, records, radii, surfels, width, height):
+def _bin_chunk(ch, records, radii, surfels, width, height, counted=None):
+    """Sort one chunk's (record, tile) slots; ``counted`` reuses a finished count."""
     device = records.device
     rec = _at(records, ch.record0 * nat.RECORD_FLOATS)
     rad = _at(radii, ch.record0)
-    ws1, bytes1, total = _count(_Ptr(rec, device), _Ptr(rad, device), ch.record_count, surfels,
-                                ch.images, width, height)
+    if counted is None:
+        counted = _count(_Ptr(rec, device), _Ptr(rad, device), ch.record_count, surfels,
+                         ch.images, width, height)
+    ws1, bytes1, total = counted
     tw, th = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
     bytes2 = ctypes.c_size_t()
     nat.call("gs_bin_sort_workspace", ch.record_count, total, ch.images, width, height,
@@ -286,10 +289,12 @@ def bin_chunks(records, radii, scenes, cameras, surfels, width, height):
     def count_of(image0, count):
         rec = _Ptr(_at(records, image0 * surfels * nat.RECORD_FLOATS), device)
         rad = _Ptr(_at(radii, image0 * surfels), device)
-        return _count(rec, rad, count * surfels, surfels, count, width, height)[2]
+        return _count(rec, rad, count * surfels, surfels, count, width, height)
 
-    if count_of(0, images) <= MAX_CHUNK_INTERSECTIONS:
-        return [_bin_chunk(whole, records, radii, surfels, width, height)]
+    counted = count_of(0, images)
+    if counted[2] <= MAX_CHUNK_INTERSECTIONS:
+        return [_bin_chunk(whole, records, radii, surfels, width, height, counted)]
+    del counted
     chunks, group, group_total = [], [], 0
 
     def flush():
@@ -299,13 +304,13 @@ def bin_chunks(records, radii, scenes, cameras, surfels, width, height):
         group, group_total = [], 0
 
     for s in range(scenes):
-        total = count_of(s * cameras, cameras)
+        total = count_of(s * cameras, cameras)[2]
         if total > MAX_CHUNK_INTERSECTIONS:
             flush()
             pending = [(s * cameras, cameras)]
             while pending:   # split the scene's cameras until each range fits
                 image0, count = pending.pop(0)
-                if count > 1 and count_of(image0, count) > MAX_CHUNK_INTERSECTIONS:
+                if count > 1 and count_of(image0, count)[2] > MAX_CHUNK_INTERSECTIONS:
                     half = count // 2
                     pending[:0] = [(image0, half), (image0 + half, count - half)]
                 else:
