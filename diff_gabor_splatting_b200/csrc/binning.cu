@@ -56,7 +56,7 @@ CountLayout count_layout(int64_t R) {
 }
 
 struct SortLayout {
-    size_t keys_in, keys_out, vals_in, temp, temp_bytes, total;
+    size_t keys_in, keys_out, vals_in, owners, temp, temp_bytes, total;
 };
 
 int tile_bits(int64_t n_tiles) {
@@ -75,6 +75,7 @@ SortLayout sort_layout(int64_t I, int64_t n_tiles) {
     L.keys_in = take(sizeof(uint32_t) * I);
     L.keys_out = take(sizeof(uint32_t) * I);
     L.vals_in = take(sizeof(int) * I);
+    L.owners = take(sizeof(int64_t) * ((I + 1023) / 1024 + 1));
     L.temp_bytes = sort_bytes;
     L.temp = take(sort_bytes);
     L.total = off;
@@ -123,19 +124,41 @@ __device__ __forceinline__ int64_t first_above(const int64_t* __restrict__ offse
     return lo;
 }
 
+// first_owner[b] = the record (in depth order) owning slot b * kExpandSlots: each
+// record writes the entries of the blocks whose first slot falls in its slot range.
+__global__ void first_owner_kernel(int64_t R, int64_t blocks, const int64_t* __restrict__ offsets,
+                                   int64_t* __restrict__ first_owner) {
+    const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= R) return;
+    const int64_t begin = j ? offsets[j - 1] : 0, end = offsets[j];
+    for (int64_t b = (begin + kExpandSlots - 1) / kExpandSlots; b * kExpandSlots < end && b < blocks;
+         ++b)
+        first_owner[b] = j;
+}
+
 __global__ __launch_bounds__(kBinThreads) void expand_kernel(
     int64_t I, int64_t R, const int64_t* __restrict__ offsets, const int* __restrict__ order,
     const float* __restrict__ records, int stride, const int* __restrict__ radii,
     const int64_t* __restrict__ image_ids, int64_t per_image, int tw, int th,
-    uint32_t* __restrict__ tile_keys, int* __restrict__ values) {
+    const int64_t* __restrict__ first_owner, uint32_t* __restrict__ tile_keys,
+    int* __restrict__ values) {
     __shared__ int64_t s_end[kExpandSlots];
     __shared__ int4 s_rect[kExpandSlots];    // x0, y0, width, record
     __shared__ uint32_t s_base[kExpandSlots];   // image * tw * th
     __shared__ int64_t s_first, s_last;
     const int64_t i0 = int64_t(blockIdx.x) * kExpandSlots;
     const int64_t i1 = min(i0 + kExpandSlots, I) - 1;
-    if (threadIdx.x == 0) s_first = first_above(offsets, R, i0);
-    if (threadIdx.x == 32) s_last = first_above(offsets, R, i1);
+    if (threadIdx.x == 0) s_first = first_owner[blockIdx.x];
+    if (threadIdx.x == 32) {
+        // an upper bound on the owner of the block's last slot, from the next block's
+        // first owner (extra empty records in the range are harmless to the search)
+        if (i1 + 1 < I) {
+            const int64_t next = first_owner[blockIdx.x + 1];
+            s_last = next > 0 && offsets[next - 1] > i1 ? next - 1 : next;
+        } else {
+            s_last = first_above(offsets, R, i1);
+        }
+    }
     __syncthreads();
     const int64_t first = s_first;
     const int64_t owners = s_last - first + 1;
@@ -332,11 +355,14 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
     auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
     auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
     auto* vals_in = reinterpret_cast<int*>(base + L.vals_in);
+    auto* owners = reinterpret_cast<int64_t*>(base + L.owners);
     void* temp = base + L.temp;
-    expand_kernel<<<unsigned((I + kExpandSlots - 1) / kExpandSlots), kBinThreads, 0, s>>>(
-        I, R, offsets, order, records, record_stride,
-                                                        radii, image_ids, records_per_image, tw, th,
-                                                        keys_in, vals_in);
+    const int64_t expand_blocks = (I + kExpandSlots - 1) / kExpandSlots;
+    first_owner_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, expand_blocks, offsets, owners);
+    GS_CHECK_LAUNCH("first_owner_kernel");
+    expand_kernel<<<unsigned(expand_blocks), kBinThreads, 0, s>>>(
+        I, R, offsets, order, records, record_stride, radii, image_ids, records_per_image, tw, th,
+        owners, keys_in, vals_in);
     GS_CHECK_LAUNCH("expand_kernel");
     size_t temp_bytes = L.temp_bytes;
     GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, point_list,

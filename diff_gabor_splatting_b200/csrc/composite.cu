@@ -364,7 +364,7 @@ struct BackShared {
 };
 
 template <bool Neural, bool Count>
-__global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params P) {
+__global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_kernel(const Params P) {
     unsigned tests = 0, accepts = 0;
     using F = Fields<Neural>;
     using S = BackShared<Neural>;
@@ -442,7 +442,7 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                 const float w = T * v.alpha;
                 // colour replay: feeds only gradients, so the waves, the SIREN's sines
                 // and its sigmoid use the fast forms (cosines kept for the adjoint)
-                float coss[6];
+                float coss[6], dots[4], h1, h2;
                 if constexpr (Neural) {
                     const float input[5] = {v.s[0] / 3, v.s[1] / 3, g[14], g[15], g[16]};
 #pragma unroll
@@ -461,11 +461,12 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
                         color[c] = __frcp_rn(1.f + __expf(-z));
                     }
                 } else {
-                    float h1 = 0, h2 = 0;
+                    h1 = 0;
+                    h2 = 0;
 #pragma unroll
                     for (int f = 0; f < 4; ++f) {
-                        const float dot = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
-                        grad_sincos(a[10 + f] * dot + a[14 + f], &sines[f], &waves[f]);
+                        dots[f] = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
+                        grad_sincos(a[10 + f] * dots[f] + a[14 + f], &sines[f], &waves[f]);
                         h1 += a[6 + f] * 0.5f * (1 + waves[f]);
                         h2 += a[6 + f] * 0.5f * (1 - waves[f]);
                     }
@@ -513,24 +514,26 @@ __global__ __launch_bounds__(kBlock) void composite_backward_kernel(const Params
 #pragma unroll
                     for (int k = 0; k < 3; ++k) gg[14 + k] += gi[k + 2];
                 } else {
+                    // The reference's per-wave loop (rasterize.cu:173-195) factored: summed
+                    // over waves, d colour / d c1 = h1 and d colour / d c2 = h2; every
+                    // wave's weight and phase terms go through S1 = sum gc (c1 + c2) and
+                    // S2 = sum gc (c1 - c2).
+                    float S1 = 0, S2 = 0;
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) {
+                        ga[c] = gc[c] * h1;
+                        ga[3 + c] = gc[c] * h2;
+                        S1 += gc[c] * (a[c] + a[3 + c]);
+                        S2 += gc[c] * (a[c] - a[3 + c]);
+                    }
 #pragma unroll
                     for (int f = 0; f < 4; ++f) {
-                        const float dx = dirs.c[f], dy = dirs.s[f];
-                        const float dot = dx * v.s[0] + dy * v.s[1];
-                        const float wave = waves[f], sine = sines[f];
-                        float gwf = 0, gt = 0;
-#pragma unroll
-                        for (int c = 0; c < 3; ++c) {
-                            ga[c] += gc[c] * a[6 + f] * 0.5f * (1 + wave);
-                            ga[3 + c] += gc[c] * a[6 + f] * 0.5f * (1 - wave);
-                            gwf += gc[c] * 0.5f * ((1 + wave) * a[c] + (1 - wave) * a[3 + c]);
-                            gt += gc[c] * a[6 + f] * 0.5f * sine * (a[3 + c] - a[c]);
-                        }
-                        ga[6 + f] += gwf;
-                        ga[10 + f] += gt * 2 * kPi * dot;
-                        ga[14 + f] += gt;
-                        gs[0] += gt * a[10 + f] * dx;   // a[10+f] = 2 pi mag_f
-                        gs[1] += gt * a[10 + f] * dy;
+                        const float gt = -0.5f * a[6 + f] * sines[f] * S2;
+                        ga[6 + f] = 0.5f * (S1 + waves[f] * S2);
+                        ga[10 + f] = gt * (2 * kPi) * dots[f];
+                        ga[14 + f] = gt;
+                        gs[0] += gt * a[10 + f] * dirs.c[f];   // a[10+f] = 2 pi mag_f
+                        gs[1] += gt * a[10 + f] * dirs.s[f];
                     }
                 }
                 // geometry: rasterize.cu:359-385
