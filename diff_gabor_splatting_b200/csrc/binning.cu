@@ -82,6 +82,46 @@ SortLayout sort_layout(int64_t I, int64_t n_tiles) {
     return L;
 }
 
+// Tile rectangle of a record.  Plain: the reference's square bounds (tile_rect).
+// Tight (GS_BIN_TIGHT, records carrying opacity in slot 17): additionally clipped to the
+// tiles that can hold a sample with alpha >= 1/255.  Such a sample has
+// o exp(-min(rho3, rho2)/2) >= 1/255, so min(rho3, rho2) <= thr = 2 ln(255 o): it lies
+// in the image of the local disc u^2 + v^2 <= thr (an ellipse, bounded by the same
+// conic formula the reference uses for its 3-sigma disc, rendering.py:189-196, with 9
+// replaced by thr) or within sqrt(thr/2) pixels of the centre (the rho2 branch).  The
+// level is widened by 5% + 0.05 and the box by 2 pixels so float rounding of the
+// per-pixel test cannot reach outside it; records whose conic is not a bounded ellipse
+// keep the plain rectangle.  Images are unchanged; only tiles no sample of the record
+// can reach are dropped.
+__device__ __forceinline__ int4 bin_rect(const float* g, int radius, int tw, int th, bool tight) {
+    const int4 b = tile_rect(g[9], g[10], radius, tw, th);
+    if (!tight || b.z <= b.x || b.w <= b.y) return b;
+    const double o = g[17];
+    if (!(o * 255.0 >= 1.0 - 1e-6)) return make_int4(b.x, b.y, b.x, b.y);   // never accepted
+    const double thr = (2.0 * log(255.0 * o)) * 1.05 + 0.05;
+    const double t6 = g[6], t7 = g[7], t8 = g[8];
+    const double den = thr * (t6 * t6 + t7 * t7) - t8 * t8;
+    if (!(den < 0.0)) return b;
+    const double fa = thr / den, fc = -1.0 / den;
+    const double cx = fa * (g[0] * t6 + g[1] * t7) + fc * g[2] * t8;
+    const double cy = fa * (g[3] * t6 + g[4] * t7) + fc * g[5] * t8;
+    const double ex2 = cx * cx - (fa * (double(g[0]) * g[0] + double(g[1]) * g[1]) + fc * double(g[2]) * g[2]);
+    const double ey2 = cy * cy - (fa * (double(g[3]) * g[3] + double(g[4]) * g[4]) + fc * double(g[5]) * g[5]);
+    if (!(ex2 >= 0.0 && ey2 >= 0.0)) return b;
+    const double ex = sqrt(ex2), ey = sqrt(ey2), rd = sqrt(fmax(thr * 0.5, 0.0));
+    const double x0 = fmin(cx - ex, g[9] - rd) - 2.0, x1 = fmax(cx + ex, g[9] + rd) + 2.0;
+    const double y0 = fmin(cy - ey, g[10] - rd) - 2.0, y1 = fmax(cy + ey, g[10] + rd) + 2.0;
+    if (!(isfinite(x0) && isfinite(x1) && isfinite(y0) && isfinite(y1))) return b;
+    const double lim = 1e9;   // far outside any image; keeps the int conversion defined
+    const int tx0 = int(floor(fmin(fmax(x0, -lim), lim) / kTile));
+    const int tx1 = int(floor(fmin(fmax(x1, -lim), lim) / kTile)) + 1;
+    const int ty0 = int(floor(fmin(fmax(y0, -lim), lim) / kTile));
+    const int ty1 = int(floor(fmin(fmax(y1, -lim), lim) / kTile)) + 1;
+    int4 c = make_int4(max(b.x, tx0), max(b.y, ty0), min(b.z, tx1), min(b.w, ty1));
+    if (c.z <= c.x || c.w <= c.y) c = make_int4(b.x, b.y, b.x, b.y);
+    return c;
+}
+
 // Depth sort keys: the 32 bits of the record's centre depth T[2][2] (record slot 8),
 // the low half of the reference's key (rasterize.cu:52-53).
 __global__ void depth_keys_kernel(int64_t R, const float* __restrict__ records, int stride,
@@ -95,14 +135,13 @@ __global__ void depth_keys_kernel(int64_t R, const float* __restrict__ records, 
 
 __global__ void tile_counts_kernel(int64_t R, const float* __restrict__ records, int stride,
                                    const int* __restrict__ radii, const int* __restrict__ order,
-                                   int tw, int th, int64_t* __restrict__ counts) {
+                                   int tw, int th, bool tight, int64_t* __restrict__ counts) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= R) return;
     const int r = order[i];
     const int radius = radii[r];
     if (radius <= 0) { counts[i] = 0; return; }
-    const int4 b = tile_rect(records[int64_t(r) * stride + 9], records[int64_t(r) * stride + 10],
-                             radius, tw, th);
+    const int4 b = bin_rect(records + int64_t(r) * stride, radius, tw, th, tight);
     counts[i] = int64_t(b.z - b.x) * (b.w - b.y);
 }
 
@@ -139,7 +178,7 @@ __global__ void first_owner_kernel(int64_t R, int64_t blocks, const int64_t* __r
 __global__ __launch_bounds__(kBinThreads) void expand_kernel(
     int64_t I, int64_t R, const int64_t* __restrict__ offsets, const int* __restrict__ order,
     const float* __restrict__ records, int stride, const int* __restrict__ radii,
-    const int64_t* __restrict__ image_ids, int64_t per_image, int tw, int th,
+    const int64_t* __restrict__ image_ids, int64_t per_image, int tw, int th, bool tight,
     const int64_t* __restrict__ first_owner, uint32_t* __restrict__ tile_keys,
     int* __restrict__ values) {
     __shared__ int64_t s_end[kExpandSlots];
@@ -167,8 +206,7 @@ __global__ __launch_bounds__(kBinThreads) void expand_kernel(
             const int64_t j = first + t;
             s_end[t] = offsets[j];
             const int r = order[j];
-            const int4 b = tile_rect(records[int64_t(r) * stride + 9],
-                                     records[int64_t(r) * stride + 10], radii[r], tw, th);
+            const int4 b = bin_rect(records + int64_t(r) * stride, radii[r], tw, th, tight);
             s_rect[t] = make_int4(b.x, b.y, max(b.z - b.x, 1), r);
             const int64_t image = image_ids ? image_ids[r] : r / per_image;
             s_base[t] = uint32_t(image * tw * th);
@@ -201,8 +239,7 @@ __global__ __launch_bounds__(kBinThreads) void expand_kernel(
         const int r = order[j];
         const int64_t start = j ? offsets[j - 1] : 0;
         const int64_t local = i - start;
-        const int4 b = tile_rect(records[int64_t(r) * stride + 9], records[int64_t(r) * stride + 10],
-                                 radii[r], tw, th);
+        const int4 b = bin_rect(records + int64_t(r) * stride, radii[r], tw, th, tight);
         const int w = b.z - b.x;
         const int64_t image = image_ids ? image_ids[r] : r / per_image;
         tile_keys[i] = uint32_t(image * tw * th + int64_t(b.y + int(local / w)) * tw + b.x +
@@ -272,11 +309,14 @@ extern "C" int gs_bin_count_workspace(int64_t records, size_t* bytes) {
 
 extern "C" int gs_bin_count(const float* records, int record_stride, const int32_t* radii,
                             const int64_t* image_ids, int64_t R, int64_t records_per_image,
-                            int64_t images, int width, int height, void* workspace1,
+                            int64_t images, int width, int height, int flags, void* workspace1,
                             size_t workspace1_bytes, int64_t* intersections, void* stream) {
     int st = check_common("gs_bin_count", records, record_stride, radii, R, records_per_image,
                           images, width, height);
     if (st) return st;
+    const bool tight = flags & GS_BIN_TIGHT;
+    if (tight && record_stride < 18)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_count: GS_BIN_TIGHT needs opacity in record slot 17");
     if (!intersections) return fail(GS_ERR_ARGUMENT, "gs_bin_count: intersections is NULL");
     *intersections = 0;
     if (R == 0) return GS_OK;
@@ -302,7 +342,7 @@ extern "C" int gs_bin_count(const float* records, int record_stride, const int32
     GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx_in, idx_out,
                                             int(R), 0, 32, s));
     tile_counts_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
-                                                             idx_out, tw, th, counts);
+                                                             idx_out, tw, th, tight, counts);
     GS_CHECK_LAUNCH("tile_counts_kernel");
     temp_bytes = L.temp_bytes;
     GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, counts, offsets, int(R), s));
@@ -328,12 +368,15 @@ extern "C" int gs_bin_sort_workspace(int64_t records, int64_t intersections, int
 
 extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_t* radii,
                            const int64_t* image_ids, int64_t R, int64_t records_per_image,
-                           int64_t images, int width, int height, const void* workspace1,
+                           int64_t images, int width, int height, int flags, const void* workspace1,
                            size_t workspace1_bytes, void* workspace2, size_t workspace2_bytes,
                            int64_t I, int32_t* point_list, int32_t* ranges, void* stream) {
     int st = check_common("gs_bin_sort", records, record_stride, radii, R, records_per_image,
                           images, width, height);
     if (st) return st;
+    const bool tight = flags & GS_BIN_TIGHT;
+    if (tight && record_stride < 18)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_sort: GS_BIN_TIGHT needs opacity in record slot 17");
     if (I < 0 || I > INT_MAX) return fail(GS_ERR_LIMIT, "gs_bin_sort: tile intersection count exceeds int32");
     if (!ranges) return fail(GS_ERR_ARGUMENT, "gs_bin_sort: ranges is NULL");
     const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
@@ -362,7 +405,7 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
     GS_CHECK_LAUNCH("first_owner_kernel");
     expand_kernel<<<unsigned(expand_blocks), kBinThreads, 0, s>>>(
         I, R, offsets, order, records, record_stride, radii, image_ids, records_per_image, tw, th,
-        owners, keys_in, vals_in);
+        tight, owners, keys_in, vals_in);
     GS_CHECK_LAUNCH("expand_kernel");
     size_t temp_bytes = L.temp_bytes;
     GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, point_list,
@@ -441,7 +484,7 @@ extern "C" int gs_bin_static(const float* records, int record_stride, const int3
         return fail(GS_ERR_LIMIT, "gs_bin_static: count workspace exceeds the static scratch");
     int64_t total = 0;
     st = gs_bin_count(records, record_stride, radii, image_ids, records_count, records_per_image,
-                      images, width, height, scratch, bytes1, &total, stream);
+                      images, width, height, 0, scratch, bytes1, &total, stream);
     if (st) return st;
     *intersections = total;
     if (total > kStaticMaxIntersections)
@@ -456,7 +499,7 @@ extern "C" int gs_bin_static(const float* records, int record_stride, const int3
     if (bytes1 + bytes2 > kStaticScratchBytes)
         return fail(GS_ERR_LIMIT, "gs_bin_static: sort workspace exceeds the static scratch");
     return gs_bin_sort(records, record_stride, radii, image_ids, records_count, records_per_image,
-                       images, width, height, scratch, bytes1,
+                       images, width, height, 0, scratch, bytes1,
                        static_cast<char*>(scratch) + bytes1, bytes2, total, point_list, ranges,
                        stream);
 }

@@ -206,6 +206,16 @@ def _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height):
                 row0=row0, pixel0=ch.image0 * height * width)
 
 
+# The public renderers bin tightly: tiles that no sample of a record can reach with
+# alpha >= 1/255 are dropped (identical images, shorter lists).  False restores the
+# reference's square 3-sigma bins.
+TIGHT_BINNING = True
+
+
+def _bin_flags() -> int:
+    return nat.BIN_TIGHT if TIGHT_BINNING else 0
+
+
 # Largest number of tile intersections binned in one pass.  Larger batches are split
 # into image chunks (whole scenes, or camera ranges of one scene), each binned and
 # composited on its own; this bounds the sort workspace (~20 bytes per intersection)
@@ -233,9 +243,9 @@ def _count(records, radii, R, per_image, images, width, height):
     ws1 = torch.empty((max(bytes1.value, 1),), device=device, dtype=torch.uint8)
     total = ctypes.c_int64()
     status = nat.call_status("gs_bin_count", records.address, nat.RECORD_FLOATS, radii.address,
-                             None, R, per_image, images,
-                                  width, height, nat.ptr(ws1), bytes1.value, ctypes.byref(total),
-                                  nat.stream_of(device))
+                             None, R, per_image, images, width, height, _bin_flags(),
+                             nat.ptr(ws1), bytes1.value, ctypes.byref(total),
+                             nat.stream_of(device))
     if status not in (0, GS_ERR_LIMIT) or (status == GS_ERR_LIMIT and total.value <= INT32_MAX):
         nat.check(status, "gs_bin_count")
     return ws1, bytes1.value, total.value
@@ -258,7 +268,8 @@ def _bin_chunk(ch, records, radii, surfels, width, height, counted=None):
     ch.point_list = torch.empty((total,), device=device, dtype=torch.int32)
     ch.ranges = torch.empty((ch.images * tw * th, 2), device=device, dtype=torch.int32)
     nat.call("gs_bin_sort", rec, nat.RECORD_FLOATS, rad, None, ch.record_count, surfels,
-             ch.images, width, height, nat.ptr(ws1), bytes1, nat.ptr(ws2), bytes2.value, total,
+             ch.images, width, height, _bin_flags(), nat.ptr(ws1), bytes1, nat.ptr(ws2),
+             bytes2.value, total,
              nat.ptr(ch.point_list), nat.ptr(ch.ranges), nat.stream_of(device))
     if WORK is not None:
         WORK["records"] = WORK.get("records", 0) + ch.record_count
@@ -326,10 +337,11 @@ def bin_chunks(records, radii, scenes, cameras, surfels, width, height):
 
 
 def bin_records(records, record_stride, radii, image_ids, records_per_image, images, width,
-                height):
+                height, flags=0):
     """Depth-ordered per-tile record lists (rasterize.cu:454-493): point_list, ranges.
 
     One pass (no chunking): used by the reference-layout entry points and the tests.
+    flags=0 gives the reference's bins exactly; nat.BIN_TIGHT drops unreachable tiles.
     """
     device = records.device
     stream = nat.stream_of(device)
@@ -340,7 +352,7 @@ def bin_records(records, record_stride, radii, image_ids, records_per_image, ima
     ws1 = torch.empty((max(bytes1.value, 1),), device=device, dtype=torch.uint8)
     total = ctypes.c_int64()
     nat.call("gs_bin_count", nat.ptr(records), record_stride, nat.ptr(radii), nat.ptr(image_ids),
-             R, records_per_image, images, width, height, nat.ptr(ws1), bytes1.value,
+             R, records_per_image, images, width, height, flags, nat.ptr(ws1), bytes1.value,
              ctypes.byref(total), stream)
     intersections = total.value
     bytes2 = ctypes.c_size_t()
@@ -350,7 +362,7 @@ def bin_records(records, record_stride, radii, image_ids, records_per_image, ima
     point_list = torch.empty((intersections,), device=device, dtype=torch.int32)
     ranges = torch.empty((images * tw * th, 2), device=device, dtype=torch.int32)
     nat.call("gs_bin_sort", nat.ptr(records), record_stride, nat.ptr(radii), nat.ptr(image_ids),
-             R, records_per_image, images, width, height, nat.ptr(ws1), bytes1.value,
+             R, records_per_image, images, width, height, flags, nat.ptr(ws1), bytes1.value,
              nat.ptr(ws2), bytes2.value, intersections, nat.ptr(point_list), nat.ptr(ranges),
              stream)
     return point_list, ranges

@@ -106,17 +106,23 @@ int gs_project_backward(const float* means, const float* quaternions, const floa
  * records: float rows of `record_stride` floats (x, y at 9-10, depth at 8);
  * image_ids: int64 per record, or NULL for image = r / records_per_image.
  * Workspace 1 must stay untouched between the two calls.
+ * flags: 0 for the reference's bins (square 3-sigma tile bounds), or GS_BIN_TIGHT to
+ * also drop the tiles of a record that no sample with alpha >= 1/255 can reach (an
+ * opacity-aware, per-axis ellipse box; images are unchanged, lists are shorter).
+ * GS_BIN_TIGHT needs records with opacity in slot 17 (record_stride >= 18) and must be
+ * passed to both calls.
  */
+#define GS_BIN_TIGHT 1
 int gs_bin_count_workspace(int64_t records, size_t* bytes);
 int gs_bin_count(const float* records, int record_stride, const int32_t* radii,
                  const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
-                 int64_t images, int width, int height, void* workspace1,
+                 int64_t images, int width, int height, int flags, void* workspace1,
                  size_t workspace1_bytes, int64_t* intersections, void* stream);
 int gs_bin_sort_workspace(int64_t records, int64_t intersections, int64_t images,
                           int width, int height, size_t* bytes);
 int gs_bin_sort(const float* records, int record_stride, const int32_t* radii,
                 const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
-                int64_t images, int width, int height, const void* workspace1,
+                int64_t images, int width, int height, int flags, const void* workspace1,
                 size_t workspace1_bytes, void* workspace2, size_t workspace2_bytes,
                 int64_t intersections, int32_t* point_list, int32_t* ranges, void* stream);
 
