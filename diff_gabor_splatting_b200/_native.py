@@ -29,9 +29,10 @@ SIGNATURES = {
     "gs_project_backward": [_p, _p, _p, _p, _p, _p, _p, _i, _l, _l, _l, _p, _p, _p, _p, _p, _p,
                             _p, _p, _p, _p, _p, _p, _p, _p, _p],
     "gs_bin_count_workspace": [_l, ctypes.POINTER(_sz)],
-    "gs_bin_count": [_p, _i, _p, _p, _l, _l, _l, _i, _i, _i, _p, _sz, ctypes.POINTER(_l), _p],
-    "gs_bin_sort_workspace": [_l, _l, _l, _i, _i, ctypes.POINTER(_sz)],
-    "gs_bin_sort": [_p, _i, _p, _p, _l, _l, _l, _i, _i, _i, _p, _sz, _p, _sz, _l, _p, _p, _p],
+    "gs_bin_count": [_p, _i, _p, _p, _l, _l, _l, _i, _i, _i, _p, _sz, ctypes.POINTER(_l),
+                     ctypes.POINTER(_l), _p],
+    "gs_bin_sort_workspace": [_l, _l, _l, _l, _i, _i, ctypes.POINTER(_sz)],
+    "gs_bin_sort": [_p, _i, _p, _p, _l, _l, _l, _i, _i, _i, _p, _sz, _p, _sz, _l, _l, _p, _p, _p],
     "gs_composite_forward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _l, _i, _i, _i, _f, _f,
                              _p, _p, _p, _p, _p],
     "gs_composite_backward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _p, _p, _p, _l, _i, _i,

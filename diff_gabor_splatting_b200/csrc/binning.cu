@@ -8,15 +8,19 @@
 //
 // Here the same order is produced with far less traffic:
 //   1. stable radix sort of the R records by their 32-bit depth bits (R << I);
-//   2. tile counts gathered in that order, inclusive scan, one host read of I
-//      (the reference's one synchronisation, rasterize.cu:466-468);
-//   3. expansion of every (record, tile) slot in depth order, writing a 32-bit
-//      tile id and the record index (8 bytes per slot, coalesced);
-//   4. stable radix sort of the slots by tile id over only ceil(log2(tiles)) bits
+//   2. per record, in that order, its tiles as row spans (one span per tile row it
+//      reaches) and their counts; inclusive scans of slots and spans; one host read
+//      of the totals (the reference's one synchronisation, rasterize.cu:466-468);
+//   3. the spans written out with their first slot and first tile;
+//   4. expansion of every (record, tile) slot in depth order, writing a 32-bit tile
+//      id and the record index (8 bytes per slot, coalesced);
+//   5. stable radix sort of the slots by tile id over only ceil(log2(tiles)) bits
 //      (2 passes for up to 65536 tiles), which keeps the depth order inside each
 //      tile;
-//   5. tile ranges from the sorted tile ids.
-// Result: point_list and ranges identical to the reference's.
+//   6. tile ranges from the sorted tile ids.
+// With the reference's rectangles (flags 0) point_list and ranges are identical to
+// the reference's.  GS_BIN_TIGHT keeps, per tile row, only the tiles a sample with
+// alpha >= 1/255 can reach (see record_region): same images, shorter lists.
 #include <cub/cub.cuh>
 
 #include <mutex>
@@ -31,7 +35,8 @@ constexpr int kBinThreads = 256;
 inline size_t align_up(size_t v) { return (v + 255) & ~size_t(255); }
 
 struct CountLayout {
-    size_t keys_in, keys_out, idx_in, idx_out, counts, offsets, temp, temp_bytes, total;
+    size_t keys_in, keys_out, idx_in, idx_out, slots, slot_end, spans, span_end, temp, temp_bytes,
+        total;
 };
 
 CountLayout count_layout(int64_t R) {
@@ -47,8 +52,10 @@ CountLayout count_layout(int64_t R) {
     L.keys_out = take(sizeof(uint32_t) * R);
     L.idx_in = take(sizeof(int) * R);
     L.idx_out = take(sizeof(int) * R);
-    L.counts = take(sizeof(int64_t) * R);
-    L.offsets = take(sizeof(int64_t) * R);
+    L.slots = take(sizeof(int64_t) * R);
+    L.slot_end = take(sizeof(int64_t) * R);
+    L.spans = take(sizeof(int64_t) * R);
+    L.span_end = take(sizeof(int64_t) * R);
     L.temp_bytes = std::max(sort_bytes, scan_bytes);
     L.temp = take(L.temp_bytes);
     L.total = off;
@@ -56,7 +63,8 @@ CountLayout count_layout(int64_t R) {
 }
 
 struct SortLayout {
-    size_t keys_in, keys_out, vals_in, owners, temp, temp_bytes, total;
+    size_t item_end, item_tile, item_record, owners, keys_in, keys_out, vals_in, temp, temp_bytes,
+        total;
 };
 
 int tile_bits(int64_t n_tiles) {
@@ -65,61 +73,123 @@ int tile_bits(int64_t n_tiles) {
     return bits;
 }
 
-SortLayout sort_layout(int64_t I, int64_t n_tiles) {
+constexpr int kExpandItems = 4;
+constexpr int kExpandSlots = kBinThreads * kExpandItems;
+
+SortLayout sort_layout(int64_t I, int64_t spans, int64_t n_tiles) {
     SortLayout L{};
     size_t sort_bytes = 0;
     cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
                                     (const int*)nullptr, (int*)nullptr, int(I), 0, tile_bits(n_tiles));
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t at = off; off += align_up(bytes); return at; };
+    L.item_end = take(sizeof(int64_t) * spans);
+    L.item_tile = take(sizeof(uint32_t) * spans);
+    L.item_record = take(sizeof(int) * spans);
+    L.owners = take(sizeof(int64_t) * ((I + kExpandSlots - 1) / kExpandSlots + 1));
     L.keys_in = take(sizeof(uint32_t) * I);
     L.keys_out = take(sizeof(uint32_t) * I);
     L.vals_in = take(sizeof(int) * I);
-    L.owners = take(sizeof(int64_t) * ((I + 1023) / 1024 + 1));
     L.temp_bytes = sort_bytes;
     L.temp = take(sort_bytes);
     L.total = off;
     return L;
 }
 
-// Tile rectangle of a record.  Plain: the reference's square bounds (tile_rect).
-// Tight (GS_BIN_TIGHT, records carrying opacity in slot 17): additionally clipped to the
-// tiles that can hold a sample with alpha >= 1/255.  Such a sample has
-// o exp(-min(rho3, rho2)/2) >= 1/255, so min(rho3, rho2) <= thr = 2 ln(255 o): it lies
-// in the image of the local disc u^2 + v^2 <= thr (an ellipse, bounded by the same
-// conic formula the reference uses for its 3-sigma disc, rendering.py:189-196, with 9
-// replaced by thr) or within sqrt(thr/2) pixels of the centre (the rho2 branch).  The
-// level is widened by 5% + 0.05 and the box by 2 pixels so float rounding of the
-// per-pixel test cannot reach outside it; records whose conic is not a bounded ellipse
-// keep the plain rectangle.  Images are unchanged; only tiles no sample of the record
-// can reach are dropped.
-__device__ __forceinline__ int4 bin_rect(const float* g, int radius, int tw, int th, bool tight) {
-    const int4 b = tile_rect(g[9], g[10], radius, tw, th);
-    if (!tight || b.z <= b.x || b.w <= b.y) return b;
+// The tiles of one record, row by row.  rect is the reference's square tile bounds
+// (tile_rect).  Tight regions (GS_BIN_TIGHT; opacity in record slot 17) keep per tile
+// row only the tiles a sample with alpha >= 1/255 can reach.  Such a sample has
+// o exp(-min(rho3, rho2)/2) >= 1/255, so min(rho3, rho2) <= thr = 2 ln(255 o): it lies in
+// the image of the local disc u^2 + v^2 <= thr -- an ellipse, the same conic the
+// reference bounds for its 3-sigma disc (rendering.py:189-196) with 9 replaced by thr
+// -- or within sqrt(thr/2) pixels of the centre (the rho2 branch).  Per row band, the
+// x-range of a convex region is taken where its boundary is extreme: the ellipse's
+// leftmost/rightmost point, or the band edge nearest to it.  The level is widened by
+// 5% + 0.05 and every range by 2 pixels, so float rounding in the per-pixel test
+// cannot reach a dropped tile; records whose conic is not a bounded ellipse keep full
+// rows.  Arithmetic in double.
+struct Region {
+    int4 rect;         // [x0, y0, x1, y1) tiles
+    bool exact;        // per-row spans from the ellipse and disc
+    double m00, m01, m02, m11, m12, m22;   // ellipse interior: (x y 1) M (x y 1)^T <= 0
+    double y_lo, y_hi, y_left, y_right;    // ellipse y-range, y of its leftmost/rightmost points
+    double cx, cy, rd;                     // low-pass disc
+};
+
+__device__ __forceinline__ Region record_region(const float* g, int radius, int tw, int th,
+                                               bool tight) {
+    Region R;
+    R.rect = tile_rect(g[9], g[10], radius, tw, th);
+    R.exact = false;
+    const int4 b = R.rect;
+    if (!tight || b.z <= b.x || b.w <= b.y) return R;
     const double o = g[17];
-    if (!(o * 255.0 >= 1.0 - 1e-6)) return make_int4(b.x, b.y, b.x, b.y);   // never accepted
+    if (!(o * 255.0 >= 1.0 - 1e-6)) {   // alpha <= o < 1/255: never accepted
+        R.rect = make_int4(b.x, b.y, b.x, b.y);
+        return R;
+    }
     const double thr = (2.0 * log(255.0 * o)) * 1.05 + 0.05;
-    const double t6 = g[6], t7 = g[7], t8 = g[8];
-    const double den = thr * (t6 * t6 + t7 * t7) - t8 * t8;
-    if (!(den < 0.0)) return b;
-    const double fa = thr / den, fc = -1.0 / den;
-    const double cx = fa * (g[0] * t6 + g[1] * t7) + fc * g[2] * t8;
-    const double cy = fa * (g[3] * t6 + g[4] * t7) + fc * g[5] * t8;
-    const double ex2 = cx * cx - (fa * (double(g[0]) * g[0] + double(g[1]) * g[1]) + fc * double(g[2]) * g[2]);
-    const double ey2 = cy * cy - (fa * (double(g[3]) * g[3] + double(g[4]) * g[4]) + fc * double(g[5]) * g[5]);
-    if (!(ex2 >= 0.0 && ey2 >= 0.0)) return b;
-    const double ex = sqrt(ex2), ey = sqrt(ey2), rd = sqrt(fmax(thr * 0.5, 0.0));
-    const double x0 = fmin(cx - ex, g[9] - rd) - 2.0, x1 = fmax(cx + ex, g[9] + rd) + 2.0;
-    const double y0 = fmin(cy - ey, g[10] - rd) - 2.0, y1 = fmax(cy + ey, g[10] + rd) + 2.0;
-    if (!(isfinite(x0) && isfinite(x1) && isfinite(y0) && isfinite(y1))) return b;
-    const double lim = 1e9;   // far outside any image; keeps the int conversion defined
-    const int tx0 = int(floor(fmin(fmax(x0, -lim), lim) / kTile));
-    const int tx1 = int(floor(fmin(fmax(x1, -lim), lim) / kTile)) + 1;
-    const int ty0 = int(floor(fmin(fmax(y0, -lim), lim) / kTile));
-    const int ty1 = int(floor(fmin(fmax(y1, -lim), lim) / kTile)) + 1;
-    int4 c = make_int4(max(b.x, tx0), max(b.y, ty0), min(b.z, tx1), min(b.w, ty1));
-    if (c.z <= c.x || c.w <= c.y) c = make_int4(b.x, b.y, b.x, b.y);
-    return c;
+    double T[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) T[k] = g[k];
+    // dual conic C = T diag(thr, thr, -1) T^T
+    auto dual = [&](int i, int j) {
+        return thr * (T[3 * i] * T[3 * j] + T[3 * i + 1] * T[3 * j + 1]) - T[3 * i + 2] * T[3 * j + 2];
+    };
+    const double c00 = dual(0, 0), c01 = dual(0, 1), c02 = dual(0, 2), c11 = dual(1, 1),
+                 c12 = dual(1, 2), c22 = dual(2, 2);
+    if (!(c22 < 0.0)) return R;   // not a bounded ellipse in front of the camera
+    const double cx = c02 / c22, cy = c12 / c22;
+    const double ex2 = cx * cx - c00 / c22, ey2 = cy * cy - c11 / c22;
+    if (!(ex2 > 0.0 && ey2 > 0.0)) return R;
+    const double ex = sqrt(ex2), ey = sqrt(ey2);
+    // primal conic: adjugate of the dual, signed so the interior is negative
+    double m00 = c11 * c22 - c12 * c12, m01 = c02 * c12 - c01 * c22, m02 = c01 * c12 - c02 * c11;
+    double m11 = c00 * c22 - c02 * c02, m12 = c01 * c02 - c00 * c12, m22 = c00 * c11 - c01 * c01;
+    const double centre = m00 * cx * cx + 2 * m01 * cx * cy + 2 * m02 * cx + m11 * cy * cy +
+                          2 * m12 * cy + m22;
+    if (centre > 0) { m00 = -m00; m01 = -m01; m02 = -m02; m11 = -m11; m12 = -m12; m22 = -m22; }
+    if (!(m00 > 0.0) || !isfinite(m00 + m01 + m02 + m11 + m12 + m22)) return R;
+    // tangent points of the vertical tangents x = cx -/+ ex: P = C (1, 0, -x)
+    const double xl = cx - ex, xr = cx + ex;
+    const double y_left = (c01 - xl * c12) / (c02 - xl * c22);
+    const double y_right = (c01 - xr * c12) / (c02 - xr * c22);
+    if (!isfinite(y_left) || !isfinite(y_right) || !isfinite(cx) || !isfinite(cy)) return R;
+    R.m00 = m00; R.m01 = m01; R.m02 = m02; R.m11 = m11; R.m12 = m12; R.m22 = m22;
+    R.y_lo = cy - ey; R.y_hi = cy + ey; R.y_left = y_left; R.y_right = y_right;
+    R.cx = g[9]; R.cy = g[10]; R.rd = sqrt(fmax(thr * 0.5, 0.0));
+    R.exact = true;
+    return R;
+}
+
+// Tiles [x0, x1) of tile row ty (x1 <= x0: none).
+__device__ __forceinline__ int2 row_span(const Region& R, int ty) {
+    if (!R.exact) return make_int2(R.rect.x, R.rect.z);
+    const double y0 = double(ty) * kTile - 2.0, y1 = double(ty) * kTile + (kTile - 1) + 2.0;
+    double lo = 1e300, hi = -1e300;
+    const double ya = fmax(y0, R.y_lo), yb = fmin(y1, R.y_hi);
+    if (ya <= yb) {
+        // x roots of m00 x^2 + 2 (m01 y + m02) x + (m11 y^2 + 2 m12 y + m22) = 0
+        auto root = [&](double y, double side) {
+            const double b = R.m01 * y + R.m02;
+            const double c = (R.m11 * y + 2.0 * R.m12) * y + R.m22;
+            const double d = fmax(b * b - R.m00 * c, 0.0);
+            return (-b + side * sqrt(d)) / R.m00;
+        };
+        lo = root(fmin(fmax(R.y_left, ya), yb), -1.0);
+        hi = root(fmin(fmax(R.y_right, ya), yb), 1.0);
+    }
+    const double dy = fmax(fmax(y0 - R.cy, R.cy - y1), 0.0);
+    if (dy <= R.rd) {
+        const double hw = sqrt(R.rd * R.rd - dy * dy);
+        lo = fmin(lo, R.cx - hw);
+        hi = fmax(hi, R.cx + hw);
+    }
+    if (!(lo <= hi)) return make_int2(R.rect.x, R.rect.x);
+    const double lim = 1e9;
+    const int x0 = int(floor(fmin(fmax(lo - 2.0, -lim), lim) / kTile));
+    const int x1 = int(floor(fmin(fmax(hi + 2.0, -lim), lim) / kTile)) + 1;
+    return make_int2(max(R.rect.x, x0), min(R.rect.z, x1));
 }
 
 // Depth sort keys: the 32 bits of the record's centre depth T[2][2] (record slot 8),
@@ -133,25 +203,63 @@ __global__ void depth_keys_kernel(int64_t R, const float* __restrict__ records, 
     idx[r] = int(r);
 }
 
+// Per record (depth order): tiles (slots) and non-empty tile rows (spans).
 __global__ void tile_counts_kernel(int64_t R, const float* __restrict__ records, int stride,
                                    const int* __restrict__ radii, const int* __restrict__ order,
-                                   int tw, int th, bool tight, int64_t* __restrict__ counts) {
+                                   int tw, int th, bool tight, int64_t* __restrict__ slots,
+                                   int64_t* __restrict__ spans) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= R) return;
     const int r = order[i];
     const int radius = radii[r];
-    if (radius <= 0) { counts[i] = 0; return; }
-    const int4 b = bin_rect(records + int64_t(r) * stride, radius, tw, th, tight);
-    counts[i] = int64_t(b.z - b.x) * (b.w - b.y);
+    int64_t n_slots = 0, n_spans = 0;
+    if (radius > 0) {
+        const Region G = record_region(records + int64_t(r) * stride, radius, tw, th, tight);
+        if (G.rect.z > G.rect.x) {
+            if (!G.exact) {
+                n_spans = G.rect.w - G.rect.y;
+                n_slots = n_spans * (G.rect.z - G.rect.x);
+            } else {
+                for (int ty = G.rect.y; ty < G.rect.w; ++ty) {
+                    const int2 sp = row_span(G, ty);
+                    if (sp.y > sp.x) { n_slots += sp.y - sp.x; ++n_spans; }
+                }
+            }
+        }
+    }
+    slots[i] = n_slots;
+    spans[i] = n_spans;
 }
 
-// Expansion of (record, tile) slots in depth order.  A block owns 1024 consecutive
-// slots: two threads find the first and last owning record (binary search of the
-// inclusive offsets in global memory), the block stages those records' offsets and
-// tile rectangles in shared memory, and each slot finds its owner there (10 shared
-// steps instead of ~21 dependent global loads per slot).  Writes are coalesced.
-constexpr int kExpandItems = 4;
-constexpr int kExpandSlots = kBinThreads * kExpandItems;
+// Write each record's spans (depth order) with their end slot (inclusive scan value),
+// first tile id and record.
+__global__ void spans_kernel(int64_t R, const float* __restrict__ records, int stride,
+                             const int* __restrict__ radii, const int* __restrict__ order,
+                             const int64_t* __restrict__ slot_end,
+                             const int64_t* __restrict__ span_end,
+                             const int64_t* __restrict__ image_ids, int64_t per_image, int tw,
+                             int th, bool tight, int64_t* __restrict__ item_end,
+                             uint32_t* __restrict__ item_tile, int* __restrict__ item_record) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= R) return;
+    const int64_t first_span = i ? span_end[i - 1] : 0;
+    if (span_end[i] == first_span) return;
+    const int r = order[i];
+    int64_t slot = i ? slot_end[i - 1] : 0;
+    int64_t k = first_span;
+    const Region G = record_region(records + int64_t(r) * stride, radii[r], tw, th, tight);
+    const int64_t image = image_ids ? image_ids[r] : r / per_image;
+    const uint32_t base = uint32_t(image * tw * th);
+    for (int ty = G.rect.y; ty < G.rect.w; ++ty) {
+        const int2 sp = row_span(G, ty);
+        if (sp.y <= sp.x) continue;
+        slot += sp.y - sp.x;
+        item_end[k] = slot;
+        item_tile[k] = base + uint32_t(ty * tw + sp.x);
+        item_record[k] = r;
+        ++k;
+    }
+}
 
 __device__ __forceinline__ int64_t first_above(const int64_t* __restrict__ offsets, int64_t n,
                                                int64_t value) {
@@ -163,88 +271,64 @@ __device__ __forceinline__ int64_t first_above(const int64_t* __restrict__ offse
     return lo;
 }
 
-// first_owner[b] = the record (in depth order) owning slot b * kExpandSlots: each
-// record writes the entries of the blocks whose first slot falls in its slot range.
-__global__ void first_owner_kernel(int64_t R, int64_t blocks, const int64_t* __restrict__ offsets,
+// first_owner[b] = the span owning slot b * kExpandSlots: each span writes the entries
+// of the blocks whose first slot falls in its slot range.
+__global__ void first_owner_kernel(int64_t S, int64_t blocks, const int64_t* __restrict__ item_end,
                                    int64_t* __restrict__ first_owner) {
     const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (j >= R) return;
-    const int64_t begin = j ? offsets[j - 1] : 0, end = offsets[j];
+    if (j >= S) return;
+    const int64_t begin = j ? item_end[j - 1] : 0, end = item_end[j];
     for (int64_t b = (begin + kExpandSlots - 1) / kExpandSlots; b * kExpandSlots < end && b < blocks;
          ++b)
         first_owner[b] = j;
 }
 
+// Expansion of (record, tile) slots in depth order.  A block owns 1024 consecutive
+// slots and the spans covering them (at most 1024: every span holds a slot); it stages
+// their end slots, first tiles and records in shared memory, and each slot finds its
+// span by a shared binary search.  Writes are coalesced.
 __global__ __launch_bounds__(kBinThreads) void expand_kernel(
-    int64_t I, int64_t R, const int64_t* __restrict__ offsets, const int* __restrict__ order,
-    const float* __restrict__ records, int stride, const int* __restrict__ radii,
-    const int64_t* __restrict__ image_ids, int64_t per_image, int tw, int th, bool tight,
+    int64_t I, int64_t S, const int64_t* __restrict__ item_end,
+    const uint32_t* __restrict__ item_tile, const int* __restrict__ item_record,
     const int64_t* __restrict__ first_owner, uint32_t* __restrict__ tile_keys,
     int* __restrict__ values) {
     __shared__ int64_t s_end[kExpandSlots];
-    __shared__ int4 s_rect[kExpandSlots];    // x0, y0, width, record
-    __shared__ uint32_t s_base[kExpandSlots];   // image * tw * th
+    __shared__ uint32_t s_tile[kExpandSlots];
+    __shared__ int s_record[kExpandSlots];
     __shared__ int64_t s_first, s_last;
     const int64_t i0 = int64_t(blockIdx.x) * kExpandSlots;
     const int64_t i1 = min(i0 + kExpandSlots, I) - 1;
     if (threadIdx.x == 0) s_first = first_owner[blockIdx.x];
     if (threadIdx.x == 32) {
-        // an upper bound on the owner of the block's last slot, from the next block's
-        // first owner (extra empty records in the range are harmless to the search)
-        if (i1 + 1 < I) {
+        if (i1 + 1 < I) {   // owner of the last slot, from the next block's first owner
             const int64_t next = first_owner[blockIdx.x + 1];
-            s_last = next > 0 && offsets[next - 1] > i1 ? next - 1 : next;
+            s_last = next > 0 && item_end[next - 1] > i1 ? next - 1 : next;
         } else {
-            s_last = first_above(offsets, R, i1);
+            s_last = S - 1;
         }
     }
     __syncthreads();
     const int64_t first = s_first;
-    const int64_t owners = s_last - first + 1;
-    if (owners <= kExpandSlots) {
-        for (int t = threadIdx.x; t < owners; t += blockDim.x) {
-            const int64_t j = first + t;
-            s_end[t] = offsets[j];
-            const int r = order[j];
-            const int4 b = bin_rect(records + int64_t(r) * stride, radii[r], tw, th, tight);
-            s_rect[t] = make_int4(b.x, b.y, max(b.z - b.x, 1), r);
-            const int64_t image = image_ids ? image_ids[r] : r / per_image;
-            s_base[t] = uint32_t(image * tw * th);
-        }
-        __syncthreads();
-#pragma unroll
-        for (int k = 0; k < kExpandItems; ++k) {
-            const int64_t i = i0 + k * kBinThreads + threadIdx.x;
-            if (i > i1) break;
-            int lo = 0, hi = int(owners) - 1;
-            while (lo < hi) {
-                const int mid = (lo + hi) >> 1;
-                if (s_end[mid] > i) hi = mid; else lo = mid + 1;
-            }
-            const int64_t start = lo ? s_end[lo - 1] : (first ? offsets[first - 1] : 0);
-            const int local = int(i - start);
-            const int4 b = s_rect[lo];
-            tile_keys[i] = s_base[lo] + uint32_t((b.y + local / b.z) * tw + b.x + local % b.z);
-            values[i] = b.w;
-        }
-        return;
+    const int owners = int(s_last - first + 1);
+    for (int t = threadIdx.x; t < owners; t += blockDim.x) {
+        s_end[t] = item_end[first + t];
+        s_tile[t] = item_tile[first + t];
+        s_record[t] = item_record[first + t];
     }
-    // many empty owners in range (only possible with caller-made records whose
-    // radius is positive but whose tile rectangle is empty): per-slot global search
-#pragma unroll 1
+    const int64_t first_start = first ? item_end[first - 1] : 0;
+    __syncthreads();
+#pragma unroll
     for (int k = 0; k < kExpandItems; ++k) {
         const int64_t i = i0 + k * kBinThreads + threadIdx.x;
         if (i > i1) break;
-        const int64_t j = first_above(offsets, R, i);
-        const int r = order[j];
-        const int64_t start = j ? offsets[j - 1] : 0;
-        const int64_t local = i - start;
-        const int4 b = bin_rect(records + int64_t(r) * stride, radii[r], tw, th, tight);
-        const int w = b.z - b.x;
-        const int64_t image = image_ids ? image_ids[r] : r / per_image;
-        tile_keys[i] = uint32_t(image * tw * th + int64_t(b.y + int(local / w)) * tw + b.x +
-                                int(local % w));
-        values[i] = r;
+        int lo = 0, hi = owners - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (s_end[mid] > i) hi = mid; else lo = mid + 1;
+        }
+        const int64_t start = lo ? s_end[lo - 1] : first_start;
+        tile_keys[i] = s_tile[lo] + uint32_t(i - start);
+        values[i] = s_record[lo];
     }
 }
 
@@ -310,15 +394,17 @@ extern "C" int gs_bin_count_workspace(int64_t records, size_t* bytes) {
 extern "C" int gs_bin_count(const float* records, int record_stride, const int32_t* radii,
                             const int64_t* image_ids, int64_t R, int64_t records_per_image,
                             int64_t images, int width, int height, int flags, void* workspace1,
-                            size_t workspace1_bytes, int64_t* intersections, void* stream) {
+                            size_t workspace1_bytes, int64_t* intersections, int64_t* spans,
+                            void* stream) {
     int st = check_common("gs_bin_count", records, record_stride, radii, R, records_per_image,
                           images, width, height);
     if (st) return st;
     const bool tight = flags & GS_BIN_TIGHT;
     if (tight && record_stride < 18)
         return fail(GS_ERR_ARGUMENT, "gs_bin_count: GS_BIN_TIGHT needs opacity in record slot 17");
-    if (!intersections) return fail(GS_ERR_ARGUMENT, "gs_bin_count: intersections is NULL");
+    if (!intersections || !spans) return fail(GS_ERR_ARGUMENT, "gs_bin_count: NULL output");
     *intersections = 0;
+    *spans = 0;
     if (R == 0) return GS_OK;
     if (!image_ids && records_per_image < 1)
         return fail(GS_ERR_ARGUMENT, "gs_bin_count: records_per_image must be positive without image_ids");
@@ -330,8 +416,10 @@ extern "C" int gs_bin_count(const float* records, int record_stride, const int32
     auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
     auto* idx_in = reinterpret_cast<int*>(base + L.idx_in);
     auto* idx_out = reinterpret_cast<int*>(base + L.idx_out);
-    auto* counts = reinterpret_cast<int64_t*>(base + L.counts);
-    auto* offsets = reinterpret_cast<int64_t*>(base + L.offsets);
+    auto* slots = reinterpret_cast<int64_t*>(base + L.slots);
+    auto* slot_end = reinterpret_cast<int64_t*>(base + L.slot_end);
+    auto* n_spans = reinterpret_cast<int64_t*>(base + L.spans);
+    auto* span_end = reinterpret_cast<int64_t*>(base + L.span_end);
     void* temp = base + L.temp;
     auto s = as_stream(stream);
     const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
@@ -342,27 +430,32 @@ extern "C" int gs_bin_count(const float* records, int record_stride, const int32
     GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx_in, idx_out,
                                             int(R), 0, 32, s));
     tile_counts_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
-                                                             idx_out, tw, th, tight, counts);
+                                                             idx_out, tw, th, tight, slots, n_spans);
     GS_CHECK_LAUNCH("tile_counts_kernel");
     temp_bytes = L.temp_bytes;
-    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, counts, offsets, int(R), s));
-    int64_t total = 0;
-    GS_CUDA(cudaMemcpyAsync(&total, offsets + R - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, slots, slot_end, int(R), s));
+    temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, n_spans, span_end, int(R), s));
+    int64_t totals[2] = {0, 0};
+    GS_CUDA(cudaMemcpyAsync(&totals[0], slot_end + R - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
+    GS_CUDA(cudaMemcpyAsync(&totals[1], span_end + R - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     GS_CUDA(cudaStreamSynchronize(s));
-    *intersections = total;
-    if (total > INT_MAX)
+    *intersections = totals[0];
+    *spans = totals[1];
+    if (totals[0] > INT_MAX)
         return fail(GS_ERR_LIMIT, "gs_bin_count: tile intersection count exceeds int32");
     return GS_OK;
 }
 
-extern "C" int gs_bin_sort_workspace(int64_t records, int64_t intersections, int64_t images,
-                                     int width, int height, size_t* bytes) {
-    if (!bytes || records < 0 || intersections < 0 || images < 1 || width < 1 || height < 1)
+extern "C" int gs_bin_sort_workspace(int64_t records, int64_t intersections, int64_t spans,
+                                     int64_t images, int width, int height, size_t* bytes) {
+    if (!bytes || records < 0 || intersections < 0 || spans < 0 || spans > intersections ||
+        images < 1 || width < 1 || height < 1)
         return fail(GS_ERR_ARGUMENT, "gs_bin_sort_workspace: invalid arguments");
     if (intersections > INT_MAX)
         return fail(GS_ERR_LIMIT, "gs_bin_sort_workspace: tile intersection count exceeds int32");
     const int64_t tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
-    *bytes = intersections ? sort_layout(intersections, images * tw * th).total : 0;
+    *bytes = intersections ? sort_layout(intersections, spans, images * tw * th).total : 0;
     return GS_OK;
 }
 
@@ -370,7 +463,8 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
                            const int64_t* image_ids, int64_t R, int64_t records_per_image,
                            int64_t images, int width, int height, int flags, const void* workspace1,
                            size_t workspace1_bytes, void* workspace2, size_t workspace2_bytes,
-                           int64_t I, int32_t* point_list, int32_t* ranges, void* stream) {
+                           int64_t I, int64_t spans, int32_t* point_list, int32_t* ranges,
+                           void* stream) {
     int st = check_common("gs_bin_sort", records, record_stride, radii, R, records_per_image,
                           images, width, height);
     if (st) return st;
@@ -378,6 +472,8 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
     if (tight && record_stride < 18)
         return fail(GS_ERR_ARGUMENT, "gs_bin_sort: GS_BIN_TIGHT needs opacity in record slot 17");
     if (I < 0 || I > INT_MAX) return fail(GS_ERR_LIMIT, "gs_bin_sort: tile intersection count exceeds int32");
+    if (spans < 0 || spans > I || (I > 0 && spans == 0))
+        return fail(GS_ERR_ARGUMENT, "gs_bin_sort: span count inconsistent with the intersections");
     if (!ranges) return fail(GS_ERR_ARGUMENT, "gs_bin_sort: ranges is NULL");
     const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
     const int64_t n_tiles = images * tw * th;
@@ -388,24 +484,34 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
     const CountLayout C = count_layout(R);
     if (!workspace1 || workspace1_bytes < C.total)
         return fail(GS_ERR_WORKSPACE, "gs_bin_sort: workspace 1 too small");
-    const SortLayout L = sort_layout(I, n_tiles);
+    const SortLayout L = sort_layout(I, spans, n_tiles);
     if (!workspace2 || workspace2_bytes < L.total)
         return fail(GS_ERR_WORKSPACE, "gs_bin_sort: workspace 2 too small");
     const auto* base1 = static_cast<const char*>(workspace1);
     const auto* order = reinterpret_cast<const int*>(base1 + C.idx_out);
-    const auto* offsets = reinterpret_cast<const int64_t*>(base1 + C.offsets);
+    const auto* slot_end = reinterpret_cast<const int64_t*>(base1 + C.slot_end);
+    const auto* span_end = reinterpret_cast<const int64_t*>(base1 + C.span_end);
     auto* base = static_cast<char*>(workspace2);
+    auto* item_end = reinterpret_cast<int64_t*>(base + L.item_end);
+    auto* item_tile = reinterpret_cast<uint32_t*>(base + L.item_tile);
+    auto* item_record = reinterpret_cast<int*>(base + L.item_record);
+    auto* owners = reinterpret_cast<int64_t*>(base + L.owners);
     auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
     auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
     auto* vals_in = reinterpret_cast<int*>(base + L.vals_in);
-    auto* owners = reinterpret_cast<int64_t*>(base + L.owners);
     void* temp = base + L.temp;
+    spans_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii, order,
+                                                       slot_end, span_end, image_ids,
+                                                       records_per_image, tw, th, tight, item_end,
+                                                       item_tile, item_record);
+    GS_CHECK_LAUNCH("spans_kernel");
     const int64_t expand_blocks = (I + kExpandSlots - 1) / kExpandSlots;
-    first_owner_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, expand_blocks, offsets, owners);
+    first_owner_kernel<<<blocks_for(spans), kBinThreads, 0, s>>>(spans, expand_blocks, item_end,
+                                                                 owners);
     GS_CHECK_LAUNCH("first_owner_kernel");
-    expand_kernel<<<unsigned(expand_blocks), kBinThreads, 0, s>>>(
-        I, R, offsets, order, records, record_stride, radii, image_ids, records_per_image, tw, th,
-        tight, owners, keys_in, vals_in);
+    expand_kernel<<<unsigned(expand_blocks), kBinThreads, 0, s>>>(I, spans, item_end, item_tile,
+                                                                  item_record, owners, keys_in,
+                                                                  vals_in);
     GS_CHECK_LAUNCH("expand_kernel");
     size_t temp_bytes = L.temp_bytes;
     GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, point_list,
@@ -482,9 +588,9 @@ extern "C" int gs_bin_static(const float* records, int record_stride, const int3
     bytes1 = align_up(bytes1);
     if (bytes1 > kStaticScratchBytes)
         return fail(GS_ERR_LIMIT, "gs_bin_static: count workspace exceeds the static scratch");
-    int64_t total = 0;
+    int64_t total = 0, spans = 0;
     st = gs_bin_count(records, record_stride, radii, image_ids, records_count, records_per_image,
-                      images, width, height, 0, scratch, bytes1, &total, stream);
+                      images, width, height, 0, scratch, bytes1, &total, &spans, stream);
     if (st) return st;
     *intersections = total;
     if (total > kStaticMaxIntersections)
@@ -494,12 +600,12 @@ extern "C" int gs_bin_static(const float* records, int record_stride, const int3
         return fail(GS_ERR_ARGUMENT, "gs_bin_static: point_list capacity is below the "
                                      "intersection count returned in *intersections");
     size_t bytes2 = 0;
-    st = gs_bin_sort_workspace(records_count, total, images, width, height, &bytes2);
+    st = gs_bin_sort_workspace(records_count, total, spans, images, width, height, &bytes2);
     if (st) return st;
     if (bytes1 + bytes2 > kStaticScratchBytes)
         return fail(GS_ERR_LIMIT, "gs_bin_static: sort workspace exceeds the static scratch");
     return gs_bin_sort(records, record_stride, radii, image_ids, records_count, records_per_image,
                        images, width, height, 0, scratch, bytes1,
-                       static_cast<char*>(scratch) + bytes1, bytes2, total, point_list, ranges,
-                       stream);
+                       static_cast<char*>(scratch) + bytes1, bytes2, total, spans, point_list,
+                       ranges, stream);
 }

@@ -241,14 +241,14 @@ def _count(records, radii, R, per_image, images, width, height):
     bytes1 = ctypes.c_size_t()
     nat.call("gs_bin_count_workspace", R, ctypes.byref(bytes1))
     ws1 = torch.empty((max(bytes1.value, 1),), device=device, dtype=torch.uint8)
-    total = ctypes.c_int64()
+    total, spans = ctypes.c_int64(), ctypes.c_int64()
     status = nat.call_status("gs_bin_count", records.address, nat.RECORD_FLOATS, radii.address,
                              None, R, per_image, images, width, height, _bin_flags(),
-                             nat.ptr(ws1), bytes1.value, ctypes.byref(total),
+                             nat.ptr(ws1), bytes1.value, ctypes.byref(total), ctypes.byref(spans),
                              nat.stream_of(device))
     if status not in (0, GS_ERR_LIMIT) or (status == GS_ERR_LIMIT and total.value <= INT32_MAX):
         nat.check(status, "gs_bin_count")
-    return ws1, bytes1.value, total.value
+    return ws1, bytes1.value, total.value, spans.value
 
 
 def _bin_chunk(ch, records, radii, surfels, width, height, counted=None):
@@ -259,17 +259,17 @@ def _bin_chunk(ch, records, radii, surfels, width, height, counted=None):
     if counted is None:
         counted = _count(_Ptr(rec, device), _Ptr(rad, device), ch.record_count, surfels,
                          ch.images, width, height)
-    ws1, bytes1, total = counted
+    ws1, bytes1, total, spans = counted
     tw, th = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
     bytes2 = ctypes.c_size_t()
-    nat.call("gs_bin_sort_workspace", ch.record_count, total, ch.images, width, height,
+    nat.call("gs_bin_sort_workspace", ch.record_count, total, spans, ch.images, width, height,
              ctypes.byref(bytes2))
     ws2 = torch.empty((max(bytes2.value, 1),), device=device, dtype=torch.uint8)
     ch.point_list = torch.empty((total,), device=device, dtype=torch.int32)
     ch.ranges = torch.empty((ch.images * tw * th, 2), device=device, dtype=torch.int32)
     nat.call("gs_bin_sort", rec, nat.RECORD_FLOATS, rad, None, ch.record_count, surfels,
              ch.images, width, height, _bin_flags(), nat.ptr(ws1), bytes1, nat.ptr(ws2),
-             bytes2.value, total,
+             bytes2.value, total, spans,
              nat.ptr(ch.point_list), nat.ptr(ch.ranges), nat.stream_of(device))
     if WORK is not None:
         WORK["records"] = WORK.get("records", 0) + ch.record_count
@@ -350,21 +350,21 @@ def bin_records(records, record_stride, radii, image_ids, records_per_image, ima
     bytes1 = ctypes.c_size_t()
     nat.call("gs_bin_count_workspace", R, ctypes.byref(bytes1))
     ws1 = torch.empty((max(bytes1.value, 1),), device=device, dtype=torch.uint8)
-    total = ctypes.c_int64()
+    total, spans = ctypes.c_int64(), ctypes.c_int64()
     nat.call("gs_bin_count", nat.ptr(records), record_stride, nat.ptr(radii), nat.ptr(image_ids),
              R, records_per_image, images, width, height, flags, nat.ptr(ws1), bytes1.value,
-             ctypes.byref(total), stream)
+             ctypes.byref(total), ctypes.byref(spans), stream)
     intersections = total.value
     bytes2 = ctypes.c_size_t()
-    nat.call("gs_bin_sort_workspace", R, intersections, images, width, height,
+    nat.call("gs_bin_sort_workspace", R, intersections, spans.value, images, width, height,
              ctypes.byref(bytes2))
     ws2 = torch.empty((max(bytes2.value, 1),), device=device, dtype=torch.uint8)
     point_list = torch.empty((intersections,), device=device, dtype=torch.int32)
     ranges = torch.empty((images * tw * th, 2), device=device, dtype=torch.int32)
     nat.call("gs_bin_sort", nat.ptr(records), record_stride, nat.ptr(radii), nat.ptr(image_ids),
              R, records_per_image, images, width, height, flags, nat.ptr(ws1), bytes1.value,
-             nat.ptr(ws2), bytes2.value, intersections, nat.ptr(point_list), nat.ptr(ranges),
-             stream)
+             nat.ptr(ws2), bytes2.value, intersections, spans.value, nat.ptr(point_list),
+             nat.ptr(ranges), stream)
     return point_list, ranges
 
 

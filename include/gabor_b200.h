@@ -97,34 +97,36 @@ int gs_project_backward(const float* means, const float* quaternions, const floa
 /* ---------------------------------------------------------------------------
  * Tile binning (rasterize.cu:23-69, 454-493).  Two phases around the one host
  * synchronisation the reference also has (rasterize.cu:466-468):
- *   gs_bin_count : depth-sort the records, count tiles, scan; returns the
- *                  intersection count I to the host (waits on the stream).
- *   gs_bin_sort  : expand (tile, record) pairs in depth order, stable-sort by
- *                  tile, write point_list[I] (record indices) and ranges.
- * The result is identical to the reference's stable 64-bit (tile << 32 | depth
- * bits) sort: within a tile, records are ordered by depth bits, then index.
+ *   gs_bin_count : depth-sort the records, count each record's tiles as row spans
+ *                  (one span per tile row it reaches), scan; returns the intersection
+ *                  count I and the span count to the host (waits on the stream).
+ *   gs_bin_sort  : write the spans, expand (tile, record) slots in depth order,
+ *                  stable-sort by tile, write point_list[I] (record indices) and ranges.
+ * With flags 0 the result is identical to the reference's stable 64-bit
+ * (tile << 32 | depth bits) sort of its square 3-sigma tile bounds: within a tile,
+ * records are ordered by depth bits, then index.  GS_BIN_TIGHT keeps, per tile row,
+ * only the tiles a sample with alpha >= 1/255 can reach (the projected ellipse of the
+ * opacity's alpha level and the low-pass disc, widened for rounding): images are
+ * unchanged, lists shorter.  It needs opacity in record slot 17 (record_stride >= 18)
+ * and must be given to both calls.
  * records: float rows of `record_stride` floats (x, y at 9-10, depth at 8);
  * image_ids: int64 per record, or NULL for image = r / records_per_image.
  * Workspace 1 must stay untouched between the two calls.
- * flags: 0 for the reference's bins (square 3-sigma tile bounds), or GS_BIN_TIGHT to
- * also drop the tiles of a record that no sample with alpha >= 1/255 can reach (an
- * opacity-aware, per-axis ellipse box; images are unchanged, lists are shorter).
- * GS_BIN_TIGHT needs records with opacity in slot 17 (record_stride >= 18) and must be
- * passed to both calls.
  */
 #define GS_BIN_TIGHT 1
 int gs_bin_count_workspace(int64_t records, size_t* bytes);
 int gs_bin_count(const float* records, int record_stride, const int32_t* radii,
                  const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
                  int64_t images, int width, int height, int flags, void* workspace1,
-                 size_t workspace1_bytes, int64_t* intersections, void* stream);
-int gs_bin_sort_workspace(int64_t records, int64_t intersections, int64_t images,
+                 size_t workspace1_bytes, int64_t* intersections, int64_t* spans, void* stream);
+int gs_bin_sort_workspace(int64_t records, int64_t intersections, int64_t spans, int64_t images,
                           int width, int height, size_t* bytes);
 int gs_bin_sort(const float* records, int record_stride, const int32_t* radii,
                 const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
                 int64_t images, int width, int height, int flags, const void* workspace1,
                 size_t workspace1_bytes, void* workspace2, size_t workspace2_bytes,
-                int64_t intersections, int32_t* point_list, int32_t* ranges, void* stream);
+                int64_t intersections, int64_t spans, int32_t* point_list, int32_t* ranges,
+                void* stream);
 
 /* No-allocation binning: gs_bin_count followed by gs_bin_sort with both workspaces
  * taken from a 32 MiB array compiled into the library (one per GPU, held until

@@ -59,7 +59,8 @@ def test_invalid_arguments_fail_before_any_gpu_work():
                                      None, None, None, None, None) == 1
     assert b"row mode" in lib.gs_last_error()
     # tiles beyond int32
-    assert lib.gs_bin_sort_workspace(10, 10**10, 1, 8, 8, ctypes.byref(size)) == 2
+    assert lib.gs_bin_sort_workspace(10, 10**10, 10, 1, 8, 8, ctypes.byref(size)) == 2
+    assert lib.gs_bin_sort_workspace(10, 5, 6, 1, 8, 8, ctypes.byref(size)) == 1   # spans > slots
 
 
 def test_check_values_messages_match_reference():
