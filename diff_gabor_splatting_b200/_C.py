@@ -25,7 +25,7 @@ from __future__ import annotations
 import torch
 
 from . import _native as nat
-from .rendering import SHColors, _check_sh, bin_records
+from .rendering import SHColors, _check_sh, _composite_flags, bin_records
 
 TILE = 16
 
@@ -99,7 +99,8 @@ def rasterize_forward(geometry, appearance, opacities, primitive_ids, image_ids,
         nat.call("gs_composite_forward", nat.ptr(records), nat.ptr(rows), nat.ROWS_EXPLICIT,
                  nat.ptr(primitive_ids), 1, 1, records.shape[0], rows.shape[0],
                  nat.ptr(backgrounds), nat.ptr(point_list), nat.ptr(ranges), images, width,
-                 height, int(neural), float(near_plane), float(far_plane), nat.ptr(maps),
+                 height, int(neural), _composite_flags(), float(near_plane), float(far_plane),
+                 nat.ptr(maps),
                  nat.ptr(state), nat.ptr(contributors), None, nat.stream_of(device))
     return [maps, point_list, ranges, state, contributors]
 

@@ -33,8 +33,8 @@ SIGNATURES = {
                      ctypes.POINTER(_l), _p],
     "gs_bin_sort_workspace": [_l, _l, _l, _l, _i, _i, ctypes.POINTER(_sz)],
     "gs_bin_sort": [_p, _i, _p, _p, _l, _l, _l, _i, _i, _i, _p, _sz, _p, _sz, _l, _l, _p, _p, _p],
-    "gs_composite_forward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _l, _i, _i, _i, _f, _f,
-                             _p, _p, _p, _p, _p],
+    "gs_composite_forward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _l, _i, _i, _i, _i, _f,
+                             _f, _p, _p, _p, _p, _p],
     "gs_composite_backward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _p, _p, _p, _l, _i, _i,
                               _i, _f, _f, _p, _p, _p, _p, _p, _p],
     "gs_pack_geometry": [_p, _p, _p, _l, _l, _p, _p],
@@ -47,6 +47,7 @@ SIGNATURES = {
 
 ROWS_PER_RECORD, ROWS_PER_SURFEL, ROWS_EXPLICIT = 0, 1, 2
 BIN_TIGHT = 1
+COMPOSITE_EXACT = 1
 RECORD_FLOATS, CLASSIC_ROW_FLOATS, NEURAL_ROW_FLOATS = 20, 20, 60
 
 

@@ -200,8 +200,27 @@ __device__ __forceinline__ void grad_sincos(float x, float* s, float* c) {
     __sincosf(r, s, c);
 }
 
-// Appearance: rasterize.cu:105-138.
-template <bool Neural>
+// Fast forms for the appearance, used unless exact appearance is requested:
+// Cody-Waite reduction by 2*pi as in grad_sincos, then the SFU approximations
+// (|error| < 4e-7 for the waves, so an image moves by less than 1e-6), and the SFU
+// exponential with a fast divide for the sigmoid.
+__device__ __forceinline__ float fast_cos(float x) {
+    const float k = rintf(x * 0.159154943091895336f);
+    float r = fmaf(-k, 6.28318548202514648f, x);
+    r = fmaf(-k, -1.74845553e-07f, r);
+    return __cosf(r);
+}
+__device__ __forceinline__ float fast_sin(float x) {
+    const float k = rintf(x * 0.159154943091895336f);
+    float r = fmaf(-k, 6.28318548202514648f, x);
+    r = fmaf(-k, -1.74845553e-07f, r);
+    return __sinf(r);
+}
+
+// Appearance: rasterize.cu:105-138.  Exact: the reference's expressions with
+// full-precision cosf/sinf/expf (images bit-identical to the reference's); otherwise
+// the fast forms above.
+template <bool Neural, bool Exact>
 __device__ __forceinline__ void appearance_forward(const float* a, const float* g, const Sample& v,
                                                    const Directions& dirs, float* color,
                                                    float* hidden, float* pre) {
@@ -213,21 +232,22 @@ __device__ __forceinline__ void appearance_forward(const float* a, const float* 
 #pragma unroll
             for (int k = 0; k < 5; ++k) z += a[h * 5 + k] * input[k];
             pre[h] = z;
-            hidden[h] = sinf(30 * z);
+            hidden[h] = Exact ? sinf(30 * z) : fast_sin(30 * z);
         }
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             float z = a[54 + c];
 #pragma unroll
             for (int h = 0; h < 6; ++h) z += a[36 + c * 6 + h] * hidden[h];
-            color[c] = 1 / (1 + expf(-z));
+            color[c] = Exact ? 1 / (1 + expf(-z)) : __fdividef(1.f, 1.f + __expf(-z));
         }
     } else {
         float h1 = 0, h2 = 0;
 #pragma unroll
         for (int f = 0; f < 4; ++f) {
             const float dot = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
-            const float wave = cosf(a[10 + f] * dot + a[14 + f]);   // a[10+f] = 2 pi mag_f
+            const float arg = a[10 + f] * dot + a[14 + f];   // a[10+f] = 2 pi mag_f
+            const float wave = Exact ? cosf(arg) : fast_cos(arg);
             h1 += a[6 + f] * 0.5f * (1 + wave);
             h2 += a[6 + f] * 0.5f * (1 - wave);
         }
@@ -236,7 +256,7 @@ __device__ __forceinline__ void appearance_forward(const float* a, const float* 
     }
 }
 
-template <bool Neural, bool Count>
+template <bool Neural, bool Count, bool Exact>
 __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params P) {
     unsigned tests = 0, accepts = 0;
     __shared__ Batch<Neural> batch;
@@ -266,7 +286,7 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
             if (next < 0.0001f) { done = true; break; }
             if constexpr (Count) ++accepts;
             float color[3], hidden[6], pre[6];
-            appearance_forward<Neural>(reinterpret_cast<const float*>(batch.app[j]), g, v, dirs,
+            appearance_forward<Neural, Exact>(reinterpret_cast<const float*>(batch.app[j]), g, v, dirs,
                                        color, hidden, pre);
             const float w = T * v.alpha;
             const float m = mscale * (1 - P.near_plane / v.depth);
@@ -634,9 +654,9 @@ extern "C" int gs_composite_forward(const float* records, const float* rows, int
                                     int64_t records_count, int64_t rows_count,
                                     const float* backgrounds, const int32_t* point_list,
                                     const int32_t* ranges, int64_t images, int width, int height,
-                                    int neural, float near_plane, float far_plane, float* maps,
-                                    float* state, int32_t* contributors, uint64_t* counters,
-                                    void* stream) {
+                                    int neural, int flags, float near_plane, float far_plane,
+                                    float* maps, float* state, int32_t* contributors,
+                                    uint64_t* counters, void* stream) {
     int st = check_composite("gs_composite_forward", records, rows, row_mode, primitive_ids, cameras,
                              surfels, records_count, backgrounds, ranges, images, width, height);
     if (st) return st;
@@ -665,14 +685,17 @@ extern "C" int gs_composite_forward(const float* records, const float* rows, int
     auto s = as_stream(stream);
     P.counters = reinterpret_cast<unsigned long long*>(counters);
     const dim3 block(kTile, kTile);
-    if (neural && counters)
-        composite_forward_kernel<true, true><<<unsigned(tiles), block, 0, s>>>(P);
-    else if (neural)
-        composite_forward_kernel<true, false><<<unsigned(tiles), block, 0, s>>>(P);
-    else if (counters)
-        composite_forward_kernel<false, true><<<unsigned(tiles), block, 0, s>>>(P);
-    else
-        composite_forward_kernel<false, false><<<unsigned(tiles), block, 0, s>>>(P);
+    const bool exact = flags & GS_COMPOSITE_EXACT;
+    const unsigned grid = unsigned(tiles);
+#define GS_FWD(N, C, E) composite_forward_kernel<N, C, E><<<grid, block, 0, s>>>(P)
+    if (neural) {
+        if (counters) { if (exact) GS_FWD(true, true, true); else GS_FWD(true, true, false); }
+        else { if (exact) GS_FWD(true, false, true); else GS_FWD(true, false, false); }
+    } else {
+        if (counters) { if (exact) GS_FWD(false, true, true); else GS_FWD(false, true, false); }
+        else { if (exact) GS_FWD(false, false, true); else GS_FWD(false, false, false); }
+    }
+#undef GS_FWD
     GS_CHECK_LAUNCH("composite_forward_kernel");
     return GS_OK;
 }

@@ -143,8 +143,9 @@ class Composite(torch.autograd.Function):
             nat.call("gs_composite_forward", a["records"], a["rows"], row_mode, None,
                      a["cameras"], surfels, ch.record_count, a["rows_count"],
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
-                     nat.ptr(ch.ranges), ch.images, width, height, int(neural), near_plane,
-                     far_plane, _at(maps, a["pixel0"] * 9), _at(state, a["pixel0"] * 3),
+                     nat.ptr(ch.ranges), ch.images, width, height, int(neural),
+                     _composite_flags(), near_plane, far_plane, _at(maps, a["pixel0"] * 9),
+                     _at(state, a["pixel0"] * 3),
                      _at(contributors, a["pixel0"]), nat.ptr(_counters("forward", device)),
                      stream)
         ctx.save_for_backward(records, rows, backgrounds, selected, state, contributors)
@@ -204,6 +205,16 @@ def _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height):
     return dict(records=_at(records, ch.record0 * nat.RECORD_FLOATS),
                 rows=_at(rows, row0 * rows.shape[1]), cameras=cams, rows_count=rows_count,
                 row0=row0, pixel0=ch.image0 * height * width)
+
+
+# Appearance evaluation in the forward compositor: False (default) uses the SFU forms
+# (images within 1e-6 of exact), True the reference's full-precision cosf/sinf/expf
+# (images bit-identical to the reference's).
+EXACT_APPEARANCE = False
+
+
+def _composite_flags() -> int:
+    return nat.COMPOSITE_EXACT if EXACT_APPEARANCE else 0
 
 
 # The public renderers bin tightly: tiles that no sample of a record can reach with

@@ -154,16 +154,21 @@ int gs_bin_static(const float* records, int record_stride, const int32_t* radii,
  * zeroes them, so several calls over image chunks can accumulate into shared
  * appearance rows); grad_xy (nullable, [R][2]) receives the slot 9-10
  * (screen-centre) gradients instead of grad_records when given.
+ * Forward flags: 0 evaluates the Gabor waves, SIREN sines and sigmoid with the SFU
+ * (wave error < 4e-7, images within 1e-6 of the exact evaluation); GS_COMPOSITE_EXACT
+ * uses full-precision cosf/sinf/expf in the reference's expression order, which makes
+ * images bit-identical to the reference's.
  * counters (nullable, uint64[2], zeroed by the caller) receives the work done:
  * [0] ray/splat samples tested, [1] contributions accepted (blended forward,
  * differentiated backward).  A NULL pointer selects kernels without counting.
  */
+#define GS_COMPOSITE_EXACT 1   /* forward flags: full-precision cosf/sinf/expf appearance */
 int gs_composite_forward(const float* records, const float* rows, int row_mode,
                          const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
                          int64_t records_count, int64_t rows_count,
                          const float* backgrounds, const int32_t* point_list,
                          const int32_t* ranges, int64_t images, int width, int height,
-                         int neural, float near_plane, float far_plane, float* maps,
+                         int neural, int flags, float near_plane, float far_plane, float* maps,
                          float* state, int32_t* contributors, uint64_t* counters,
                          void* stream);
 int gs_composite_backward(const float* records, const float* rows, int row_mode,

@@ -100,8 +100,8 @@ def test_composite_forward_matches_oracle(method):
     from diff_gabor_splatting_b200 import _native as nat
     nat.call("gs_composite_forward", nat.ptr(records), nat.ptr(rows), nat.ROWS_PER_SURFEL, None,
              C, N, records.shape[0], rows.shape[0], nat.ptr(v["backgrounds"]),
-             nat.ptr(point_list), nat.ptr(ranges), images, W, H, int(method == "neural"), 0.2,
-             100.0, nat.ptr(maps), nat.ptr(state), nat.ptr(contrib), None,
+             nat.ptr(point_list), nat.ptr(ranges), images, W, H, int(method == "neural"), 0,
+             0.2, 100.0, nat.ptr(maps), nat.ptr(state), nat.ptr(contrib), None,
              nat.stream_of(records.device))
     geometry, appearance, opacities, prim_ids = _oracle_inputs(v, records, rows, method)
     out = O.composite(geometry, appearance, opacities, prim_ids,

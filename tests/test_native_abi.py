@@ -53,9 +53,9 @@ def test_invalid_arguments_fail_before_any_gpu_work():
     assert lib.gs_pack_rows(None, 4, 17, None, None) == 1
     assert lib.gs_sh_forward(None, None, None, 4, 1, 1, 1, None, None) == 1
     assert lib.gs_composite_forward(None, None, 0, None, 1, 1, 0, 0, None, None, None, 0, 8, 8, 0,
-                                    0.2, 100.0, None, None, None, None, None) == 1
+                                    0, 0.2, 100.0, None, None, None, None, None) == 1
     assert lib.gs_composite_forward(None, None, 7, None, 1, 1, 0, 0, ctypes.c_void_p(16),
-                                     None, ctypes.c_void_p(16), 1, 8, 8, 0, 0.2, 100.0,
+                                     None, ctypes.c_void_p(16), 1, 8, 8, 0, 0, 0.2, 100.0,
                                      None, None, None, None, None) == 1
     assert b"row mode" in lib.gs_last_error()
     # tiles beyond int32

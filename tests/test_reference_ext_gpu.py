@@ -151,7 +151,29 @@ def test_public_api_benchmark_like_scene(method, sh_degree):
         assert rel <= 1e-3, f"{name}: relative L2 error {rel:.2e}"
 
 
-def test_reference_varies_with_batch_shape():
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_exact_appearance_is_bit_identical(method, monkeypatch):
+    """With exact appearance (full-precision cosf/sinf/expf) the native layer reproduces
+    the reference's images, state and contributor counts bit for bit; the default fast
+    appearance stays within 1e-6 absolute."""
+    import diff_gabor_splatting_b200.rendering as rendering
+
+    v = random_scene(method, scenes=2, cameras=2, n=400, width=W, height=H)
+    args = packed_inputs(v, method, packed=True)
+    bg = v["backgrounds"].reshape(-1, 3).contiguous()
+    flags = (W, H, method == "neural", 0.2, 100.0)
+    ref_out = ref_C.rasterize_forward(*args, bg, *flags)
+    monkeypatch.setattr(rendering, "EXACT_APPEARANCE", True)
+    exact = our_C.rasterize_forward(*args, bg, *flags)
+    for k in (0, 3, 4):
+        assert torch.equal(exact[k], ref_out[k]), k
+    monkeypatch.setattr(rendering, "EXACT_APPEARANCE", False)
+    fast = our_C.rasterize_forward(*args, bg, *flags)
+    assert (fast[0] - ref_out[0]).abs().max().item() <= 1e-6
+    assert torch.equal(fast[4], ref_out[4])
+
+
+def test_reference_varies_with_batch_shape(monkeypatch):
     """The reference's own images of one scene change with the batch it is rendered in.
 
     For a single small scene PyTorch's einsum (inside the reference's projection) takes
@@ -162,6 +184,9 @@ def test_reference_varies_with_batch_shape():
     alone it differs from the reference-alone result exactly as the reference differs
     from itself between the two batch shapes, and equals the reference-batched result.
     """
+    import diff_gabor_splatting_b200.rendering as rendering
+
+    monkeypatch.setattr(rendering, "EXACT_APPEARANCE", True)
     v = random_scene("classic", scenes=1, cameras=3, n=500, width=W, height=H)
     vals = ordered(v, "classic")
     ref_alone = maps_from_result(ref.rasterize_gabors(**vals, width=W, height=H))
