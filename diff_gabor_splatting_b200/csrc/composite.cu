@@ -335,53 +335,63 @@ struct Fields {
     }
 };
 
-constexpr int kBackBatch = 32;
+constexpr int kBackBatch = 16;
 constexpr int kWarps = kBlock / 32;
 
-// Reduce `vals` across the warp (lane i ends up owning packed field i) and store the
-// warp's sums in its own shared row; `mask` records which warps stored for the record.
-// Plain stores, no shared atomics: the CTA's eight rows are summed at the flush.
-template <bool Neural>
-__device__ __forceinline__ void warp_store(float* vals, float* row, unsigned* mask, int warp,
-                                           int lane) {
-    using F = Fields<Neural>;
-    constexpr int kFull = F::kCount / 32;
-    constexpr int kRest = F::kCount - kFull * 32;
-#pragma unroll
-    for (int chunk = 0; chunk < kFull; ++chunk) {
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = vals[chunk * 32 + i];
-        warp_reduce_scatter<32>(v, lane);
-        row[chunk * 32 + lane] = v[0];
-    }
-    if constexpr (kRest > 0) {
-        constexpr int kPad = kRest <= 1 ? 1 : kRest <= 2 ? 2 : kRest <= 4 ? 4 : kRest <= 8 ? 8
-                           : kRest <= 16 ? 16 : 32;
-        constexpr int kShift = kPad == 1 ? 5 : kPad == 2 ? 4 : kPad == 4 ? 3 : kPad == 8 ? 2
-                             : kPad == 16 ? 1 : 0;
-        float v[kPad];
-#pragma unroll
-        for (int i = 0; i < kPad; ++i) v[i] = i < kRest ? vals[kFull * 32 + i] : 0.f;
-        warp_reduce_scatter<kPad>(v, lane);
-        const int field = lane >> kShift;
-        if ((lane & ((1 << kShift) - 1)) == 0 && field < kRest) row[kFull * 32 + field] = v[0];
-    }
-    if (lane == 0) atomicOr(mask, 1u << warp);
-}
+constexpr int kLaneStride = 36;   // 32 fields + 4 pad: a lane's 16-byte stores hit 4 new banks
 
-// Shared memory of the backward kernel: the record batch, one partial-sum row per
-// (warp, record), and the per-record masks of warps that stored.
 template <bool Neural>
 struct BackShared {
     using F = Fields<Neural>;
     static constexpr int kStride = (F::kCount + 3) / 4 * 4;   // 36 classic, 76 neural
     Batch<Neural, kBackBatch> batch;
-    float rows[kWarps][kBackBatch][kStride];
-    unsigned mask[kBackBatch];
+    float rows[kWarps][kBackBatch][kStride];   // per (warp, record) field sums
+    float lanes[kWarps][32][kLaneStride];      // per-warp transpose scratch, 32 fields a pass
+    unsigned mask[kBackBatch];                 // warps that stored a row for the record
     int warp_max[kWarps];
     float bg[3];
 };
+
+// Sum `vals` over the warp's 32 lanes into the warp's row for the record, 32 fields a
+// pass: every lane stores its fields as one row of the warp's scratch (16-byte stores,
+// conflict-free), then lane l adds up column l (32 loads + 31 adds, where a shuffle
+// butterfly costs 31 shuffles, 62 selects and 31 adds).  One or two fields left over
+// past the passes are summed with a plain butterfly.  Plain stores, no shared atomics:
+// the CTA's eight rows are summed at the flush; `mask` records which warps stored.
+template <bool Neural>
+__device__ __forceinline__ void warp_store(const float* vals, float (*scratch)[kLaneStride],
+                                           float* row, unsigned* mask, int warp, int lane) {
+    using F = Fields<Neural>;
+    constexpr int kPasses = F::kCount / 32 + (F::kCount % 32 > 2 ? 1 : 0);
+#pragma unroll
+    for (int pass = 0; pass < kPasses; ++pass) {
+        if (pass) __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int f = pass * 32 + 4 * k;
+            float4 q;
+            q.x = f + 0 < F::kCount ? vals[f + 0] : 0.f;
+            q.y = f + 1 < F::kCount ? vals[f + 1] : 0.f;
+            q.z = f + 2 < F::kCount ? vals[f + 2] : 0.f;
+            q.w = f + 3 < F::kCount ? vals[f + 3] : 0.f;
+            *reinterpret_cast<float4*>(&scratch[lane][4 * k]) = q;
+        }
+        __syncwarp();
+        float sum = 0.f;
+#pragma unroll
+        for (int r = 0; r < 32; ++r) sum += scratch[r][lane];
+        if (pass * 32 + lane < F::kCount) row[pass * 32 + lane] = sum;
+    }
+#pragma unroll
+    for (int f = kPasses * 32; f < F::kCount; ++f) {
+        float v = vals[f];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) row[f] = v;
+    }
+    __syncwarp();   // column reads done before the next record's stores
+    if (lane == 0) atomicOr(mask, 1u << warp);
+}
 
 template <bool Neural, bool Count>
 __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_kernel(const Params P) {
@@ -591,7 +601,7 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                     gg[6 + k] += x * gk[k] + y * gl[k];
                 }
             }
-            warp_store<Neural>(vals, sh.rows[warp][j], &sh.mask[j], warp, lane);
+            warp_store<Neural>(vals, sh.lanes[warp], sh.rows[warp][j], &sh.mask[j], warp, lane);
         }
         // flush: sum the warps' rows of each record in warp order, one global atomic per
         // (tile, record, field)

@@ -70,13 +70,20 @@ def stage_model(name: str, counts: dict, w) -> dict:
                     basis=f"{TEST_FLOP} flop/test x tests + {BACKWARD_ACCEPT_FLOP[w.method]} "
                           "flop/accept x accepts (kernel counters)")
     if name == "gs_bin_sort":
-        # expand writes 8 B/slot; 2 onesweep passes read+write 8 B/slot each plus a 4 B
-        # histogram read; ranges read 4 B/slot
-        return dict(bound="hbm", unit="GB/s", work=I * (8 + 2 * 16 + 4 + 4),
-                    basis="48 B per tile intersection")
+        # spans: 16 B written per span (end, tile, record) and read back twice (owner
+        # table, expand); expand writes key+value 8 B/slot; each 8-bit radix pass of the
+        # tile sort reads and writes key+value 16 B/slot (+4 B/slot for the histograms,
+        # once); ranges read the sorted keys 4 B/slot
+        P = counts.get("sort_passes", 2 * I)
+        Sp = counts.get("spans", 0)
+        return dict(bound="hbm", unit="GB/s", work=Sp * 48 + I * (8 + 4 + 4) + 16 * P,
+                    basis="48 B per row span + 16 B per intersection + 16 B per intersection"
+                          " and radix pass")
     if name == "gs_bin_count":
-        return dict(bound="hbm", unit="GB/s", work=R * (8 + 4 * 16 + 4 + 8 + 16),
-                    basis="100 B per record (keys, 4-pass depth sort, counts, scan)")
+        # depth keys 8 B written/record; 32-bit key-value depth sort, 4 passes of 16 B +
+        # 4 B histogram read; tile and span counts 16 B written; two scans 32 B
+        return dict(bound="hbm", unit="GB/s", work=R * (8 + 4 * 16 + 4 + 16 + 32),
+                    basis="124 B per record (keys, 4-pass depth sort, counts, scans)")
     surfel_in = 4 * (3 + 4 + 2 + 1 + (2 * K * 3 + 12 if K else 0))
     if name == "gs_project_forward":
         pair_out = 4 * (20 + 2 + 1 + (20 if K else 0))

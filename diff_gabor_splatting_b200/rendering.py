@@ -285,7 +285,11 @@ def _bin_chunk(ch, records, radii, surfels, width, height, counted=None):
     if WORK is not None:
         WORK["records"] = WORK.get("records", 0) + ch.record_count
         WORK["intersections"] = WORK.get("intersections", 0) + total
+        WORK["spans"] = WORK.get("spans", 0) + spans
         WORK["tiles"] = WORK.get("tiles", 0) + ch.images * tw * th
+        # intersections x 8-bit radix passes of the tile-id sort
+        passes = -(-max(1, (ch.images * tw * th - 1).bit_length()) // 8)
+        WORK["sort_passes"] = WORK.get("sort_passes", 0) + total * passes
     return ch
 
 
