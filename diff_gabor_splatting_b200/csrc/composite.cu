@@ -336,6 +336,7 @@ struct Fields {
 };
 
 constexpr int kBackBatch = 16;
+constexpr float kThird = 1.f / 3;   // gradient-only replay: multiply instead of divide
 constexpr int kWarps = kBlock / 32;
 
 constexpr int kLaneStride = 36;   // 32 fields + 4 pad: a lane's 16-byte stores hit 4 new banks
@@ -468,13 +469,15 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
             if (active) {
                 float color[3], hidden[6], pre[6], gc[3], gs[2] = {0.f, 0.f};
                 float waves[4], sines[4];
-                T /= 1 - v.alpha;
+                // T before this sample: one correctly rounded reciprocal, shared with galpha
+                const float inv_transmit = __frcp_rn(1 - v.alpha);
+                T *= inv_transmit;
                 const float w = T * v.alpha;
                 // colour replay: feeds only gradients, so the waves, the SIREN's sines
                 // and its sigmoid use the fast forms (cosines kept for the adjoint)
                 float coss[6], dots[4], h1, h2;
                 if constexpr (Neural) {
-                    const float input[5] = {v.s[0] / 3, v.s[1] / 3, g[14], g[15], g[16]};
+                    const float input[5] = {v.s[0] * kThird, v.s[1] * kThird, g[14], g[15], g[16]};
 #pragma unroll
                     for (int h = 0; h < 6; ++h) {
                         float z = a[30 + h];
@@ -488,7 +491,7 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                         float z = a[54 + c];
 #pragma unroll
                         for (int h = 0; h < 6; ++h) z += a[36 + c * 6 + h] * hidden[h];
-                        color[c] = __frcp_rn(1.f + __expf(-z));
+                        color[c] = __fdividef(1.f, 1.f + __expf(-z));
                     }
                 } else {
                     h1 = 0;
@@ -511,13 +514,12 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                     gc[c] = w * go[c];
                     gg[11 + c] += w * go[5 + c];
                 }
-                const float inv_transmit = __frcp_rn(1 - v.alpha);
                 const float galpha = T * gw - suffix * inv_transmit +
                                      final_t * (go[3] - background_dot) * inv_transmit;
                 suffix += w * gw;
                 // appearance backward: rasterize.cu:146-197
                 if constexpr (Neural) {
-                    const float input[5] = {v.s[0] / 3, v.s[1] / 3, g[14], g[15], g[16]};
+                    const float input[5] = {v.s[0] * kThird, v.s[1] * kThird, g[14], g[15], g[16]};
                     float gh[6] = {}, gi[5] = {};
 #pragma unroll
                     for (int c = 0; c < 3; ++c) {
@@ -539,8 +541,8 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                             gi[k] += gz * a[h * 5 + k];
                         }
                     }
-                    gs[0] += gi[0] / 3;
-                    gs[1] += gi[1] / 3;
+                    gs[0] += gi[0] * kThird;
+                    gs[1] += gi[1] * kThird;
 #pragma unroll
                     for (int k = 0; k < 3; ++k) gg[14 + k] += gi[k + 2];
                 } else {
@@ -568,7 +570,7 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                 }
                 // geometry: rasterize.cu:359-385
                 const float gz = w * go[4] + go[8] * 2 * w * (m * total_a - m1) * mscale *
-                                                 P.near_plane * __frcp_rn(v.depth * v.depth);
+                                                 P.near_plane * __fdividef(1.f, v.depth * v.depth);
                 if (Neural || v.surface) {
                     gs[0] += gz * g[6];
                     gs[1] += gz * g[7];

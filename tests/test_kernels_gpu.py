@@ -284,14 +284,15 @@ def test_scene_grouped_chunks(monkeypatch):
 @pytest.mark.parametrize("config,cameras,scenes", [(1, 1, None), (2, None, None), (3, None, 4)])
 def test_tight_bins_render_identically_at_benchmark_size(config, cameras, scenes, monkeypatch):
     """Tight binning drops only tiles no sample can reach: at the benchmark configs' sizes
-    and distributions the images are bit-identical to the reference's square bins and the
-    gradients equal to float-atomic order, with fewer tile intersections."""
+    and distributions the images are bit-identical to the reference's square bins, with
+    fewer tile intersections, and the gradients differ only by float-atomic order: no
+    more than two square-bin runs differ from each other (x4), or 1e-4 of the scale."""
     from diff_gabor_splatting_b200.workloads import loss_of, make_workload
 
     w = make_workload(config, cameras=cameras, scenes=scenes)
     fn = rasterize_gabors if w.method == "classic" else rasterize_neural_gabors
     results = {}
-    for tight in (False, True):
+    for run, tight in (("square", False), ("square again", False), ("tight", True)):
         monkeypatch.setattr(rendering, "TIGHT_BINNING", tight)
         values = {k: t.cuda().requires_grad_() for k, t in w.inputs.items()}
         rendering.WORK = {}
@@ -303,10 +304,20 @@ def test_tight_bins_render_identically_at_benchmark_size(config, cameras, scenes
             work = rendering.WORK
         finally:
             rendering.WORK = None
-        results[tight] = (maps.detach(), {k: v.grad for k, v in values.items()},
-                          work["intersections"])
+        results[run] = (maps.detach(), {k: v.grad for k, v in values.items()},
+                        work["intersections"])
         del values, rgb, alpha, meta, maps
-    assert results[True][2] < results[False][2]
-    assert torch.equal(results[True][0], results[False][0])
-    for name, g in results[False][1].items():
-        assert_grads_close(results[True][1][name], g, name, elementwise=1e-4)
+    assert results["tight"][2] < results["square"][2]
+    assert torch.equal(results["tight"][0], results["square"][0])
+
+    def max_error(a, e):
+        d = (a.double() - e.double()).abs()
+        return d.max().item() / (e.abs().max().item() + 1e-12), d.argmax().item()
+
+    for name, g in results["square"][1].items():
+        noise, _ = max_error(results["square again"][1][name], g)
+        err, at = max_error(results["tight"][1][name], g)
+        assert err <= max(4 * noise, 1e-4), (
+            f"{name}: {err:.2e} of scale (atomic-order noise {noise:.2e}) at flat index {at}: "
+            f"square {g.flatten()[at].item():.6e} / {results['square again'][1][name].flatten()[at].item():.6e}, "
+            f"tight {results['tight'][1][name].flatten()[at].item():.6e}")
