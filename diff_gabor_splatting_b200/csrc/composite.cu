@@ -98,6 +98,7 @@ struct Batch {
     int64_t rows[kSize];
     float4 geo[kSize][kRec / 4];
     float4 app[kSize][kRow / 4];
+    float half_weight[Neural ? 1 : kSize];   // classic: half the sum of the 4 wave weights
 };
 
 // Stage `count` records (list positions first + stride*e) and their rows.  Per record
@@ -129,7 +130,12 @@ __device__ __forceinline__ void load_batch(B& b, const Params& P, int first, int
             float4 v = __ldg(P.rows + b.rows[e] * (kRow / 4) + q);
             if constexpr (!B::kNeural) {
                 constexpr float kTwoPi = 2 * kPi;
-                if (q == 2) { v.z = kTwoPi * v.z; v.w = kTwoPi * v.w; }   // magnitudes 0-1
+                if (q == 2) {   // weights 2-3, magnitudes 0-1
+                    const float4 w01 = __ldg(P.rows + b.rows[e] * (kRow / 4) + 1);
+                    b.half_weight[e] = 0.5f * ((w01.z + w01.w) + (v.x + v.y));
+                    v.z = kTwoPi * v.z;
+                    v.w = kTwoPi * v.w;
+                }
                 if (q == 3) { v.x = kTwoPi * v.x; v.y = kTwoPi * v.y; }   // magnitudes 2-3
             }
             b.app[e][q] = v;
@@ -204,6 +210,8 @@ __device__ __forceinline__ void grad_sincos(float x, float* s, float* c) {
 // Cody-Waite reduction by 2*pi as in grad_sincos, then the SFU approximations
 // (|error| < 4e-7 for the waves, so an image moves by less than 1e-6), and the SFU
 // exponential with a fast divide for the sigmoid.
+constexpr float kThird = 1.f / 3;   // fast and gradient-only forms multiply instead of divide
+
 __device__ __forceinline__ float fast_cos(float x) {
     const float k = rintf(x * 0.159154943091895336f);
     float r = fmaf(-k, 6.28318548202514648f, x);
@@ -222,10 +230,11 @@ __device__ __forceinline__ float fast_sin(float x) {
 // the fast forms above.
 template <bool Neural, bool Exact>
 __device__ __forceinline__ void appearance_forward(const float* a, const float* g, const Sample& v,
-                                                   const Directions& dirs, float* color,
-                                                   float* hidden, float* pre) {
+                                                   const Directions& dirs, float half_weight,
+                                                   float* color, float* hidden, float* pre) {
     if constexpr (Neural) {
-        const float input[5] = {v.s[0] / 3, v.s[1] / 3, g[14], g[15], g[16]};
+        const float input[5] = {Exact ? v.s[0] / 3 : v.s[0] * kThird,
+                                Exact ? v.s[1] / 3 : v.s[1] * kThird, g[14], g[15], g[16]};
 #pragma unroll
         for (int h = 0; h < 6; ++h) {
             float z = a[30 + h];
@@ -241,16 +250,28 @@ __device__ __forceinline__ void appearance_forward(const float* a, const float* 
             for (int h = 0; h < 6; ++h) z += a[36 + c * 6 + h] * hidden[h];
             color[c] = Exact ? 1 / (1 + expf(-z)) : __fdividef(1.f, 1.f + __expf(-z));
         }
-    } else {
+    } else if constexpr (Exact) {
         float h1 = 0, h2 = 0;
 #pragma unroll
         for (int f = 0; f < 4; ++f) {
             const float dot = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
             const float arg = a[10 + f] * dot + a[14 + f];   // a[10+f] = 2 pi mag_f
-            const float wave = Exact ? cosf(arg) : fast_cos(arg);
+            const float wave = cosf(arg);
             h1 += a[6 + f] * 0.5f * (1 + wave);
             h2 += a[6 + f] * 0.5f * (1 - wave);
         }
+#pragma unroll
+        for (int c = 0; c < 3; ++c) color[c] = h1 * a[c] + h2 * a[3 + c];
+    } else {
+        // h1 = sum w_f (1 + wave_f) / 2 = W/2 + hw/2 and h2 = W/2 - hw/2 with
+        // hw = sum w_f wave_f and W/2 staged per record: one FMA per wave.
+        float hw = 0;
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+            const float dot = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
+            hw = fmaf(a[6 + f], fast_cos(a[10 + f] * dot + a[14 + f]), hw);
+        }
+        const float h1 = fmaf(0.5f, hw, half_weight), h2 = fmaf(-0.5f, hw, half_weight);
 #pragma unroll
         for (int c = 0; c < 3; ++c) color[c] = h1 * a[c] + h2 * a[3 + c];
     }
@@ -273,6 +294,7 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
     const int2 range = P.ranges[tile];
     const Directions dirs;
     const float mscale = P.far_plane / (P.far_plane - P.near_plane);
+    const float mscale_near = mscale * P.near_plane;
     for (int start = range.x; start < range.y; start += kBatch) {
         if (__syncthreads_count(done) == kBlock) break;
         const int count = min(kBatch, range.y - start);
@@ -287,9 +309,11 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
             if constexpr (Count) ++accepts;
             float color[3], hidden[6], pre[6];
             appearance_forward<Neural, Exact>(reinterpret_cast<const float*>(batch.app[j]), g, v, dirs,
-                                       color, hidden, pre);
+                                              batch.half_weight[Neural ? 0 : j], color, hidden,
+                                              pre);
             const float w = T * v.alpha;
-            const float m = mscale * (1 - P.near_plane / v.depth);
+            const float m = Exact ? mscale * (1 - P.near_plane / v.depth)
+                                  : fmaf(-mscale_near, __fdividef(1.f, v.depth), mscale);
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
                 out[c] += w * color[c];
@@ -336,7 +360,6 @@ struct Fields {
 };
 
 constexpr int kBackBatch = 16;
-constexpr float kThird = 1.f / 3;   // gradient-only replay: multiply instead of divide
 constexpr int kWarps = kBlock / 32;
 
 constexpr int kLaneStride = 36;   // 32 fields + 4 pad: a lane's 16-byte stores hit 4 new banks
@@ -446,6 +469,10 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     const int2 range = P.ranges[tile];
     const Directions dirs;
     const float mscale = P.far_plane / (P.far_plane - P.near_plane);
+    // per-pixel constants of the gradient expressions
+    const float mscale_near = mscale * P.near_plane;
+    const float depth_term = go[8] * 2 * mscale_near;                // d distortion / d depth
+    const float background_term = final_t * (go[3] - background_dot);  // galpha's T-independent part
     for (int start = block_last; start > 0; start -= kBackBatch) {
         const int count = min(kBackBatch, start);
         __syncthreads();   // every thread has finished the previous batch's flush
@@ -494,19 +521,20 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                         color[c] = __fdividef(1.f, 1.f + __expf(-z));
                     }
                 } else {
-                    h1 = 0;
-                    h2 = 0;
+                    float hw = 0;
 #pragma unroll
                     for (int f = 0; f < 4; ++f) {
                         dots[f] = dirs.c[f] * v.s[0] + dirs.s[f] * v.s[1];
                         grad_sincos(a[10 + f] * dots[f] + a[14 + f], &sines[f], &waves[f]);
-                        h1 += a[6 + f] * 0.5f * (1 + waves[f]);
-                        h2 += a[6 + f] * 0.5f * (1 - waves[f]);
+                        hw = fmaf(a[6 + f], waves[f], hw);
                     }
+                    h1 = fmaf(0.5f, hw, batch.half_weight[Neural ? 0 : j]);
+                    h2 = fmaf(-0.5f, hw, batch.half_weight[Neural ? 0 : j]);
 #pragma unroll
                     for (int c = 0; c < 3; ++c) color[c] = h1 * a[c] + h2 * a[3 + c];
                 }
-                const float m = mscale * (1 - __fdividef(P.near_plane, v.depth));
+                const float inv_depth = __fdividef(1.f, v.depth);
+                const float m = fmaf(-mscale_near, inv_depth, mscale);
                 float gw = go[4] * v.depth + go[8] * (m * m * total_a + m2 - 2 * m * m1);
 #pragma unroll
                 for (int c = 0; c < 3; ++c) {
@@ -514,8 +542,7 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                     gc[c] = w * go[c];
                     gg[11 + c] += w * go[5 + c];
                 }
-                const float galpha = T * gw - suffix * inv_transmit +
-                                     final_t * (go[3] - background_dot) * inv_transmit;
+                const float galpha = fmaf(T, gw, (background_term - suffix) * inv_transmit);
                 suffix += w * gw;
                 // appearance backward: rasterize.cu:146-197
                 if constexpr (Neural) {
@@ -548,29 +575,33 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                 } else {
                     // The reference's per-wave loop (rasterize.cu:173-195) factored: summed
                     // over waves, d colour / d c1 = h1 and d colour / d c2 = h2; every
-                    // wave's weight and phase terms go through S1 = sum gc (c1 + c2) and
-                    // S2 = sum gc (c1 - c2).
+                    // wave's weight and phase terms go through S1 = sum gc (c1 + c2) / 2 and
+                    // S2 = sum gc (c1 - c2) / 2.  The magnitude field holds gt * dot; the
+                    // flush multiplies its per-tile sum by 2 pi.
                     float S1 = 0, S2 = 0;
 #pragma unroll
                     for (int c = 0; c < 3; ++c) {
                         ga[c] = gc[c] * h1;
                         ga[3 + c] = gc[c] * h2;
-                        S1 += gc[c] * (a[c] + a[3 + c]);
-                        S2 += gc[c] * (a[c] - a[3 + c]);
+                        S1 = fmaf(gc[c], a[c] + a[3 + c], S1);
+                        S2 = fmaf(gc[c], a[c] - a[3 + c], S2);
                     }
+                    S1 *= 0.5f;
+                    S2 *= 0.5f;
 #pragma unroll
                     for (int f = 0; f < 4; ++f) {
-                        const float gt = -0.5f * a[6 + f] * sines[f] * S2;
-                        ga[6 + f] = 0.5f * (S1 + waves[f] * S2);
-                        ga[10 + f] = gt * (2 * kPi) * dots[f];
+                        const float gt = -(a[6 + f] * sines[f]) * S2;
+                        ga[6 + f] = fmaf(waves[f], S2, S1);
+                        ga[10 + f] = gt * dots[f];
                         ga[14 + f] = gt;
-                        gs[0] += gt * a[10 + f] * dirs.c[f];   // a[10+f] = 2 pi mag_f
-                        gs[1] += gt * a[10 + f] * dirs.s[f];
+                        const float u = gt * a[10 + f];   // a[10+f] = 2 pi mag_f
+                        gs[0] = fmaf(u, dirs.c[f], gs[0]);
+                        gs[1] = fmaf(u, dirs.s[f], gs[1]);
                     }
                 }
                 // geometry: rasterize.cu:359-385
-                const float gz = w * go[4] + go[8] * 2 * w * (m * total_a - m1) * mscale *
-                                                 P.near_plane * __fdividef(1.f, v.depth * v.depth);
+                const float gz = w * fmaf(depth_term * fmaf(m, total_a, -m1), inv_depth * inv_depth,
+                                          go[4]);
                 if (Neural || v.surface) {
                     gs[0] += gz * g[6];
                     gs[1] += gz * g[7];
@@ -617,6 +648,7 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                 if (mask & (1u << w)) val += sh.rows[w][e][field];
             if (val == 0.f) continue;
             const int slot = F::slot(field);
+            if (!Neural && slot >= kRec + 10 && slot < kRec + 14) val *= 2 * kPi;   // magnitudes
             if (slot < kRec) {
                 const int64_t r = batch.ids[e];
                 if (P.grad_xy && (slot == 9 || slot == 10))
