@@ -37,6 +37,10 @@ SIGNATURES = {
                              _f, _p, _p, _p, _p, _p],
     "gs_composite_backward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _p, _p, _p, _l, _i, _i,
                               _i, _f, _f, _p, _p, _p, _p, _p, _p],
+    "gs_composite_forward_split": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _l, _i, _i, _i, _i,
+                                   _f, _f, _p, _p, _p, _p, _p, _p],
+    "gs_composite_backward_split": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _p, _p, _p, _p, _l,
+                                    _i, _i, _i, _f, _f, _p, _p, _p, _p, _p, _p],
     "gs_pack_geometry": [_p, _p, _p, _l, _l, _p, _p],
     "gs_pack_rows": [_p, _l, _i, _p, _p],
     "gs_unpack_geometry_grads": [_p, _p, _l, _l, _p, _p, _p],
@@ -132,6 +136,12 @@ def ptr(t: torch.Tensor | None) -> int | None:
     if t is None:
         return None
     return t.data_ptr() if t.numel() else None
+
+
+def host_array(ctype, values):
+    """A host C array of ``values`` (keep it alive across the call) and its address."""
+    array = (ctype * len(values))(*[0 if v is None else v for v in values])
+    return array, ctypes.cast(array, ctypes.c_void_p)
 
 
 def stream_of(device: torch.device) -> int:

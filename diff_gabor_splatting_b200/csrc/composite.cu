@@ -39,11 +39,16 @@ struct Params {
     const int2* ranges;
     int width, height, tw, th;
     float near_plane, far_plane;
-    // forward outputs / backward inputs
-    float* maps;
+    // forward outputs / backward inputs.  The nine maps as five planes: rgb (3
+    // channels), alpha, depth, normals (3), distortion; plane g of pixel p starts at
+    // out[g] + p * out_px[g] (channels adjacent).  Gradients likewise with a channel
+    // stride (0 for a broadcast gradient); a NULL plane is a zero gradient.
+    float* out[5];
+    int64_t out_px[5];
     float* state;
     int* contributors;
-    const float* grad_maps;
+    const float* gin[5];
+    int64_t gin_px[5], gin_ch[5];
     // backward outputs
     float* grad_records;
     float* grad_xy;
@@ -52,6 +57,12 @@ struct Params {
     // optional work counters: [0] samples tested, [1] contributions accepted
     unsigned long long* counters;
 };
+
+// First map channel and channel count of plane g (rgb, alpha, depth, normals, distortion).
+__host__ __device__ constexpr int plane_first(int g) {
+    return g == 0 ? 0 : g == 1 ? 3 : g == 2 ? 4 : g == 3 ? 5 : 8;
+}
+__host__ __device__ constexpr int plane_size(int g) { return g == 0 || g == 3 ? 3 : 1; }
 
 // Add this thread's counts into the block total and then into counters[0..1].
 __device__ __forceinline__ void add_counts(unsigned long long* counters, unsigned tests,
@@ -332,7 +343,11 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
         for (int c = 0; c < 3; ++c) out[c] += T * P.backgrounds[image * 3 + c];
         out[3] = 1 - T;
 #pragma unroll
-        for (int c = 0; c < kMaps; ++c) P.maps[pixel * kMaps + c] = out[c];
+        for (int g = 0; g < 5; ++g) {
+            float* o = P.out[g] + pixel * P.out_px[g];
+#pragma unroll
+            for (int k = 0; k < plane_size(g); ++k) o[k] = out[plane_first(g) + k];
+        }
         P.state[pixel * 3] = T;
         P.state[pixel * 3 + 1] = m1;
         P.state[pixel * 3 + 2] = m2;
@@ -446,7 +461,12 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     float go[kMaps] = {};
     if (inside) {
 #pragma unroll
-        for (int c = 0; c < kMaps; ++c) go[c] = P.grad_maps[pixel * kMaps + c];
+        for (int g = 0; g < 5; ++g) {
+            if (!P.gin[g]) continue;
+            const float* gi = P.gin[g] + pixel * P.gin_px[g];
+#pragma unroll
+            for (int k = 0; k < plane_size(g); ++k) go[plane_first(g) + k] = gi[k * P.gin_ch[g]];
+        }
     }
     const float final_t = inside ? P.state[pixel * 3] : 0;
     const float total_a = 1 - final_t;
@@ -693,19 +713,13 @@ int check_composite(const char* fn, const float* records, const float* rows, int
 
 using namespace gs;
 
-extern "C" int gs_composite_forward(const float* records, const float* rows, int row_mode,
-                                    const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
-                                    int64_t records_count, int64_t rows_count,
-                                    const float* backgrounds, const int32_t* point_list,
-                                    const int32_t* ranges, int64_t images, int width, int height,
-                                    int neural, int flags, float near_plane, float far_plane,
-                                    float* maps, float* state, int32_t* contributors,
-                                    uint64_t* counters, void* stream) {
-    int st = check_composite("gs_composite_forward", records, rows, row_mode, primitive_ids, cameras,
-                             surfels, records_count, backgrounds, ranges, images, width, height);
-    if (st) return st;
-    (void)rows_count;
-    if (!maps || !state || !contributors) return fail(GS_ERR_ARGUMENT, "gs_composite_forward: NULL output");
+namespace gs {
+namespace {
+
+Params common_params(const float* records, const float* rows, int row_mode,
+                     const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
+                     const float* backgrounds, const int32_t* point_list, const int32_t* ranges,
+                     int width, int height, float near_plane, float far_plane) {
     Params P{};
     P.records = reinterpret_cast<const float4*>(records);
     P.rows = reinterpret_cast<const float4*>(rows);
@@ -722,9 +736,11 @@ extern "C" int gs_composite_forward(const float* records, const float* rows, int
     P.th = (height + kTile - 1) / kTile;
     P.near_plane = near_plane;
     P.far_plane = far_plane;
-    P.maps = maps;
-    P.state = state;
-    P.contributors = contributors;
+    return P;
+}
+
+int launch_forward(Params& P, int64_t images, int neural, int flags, uint64_t* counters,
+                   void* stream) {
     const int64_t tiles = images * P.tw * P.th;
     auto s = as_stream(stream);
     P.counters = reinterpret_cast<unsigned long long*>(counters);
@@ -744,6 +760,97 @@ extern "C" int gs_composite_forward(const float* records, const float* rows, int
     return GS_OK;
 }
 
+int launch_backward(Params& P, int64_t images, int neural, uint64_t* counters, void* stream) {
+    auto s = as_stream(stream);
+    const int64_t tiles = images * P.tw * P.th;
+    P.counters = reinterpret_cast<unsigned long long*>(counters);
+    const dim3 block(kTile, kTile);
+    auto launch = [&](auto kernel, size_t smem) -> int {
+        GS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     int(smem)));
+        kernel<<<unsigned(tiles), block, smem, s>>>(P);
+        return GS_OK;
+    };
+    int st;
+    if (neural && counters)
+        st = launch(composite_backward_kernel<true, true>, sizeof(BackShared<true>));
+    else if (neural)
+        st = launch(composite_backward_kernel<true, false>, sizeof(BackShared<true>));
+    else if (counters)
+        st = launch(composite_backward_kernel<false, true>, sizeof(BackShared<false>));
+    else
+        st = launch(composite_backward_kernel<false, false>, sizeof(BackShared<false>));
+    if (st) return st;
+    GS_CHECK_LAUNCH("composite_backward_kernel");
+    return GS_OK;
+}
+
+int check_backward_buffers(const char* fn, const float* state, const int32_t* contributors,
+                           const float* grad_backgrounds, int64_t records_count,
+                           const float* grad_records, const float* grad_rows) {
+    if (!state || !contributors || !grad_backgrounds ||
+        (records_count > 0 && (!grad_records || !grad_rows)))
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": NULL buffer");
+    return GS_OK;
+}
+
+}  // namespace
+}  // namespace gs
+
+extern "C" int gs_composite_forward(const float* records, const float* rows, int row_mode,
+                                    const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
+                                    int64_t records_count, int64_t rows_count,
+                                    const float* backgrounds, const int32_t* point_list,
+                                    const int32_t* ranges, int64_t images, int width, int height,
+                                    int neural, int flags, float near_plane, float far_plane,
+                                    float* maps, float* state, int32_t* contributors,
+                                    uint64_t* counters, void* stream) {
+    int st = check_composite("gs_composite_forward", records, rows, row_mode, primitive_ids, cameras,
+                             surfels, records_count, backgrounds, ranges, images, width, height);
+    if (st) return st;
+    (void)rows_count;
+    if (!maps || !state || !contributors) return fail(GS_ERR_ARGUMENT, "gs_composite_forward: NULL output");
+    Params P = common_params(records, rows, row_mode, primitive_ids, cameras, surfels, backgrounds,
+                             point_list, ranges, width, height, near_plane, far_plane);
+    for (int g = 0; g < 5; ++g) {
+        P.out[g] = maps + plane_first(g);
+        P.out_px[g] = kMaps;
+    }
+    P.state = state;
+    P.contributors = contributors;
+    return launch_forward(P, images, neural, flags, counters, stream);
+}
+
+extern "C" int gs_composite_forward_split(const float* records, const float* rows, int row_mode,
+                                          const int64_t* primitive_ids, int64_t cameras,
+                                          int64_t surfels, int64_t records_count,
+                                          int64_t rows_count, const float* backgrounds,
+                                          const int32_t* point_list, const int32_t* ranges,
+                                          int64_t images, int width, int height, int neural,
+                                          int flags, float near_plane, float far_plane,
+                                          float* const* planes, const int64_t* plane_strides,
+                                          float* state, int32_t* contributors,
+                                          uint64_t* counters, void* stream) {
+    int st = check_composite("gs_composite_forward_split", records, rows, row_mode, primitive_ids,
+                             cameras, surfels, records_count, backgrounds, ranges, images, width,
+                             height);
+    if (st) return st;
+    (void)rows_count;
+    if (!planes || !plane_strides || !state || !contributors)
+        return fail(GS_ERR_ARGUMENT, "gs_composite_forward_split: NULL output");
+    Params P = common_params(records, rows, row_mode, primitive_ids, cameras, surfels, backgrounds,
+                             point_list, ranges, width, height, near_plane, far_plane);
+    for (int g = 0; g < 5; ++g) {
+        if (!planes[g] || plane_strides[g] < plane_size(g))
+            return fail(GS_ERR_ARGUMENT, "gs_composite_forward_split: bad plane " + std::to_string(g));
+        P.out[g] = planes[g];
+        P.out_px[g] = plane_strides[g];
+    }
+    P.state = state;
+    P.contributors = contributors;
+    return launch_forward(P, images, neural, flags, counters, stream);
+}
+
 extern "C" int gs_composite_backward(const float* records, const float* rows, int row_mode,
                                      const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
                                      int64_t records_count, int64_t rows_count,
@@ -758,52 +865,63 @@ extern "C" int gs_composite_backward(const float* records, const float* rows, in
                              cameras, surfels, records_count, backgrounds, ranges, images, width,
                              height);
     if (st) return st;
-    if (!state || !contributors || !grad_maps || !grad_backgrounds ||
-        (records_count > 0 && (!grad_records || !grad_rows)))
-        return fail(GS_ERR_ARGUMENT, "gs_composite_backward: NULL buffer");
-    auto s = as_stream(stream);
     (void)rows_count;
-    Params P{};
-    P.records = reinterpret_cast<const float4*>(records);
-    P.rows = reinterpret_cast<const float4*>(rows);
-    P.row_mode = row_mode;
-    P.prim_ids = primitive_ids;
-    P.cameras = cameras;
-    P.surfels = surfels;
-    P.backgrounds = backgrounds;
-    P.point_list = point_list;
-    P.ranges = reinterpret_cast<const int2*>(ranges);
-    P.width = width;
-    P.height = height;
-    P.tw = (width + kTile - 1) / kTile;
-    P.th = (height + kTile - 1) / kTile;
-    P.near_plane = near_plane;
-    P.far_plane = far_plane;
+    if (!grad_maps) return fail(GS_ERR_ARGUMENT, "gs_composite_backward: NULL buffer");
+    st = check_backward_buffers("gs_composite_backward", state, contributors, grad_backgrounds,
+                                records_count, grad_records, grad_rows);
+    if (st) return st;
+    Params P = common_params(records, rows, row_mode, primitive_ids, cameras, surfels, backgrounds,
+                             point_list, ranges, width, height, near_plane, far_plane);
     P.state = const_cast<float*>(state);
     P.contributors = const_cast<int*>(contributors);
-    P.grad_maps = grad_maps;
+    for (int g = 0; g < 5; ++g) {
+        P.gin[g] = grad_maps + plane_first(g);
+        P.gin_px[g] = kMaps;
+        P.gin_ch[g] = 1;
+    }
     P.grad_records = grad_records;
     P.grad_xy = grad_xy;
     P.grad_rows = grad_rows;
     P.grad_backgrounds = grad_backgrounds;
-    const int64_t tiles = images * P.tw * P.th;
-    P.counters = reinterpret_cast<unsigned long long*>(counters);
-    const dim3 block(kTile, kTile);
-    auto launch = [&](auto kernel, size_t smem) -> int {
-        GS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     int(smem)));
-        kernel<<<unsigned(tiles), block, smem, s>>>(P);
-        return GS_OK;
-    };
-    if (neural && counters)
-        st = launch(composite_backward_kernel<true, true>, sizeof(BackShared<true>));
-    else if (neural)
-        st = launch(composite_backward_kernel<true, false>, sizeof(BackShared<true>));
-    else if (counters)
-        st = launch(composite_backward_kernel<false, true>, sizeof(BackShared<false>));
-    else
-        st = launch(composite_backward_kernel<false, false>, sizeof(BackShared<false>));
+    return launch_backward(P, images, neural, counters, stream);
+}
+
+extern "C" int gs_composite_backward_split(const float* records, const float* rows, int row_mode,
+                                           const int64_t* primitive_ids, int64_t cameras,
+                                           int64_t surfels, int64_t records_count,
+                                           int64_t rows_count, const float* backgrounds,
+                                           const int32_t* point_list, const int32_t* ranges,
+                                           const float* state, const int32_t* contributors,
+                                           const float* const* grad_planes,
+                                           const int64_t* grad_strides, int64_t images,
+                                           int width, int height, int neural, float near_plane,
+                                           float far_plane, float* grad_records, float* grad_xy,
+                                           float* grad_rows, float* grad_backgrounds,
+                                           uint64_t* counters, void* stream) {
+    int st = check_composite("gs_composite_backward_split", records, rows, row_mode, primitive_ids,
+                             cameras, surfels, records_count, backgrounds, ranges, images, width,
+                             height);
     if (st) return st;
-    GS_CHECK_LAUNCH("composite_backward_kernel");
-    return GS_OK;
+    (void)rows_count;
+    if (!grad_planes || !grad_strides)
+        return fail(GS_ERR_ARGUMENT, "gs_composite_backward_split: NULL buffer");
+    st = check_backward_buffers("gs_composite_backward_split", state, contributors,
+                                grad_backgrounds, records_count, grad_records, grad_rows);
+    if (st) return st;
+    Params P = common_params(records, rows, row_mode, primitive_ids, cameras, surfels, backgrounds,
+                             point_list, ranges, width, height, near_plane, far_plane);
+    P.state = const_cast<float*>(state);
+    P.contributors = const_cast<int*>(contributors);
+    for (int g = 0; g < 5; ++g) {
+        if (grad_strides[2 * g] < 0 || grad_strides[2 * g + 1] < 0)
+            return fail(GS_ERR_ARGUMENT, "gs_composite_backward_split: negative stride");
+        P.gin[g] = grad_planes[g];
+        P.gin_px[g] = grad_strides[2 * g];
+        P.gin_ch[g] = grad_strides[2 * g + 1];
+    }
+    P.grad_records = grad_records;
+    P.grad_xy = grad_xy;
+    P.grad_rows = grad_rows;
+    P.grad_backgrounds = grad_backgrounds;
+    return launch_backward(P, images, neural, counters, stream);
 }

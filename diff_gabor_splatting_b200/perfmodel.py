@@ -52,6 +52,7 @@ def count_work(fn, workload, values) -> dict:
 
 def stage_model(name: str, counts: dict, w) -> dict:
     """{'bound', 'unit', 'work' (bytes or flop per launch), 'basis'} for one entry point."""
+    name = name.removesuffix("_split")   # same kernels, maps as separate planes
     R = counts.get("records", 0)
     I = counts.get("intersections", 0)
     S, C, N = w.scenes, w.cameras, w.surfels

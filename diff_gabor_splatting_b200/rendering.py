@@ -120,6 +120,11 @@ class Projection(torch.autograd.Function):
                 g_p, None, None, None, None, None)
 
 
+# channels of the five map planes the compositor writes: rgb, alpha, accumulated depth,
+# normals, distortion (together the reference's [..][9] maps, in that order)
+PLANES = (3, 1, 1, 3, 1)
+
+
 class Composite(torch.autograd.Function):
     """Tile compositor forward/backward (rasterize.cu:229-399) over binned records.
 
@@ -127,59 +132,93 @@ class Composite(torch.autograd.Function):
     with its own point list and ranges, and the backward adds every chunk into the
     same gradient buffers.  ``projected_means`` receives the screen-centre gradient
     (record slots 9-10), so it can be inspected with ``retain_grad`` like the
-    reference's.
+    reference's.  The maps come out as the five planes of ``PLANES`` (the reference
+    slices one [..][9] array into the same five outputs): each output's gradient goes
+    to the kernel as autograd delivers it -- broadcast, strided or absent -- with no
+    [..][9] gradient assembled.
     """
 
     @staticmethod
     def forward(ctx, records, projected_means, rows, backgrounds, selected, chunks, row_mode,
                 cameras, surfels, images, width, height, neural, near_plane, far_plane):
         device = records.device
-        maps = torch.empty((images, height, width, 9), device=device, dtype=torch.float32)
+        planes = [torch.empty((images, height, width, k), device=device, dtype=torch.float32)
+                  for k in PLANES]
         state = torch.empty((images, height, width, 3), device=device, dtype=torch.float32)
         contributors = torch.empty((images, height, width), device=device, dtype=torch.int32)
         stream = nat.stream_of(device)
+        strides, strides_ptr = nat.host_array(ctypes.c_int64, PLANES)
         for ch in chunks:
             a = _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height)
-            nat.call("gs_composite_forward", a["records"], a["rows"], row_mode, None,
+            outs, outs_ptr = nat.host_array(
+                ctypes.c_void_p, [_at(t, a["pixel0"] * k) for t, k in zip(planes, PLANES)])
+            nat.call("gs_composite_forward_split", a["records"], a["rows"], row_mode, None,
                      a["cameras"], surfels, ch.record_count, a["rows_count"],
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
                      nat.ptr(ch.ranges), ch.images, width, height, int(neural),
-                     _composite_flags(), near_plane, far_plane, _at(maps, a["pixel0"] * 9),
-                     _at(state, a["pixel0"] * 3),
-                     _at(contributors, a["pixel0"]), nat.ptr(_counters("forward", device)),
-                     stream)
+                     _composite_flags(), near_plane, far_plane, outs_ptr, strides_ptr,
+                     _at(state, a["pixel0"] * 3), _at(contributors, a["pixel0"]),
+                     nat.ptr(_counters("forward", device)), stream)
         ctx.save_for_backward(records, rows, backgrounds, selected, state, contributors)
+        ctx.set_materialize_grads(False)   # an unused output's gradient stays None (zero)
         ctx.chunks = chunks
         ctx.options = (row_mode, cameras, surfels, images, width, height, neural, near_plane,
                        far_plane)
-        return maps
+        return tuple(planes)
 
     @staticmethod
     @once_differentiable
-    def backward(ctx, grad_maps):
+    def backward(ctx, *grad_planes):
         records, rows, backgrounds, selected, state, contributors = ctx.saved_tensors
         row_mode, cameras, surfels, images, width, height, neural, near_plane, far_plane = \
             ctx.options
         device = records.device
-        grad_maps = grad_maps.contiguous()
+        grads = [_pixel_linear(g, height, width) for g in grad_planes]
         g_records = torch.zeros_like(records)
         g_xy = torch.zeros((records.shape[0], 2), device=device, dtype=torch.float32)
         g_rows = torch.zeros_like(rows)
         g_bg = torch.zeros_like(backgrounds)
         stream = nat.stream_of(device)
+        strides, strides_ptr = nat.host_array(
+            ctypes.c_int64, [x for _, px, ch in grads for x in (px, ch)])
         for ch in ctx.chunks:
             a = _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height)
-            nat.call("gs_composite_backward", a["records"], a["rows"], row_mode, None,
+            ins, ins_ptr = nat.host_array(
+                ctypes.c_void_p, [None if g is None else g.data_ptr() + a["pixel0"] * px * 4
+                                  for g, px, _ in grads])
+            nat.call("gs_composite_backward_split", a["records"], a["rows"], row_mode, None,
                      a["cameras"], surfels, ch.record_count, a["rows_count"],
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
                      nat.ptr(ch.ranges), _at(state, a["pixel0"] * 3),
-                     _at(contributors, a["pixel0"]), _at(grad_maps, a["pixel0"] * 9),
-                     ch.images, width, height, int(neural), near_plane, far_plane,
+                     _at(contributors, a["pixel0"]), ins_ptr, strides_ptr, ch.images, width,
+                     height, int(neural), near_plane, far_plane,
                      _at(g_records, ch.record0 * nat.RECORD_FLOATS), _at(g_xy, ch.record0 * 2),
                      _at(g_rows, a["row0"] * rows.shape[1]), _at(g_bg, ch.image0 * 3),
                      nat.ptr(_counters("backward", device)), stream)
         g_pm = g_xy if selected is None else g_xy[selected]
         return (g_records, g_pm, g_rows, g_bg) + (None,) * 11
+
+
+def _pixel_linear(g, height, width):
+    """(tensor, pixel stride, channel stride) of a map-plane gradient [images, H, W, k].
+
+    The kernel reads element (pixel p, channel c) at p * pixel_stride + c * channel_stride,
+    which fits a contiguous gradient and a broadcast one (all strides 0, as a mean's
+    gradient arrives); any other layout is made contiguous first.  None stays None
+    (a zero gradient).
+    """
+    if g is None:
+        return None, 0, 0
+    if g.dtype != torch.float32:
+        g = g.float()
+    images, k = g.shape[0], g.shape[3]
+    s0, s1, s2, s3 = g.stride()
+    px = s2
+    fits = ((images == 1 or s0 == height * width * px) and (height == 1 or s1 == width * px))
+    if not fits:
+        g = g.contiguous()
+        px, s3 = k, 1
+    return g, px, (s3 if k > 1 else 0)
 
 
 def _at(t: torch.Tensor, offset: int) -> int | None:
@@ -583,10 +622,11 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
     if packed:
         selected = torch.nonzero(radii > 0).reshape(-1)
         projected_means = xy[selected]
-    maps = Composite.apply(records, projected_means, rows, backgrounds.reshape(-1, 3), selected,
-                           chunks, row_mode, C, max(N, 1), images, width, height, neural,
-                           float(near_plane), float(far_plane))
-    maps = maps.reshape(batch + (C, height, width, 9))
+    rgb, alpha, depth, normals, distortion = (
+        plane.reshape(batch + (C, height, width, plane.shape[-1])) for plane in Composite.apply(
+            records, projected_means, rows, backgrounds.reshape(-1, 3), selected, chunks,
+            row_mode, C, max(N, 1), images, width, height, neural, float(near_plane),
+            float(far_plane)))
     ids = selected if packed else torch.arange(P, device=device)
     meta = {
         "radii": radii[selected] if packed else radii.reshape(batch + (C, N)),
@@ -595,11 +635,11 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
         "camera_ids": ids // max(N, 1) % C,
         "primitive_ids": ids % max(N, 1),
         "packed": packed,
-        "accumulated_depth": maps[..., 4:5],
-        "normals": maps[..., 5:8],
-        "distortion": maps[..., 8:9],
+        "accumulated_depth": depth,
+        "normals": normals,
+        "distortion": distortion,
     }
-    return maps[..., :3], maps[..., 3:4], meta
+    return rgb, alpha, meta
 
 
 def rasterize_gabors(

@@ -182,6 +182,34 @@ int gs_composite_backward(const float* records, const float* rows, int row_mode,
                           float* grad_xy, float* grad_rows, float* grad_backgrounds,
                           uint64_t* counters, void* stream);
 
+/* The same compositor with the nine maps as five planes -- rgb (3 channels), alpha,
+ * depth, normals (3), distortion -- each at its own address: plane g of pixel p
+ * starts at planes[g] + p * plane_strides[g] (floats, channels adjacent).  The
+ * backward reads each plane's gradient at grad_planes[g] + p * grad_strides[2g] +
+ * k * grad_strides[2g+1] (a stride of 0 reads a broadcast value; a NULL plane is a
+ * zero gradient).  `planes`, `plane_strides`, `grad_planes` and `grad_strides` are
+ * host arrays.  No counterpart in the reference, which writes one [..][9] array and
+ * slices it: with separate planes a framework hands each output's gradient to the
+ * kernel as it is, without assembling a full [..][9] gradient. */
+int gs_composite_forward_split(const float* records, const float* rows, int row_mode,
+                               const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
+                               int64_t records_count, int64_t rows_count,
+                               const float* backgrounds, const int32_t* point_list,
+                               const int32_t* ranges, int64_t images, int width, int height,
+                               int neural, int flags, float near_plane, float far_plane,
+                               float* const* planes, const int64_t* plane_strides, float* state,
+                               int32_t* contributors, uint64_t* counters, void* stream);
+int gs_composite_backward_split(const float* records, const float* rows, int row_mode,
+                                const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
+                                int64_t records_count, int64_t rows_count,
+                                const float* backgrounds, const int32_t* point_list,
+                                const int32_t* ranges, const float* state,
+                                const int32_t* contributors, const float* const* grad_planes,
+                                const int64_t* grad_strides, int64_t images, int width,
+                                int height, int neural, float near_plane, float far_plane,
+                                float* grad_records, float* grad_xy, float* grad_rows,
+                                float* grad_backgrounds, uint64_t* counters, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Layout converters for the reference-layout entry points (the `_C` mirror).
  * gs_pack_geometry: geometry[Q][17] + opacities[primitive_ids[q]] -> records[Q][20].

@@ -330,8 +330,8 @@ def test_tight_bins_render_identically_at_benchmark_size(config, cameras, scenes
     composite_grads = []
     original = rendering.Composite.backward
 
-    def backward(ctx, grad_maps):
-        out = original(ctx, grad_maps)
+    def backward(ctx, *grad_planes):
+        out = original(ctx, *grad_planes)
         composite_grads.append(out[:3])
         return out
 
@@ -367,3 +367,41 @@ def test_tight_bins_render_identically_at_benchmark_size(config, cameras, scenes
         e = e.double()
         rel = (a - e).norm().item() / (e.norm().item() + 1e-30)
         assert rel <= 1e-5, f"{name}: relative L2 difference {rel:.2e}"
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_output_gradient_layouts_give_the_same_gradients(method):
+    """The compositor reads each output's gradient in the layout autograd delivers:
+    broadcast (a mean), contiguous (a weighted sum), or permuted (made contiguous
+    first), and absent (an unused output).  The same loss written these three ways
+    gives the same input gradients."""
+    v = random_scene(method, scenes=2, cameras=2, n=300, width=W, height=H, conditioned=True)
+    fn = rasterize_gabors if method == "classic" else rasterize_neural_gabors
+
+    def grads(loss_of):
+        values = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+        rgb, alpha, meta = fn(**values, width=W, height=H)
+        loss_of(rgb, alpha, meta).backward()
+        return {k: t.grad for k, t in values.items()}
+
+    def broadcast(rgb, alpha, meta):
+        return rgb.mean() + 0.5 * alpha.mean() + 0.01 * meta["distortion"].mean()
+
+    def weighted(rgb, alpha, meta):
+        w = torch.full_like(rgb, 1 / rgb.numel())
+        return (rgb * w).sum() + 0.5 * alpha.sum() / alpha.numel() + \
+            0.01 * meta["distortion"].sum() / meta["distortion"].numel()
+
+    def permuted(rgb, alpha, meta):
+        w = torch.full(rgb.shape[:-3] + (rgb.shape[-2], rgb.shape[-3], 3), 1 / rgb.numel(),
+                       device=rgb.device)
+        return (rgb.transpose(-2, -3) * w).sum() + 0.5 * alpha.mean() + \
+            0.01 * meta["distortion"].mean()
+
+    expected = grads(broadcast)
+    for loss in (weighted, permuted):
+        for name, g in grads(loss).items():
+            assert_grads_close(g, expected[name], name, elementwise=1e-5)
+    # a loss on depth and normals only: rgb, alpha and distortion gradients are absent
+    only = grads(lambda rgb, alpha, meta: meta["accumulated_depth"].mean() + meta["normals"].sum())
+    assert any(g.abs().max() > 0 for g in only.values())

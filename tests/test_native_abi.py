@@ -58,6 +58,25 @@ def test_invalid_arguments_fail_before_any_gpu_work():
                                      None, ctypes.c_void_p(16), 1, 8, 8, 0, 0, 0.2, 100.0,
                                      None, None, None, None, None) == 1
     assert b"row mode" in lib.gs_last_error()
+    # split-plane compositor: a missing plane or a plane stride below its channel count
+    fake = ctypes.c_void_p(16)
+    planes, planes_ptr = nat.host_array(ctypes.c_void_p, [16, 16, None, 16, 16])
+    strides, strides_ptr = nat.host_array(ctypes.c_int64, [3, 1, 1, 3, 1])
+    assert lib.gs_composite_forward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, 1,
+                                          8, 8, 0, 0, 0.2, 100.0, planes_ptr, strides_ptr, fake,
+                                          fake, None, None) == 1
+    assert b"bad plane 2" in lib.gs_last_error()
+    planes, planes_ptr = nat.host_array(ctypes.c_void_p, [16] * 5)
+    strides, strides_ptr = nat.host_array(ctypes.c_int64, [2, 1, 1, 3, 1])
+    assert lib.gs_composite_forward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, 1,
+                                          8, 8, 0, 0, 0.2, 100.0, planes_ptr, strides_ptr, fake,
+                                          fake, None, None) == 1
+    assert b"bad plane 0" in lib.gs_last_error()
+    grad_strides, grad_strides_ptr = nat.host_array(ctypes.c_int64, [3, 1, 1, 0, 1, 0, 3, -1, 1, 0])
+    assert lib.gs_composite_backward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, fake,
+                                           fake, planes_ptr, grad_strides_ptr, 1, 8, 8, 0, 0.2,
+                                           100.0, None, None, None, fake, None, None) == 1
+    assert b"negative stride" in lib.gs_last_error()
     # tiles beyond int32
     assert lib.gs_bin_sort_workspace(10, 10**10, 10, 1, 8, 8, ctypes.byref(size)) == 2
     assert lib.gs_bin_sort_workspace(10, 5, 6, 1, 8, 8, ctypes.byref(size)) == 1   # spans > slots
