@@ -87,9 +87,15 @@ __device__ __forceinline__ void add_counts(unsigned long long* counters, unsigne
 __device__ __forceinline__ int64_t row_of(const Params& P, int r) {
     if (P.row_mode == GS_ROWS_PER_RECORD) return r;
     if (P.row_mode == GS_ROWS_EXPLICIT) return P.prim_ids[r];
-    const int64_t n = r % P.surfels;
-    const int64_t s = r / (P.surfels * P.cameras);
-    return s * P.surfels + n;
+    // r < 2^31 (int32 point lists), so 32-bit unsigned division suffices whenever the
+    // divisors fit; a scene (surfels x cameras) beyond 2^32 records takes the 64-bit path
+    const int64_t per_scene = P.surfels * P.cameras;
+    if (per_scene <= 0xffffffffLL) {
+        const unsigned u = unsigned(r), n = u % unsigned(P.surfels);
+        const unsigned s = u / unsigned(per_scene);
+        return int64_t(s) * P.surfels + n;
+    }
+    return (r / per_scene) * P.surfels + r % P.surfels;
 }
 
 // Squared local radius beyond which a sample of opacity o is certainly below the
@@ -105,6 +111,7 @@ template <bool Neural, int kSize = kBatch>
 struct Batch {
     static constexpr int kRow = Neural ? kNeuralRow : kClassicRow;
     static constexpr bool kNeural = Neural;
+    static constexpr int kCapacity = kSize;
     int ids[kSize];
     int64_t rows[kSize];
     float4 geo[kSize][kRec / 4];
@@ -119,30 +126,31 @@ struct Batch {
 // float product the per-sample expression 2 * pi * magnitude rounds to).
 template <class B>
 __device__ __forceinline__ void load_batch(B& b, const Params& P, int first, int stride,
-                                           int count, int rank) {
+                                           int count, int rank, unsigned* reset = nullptr) {
     constexpr int kRow = B::kRow;
     constexpr int kPer = kRec / 4 + kRow / 4;
-    __syncthreads();
-    if (rank < count) {
-        const int id = P.point_list[first + stride * rank];
-        b.ids[rank] = id;
-        b.rows[rank] = row_of(P, id);
-    }
-    __syncthreads();
+    __syncthreads();   // the previous batch is no longer read
+    // each loading thread reads its record id (L1-cached), so ids need no barrier of
+    // their own; the part-0 thread keeps it for the kernels' gradient writes
+    if (reset && rank < B::kCapacity) reset[rank] = 0u;   // reset[] has one entry per slot
     for (int i = rank; i < count * kPer; i += kBlock) {
         const int e = i / kPer, part = i % kPer;
+        const int id = __ldg(P.point_list + first + stride * e);
         if (part < kRec / 4) {
-            float4 v = __ldg(P.records + int64_t(b.ids[e]) * (kRec / 4) + part);
+            if (part == 0) b.ids[e] = id;
+            float4 v = __ldg(P.records + int64_t(id) * (kRec / 4) + part);
             // slot 18 (pad in memory) <- rejection threshold of this record's opacity
             if (part == 4) v.z = reject_threshold(v.y);
             b.geo[e][part] = v;
         } else {
             const int q = part - kRec / 4;
-            float4 v = __ldg(P.rows + b.rows[e] * (kRow / 4) + q);
+            const int64_t row = row_of(P, id);
+            if (q == 0) b.rows[e] = row;
+            float4 v = __ldg(P.rows + row * (kRow / 4) + q);
             if constexpr (!B::kNeural) {
                 constexpr float kTwoPi = 2 * kPi;
                 if (q == 2) {   // weights 2-3, magnitudes 0-1
-                    const float4 w01 = __ldg(P.rows + b.rows[e] * (kRow / 4) + 1);
+                    const float4 w01 = __ldg(P.rows + row * (kRow / 4) + 1);
                     b.half_weight[e] = 0.5f * ((w01.z + w01.w) + (v.x + v.y));
                     v.z = kTwoPi * v.z;
                     v.w = kTwoPi * v.w;
@@ -495,9 +503,8 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     const float background_term = final_t * (go[3] - background_dot);  // galpha's T-independent part
     for (int start = block_last; start > 0; start -= kBackBatch) {
         const int count = min(kBackBatch, start);
-        __syncthreads();   // every thread has finished the previous batch's flush
-        if (rank < kBackBatch) sh.mask[rank] = 0u;
-        load_batch(batch, P, range.x + start - 1, -1, count, rank);
+        // masks reset after the barrier that ends the previous batch's flush
+        load_batch(batch, P, range.x + start - 1, -1, count, rank, sh.mask);
         for (int j = 0; j < count; ++j) {
             const float* g = reinterpret_cast<const float*>(batch.geo[j]);
             const float* a = reinterpret_cast<const float*>(batch.app[j]);
