@@ -261,16 +261,6 @@ __global__ void spans_kernel(int64_t R, const float* __restrict__ records, int s
     }
 }
 
-__device__ __forceinline__ int64_t first_above(const int64_t* __restrict__ offsets, int64_t n,
-                                               int64_t value) {
-    int64_t lo = 0, hi = n - 1;   // first j with offsets[j] > value (offsets[n-1] > value)
-    while (lo < hi) {
-        const int64_t mid = (lo + hi) >> 1;
-        if (offsets[mid] > value) hi = mid; else lo = mid + 1;
-    }
-    return lo;
-}
-
 // first_owner[b] = the span owning slot b * kExpandSlots: each span writes the entries
 // of the blocks whose first slot falls in its slot range.
 __global__ void first_owner_kernel(int64_t S, int64_t blocks, const int64_t* __restrict__ item_end,

@@ -375,7 +375,6 @@ struct Fields {
     static constexpr int kGeo = Neural ? 17 : 14;
     static constexpr int kRow = Neural ? 57 : 18;
     static constexpr int kCount = kGeo + 1 + kRow;            // 33 classic, 75 neural
-    static constexpr int kSlots = kRec + (Neural ? kNeuralRow : kClassicRow);   // 40 / 80
     // packed field -> accumulator slot (record slots 0-19, row slots 20+)
     static __device__ __forceinline__ int slot(int i) {
         return i < kGeo ? i : (i == kGeo ? 17 : kRec + (i - kGeo - 1));
