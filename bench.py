@@ -224,8 +224,13 @@ def roofline(stage_ms, counts, w, steps, calls_per_step):
     model = perfmodel.stage_model(name, counts, w)
     work = model["work"] * calls_per_step * steps
     data, source = peaks()
+    dram = perfmodel.traffic(name, counts)
     out = {"kernel": name, "launches": launches, "ms_per_launch": total_ms / max(launches, 1),
-           "bound": model["bound"], "unit": model["unit"], "traffic": None}
+           "bound": model["bound"], "unit": model["unit"],
+           "traffic": dram * calls_per_step * steps / max(launches, 1) if dram else None}
+    if dram:
+        out["traffic_basis"] = ("DRAM read+write bytes of one ncu-profiled small-case launch, "
+                                "scaled by accepted samples")
     if model["bound"] == "hbm":
         achieved = work / (total_ms * 1e-3) / 1e9
         peak = data["hbm_gbs"]

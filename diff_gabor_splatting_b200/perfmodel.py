@@ -25,6 +25,28 @@ ACCEPT_FLOP = {"classic": 100, "neural": 156}
 BACKWARD_ACCEPT_FLOP = {"classic": 400, "neural": 520}
 
 
+# DRAM bytes (read + write) of one launch measured with ncu on the config-1 small case
+# (N=100k, 1 camera; profiles/composite_kernels_config1_small.md) and the accepted
+# samples of that launch.  A full-size launch is estimated by scaling with its own
+# accepted samples (the compositors' DRAM traffic is the record batches, gradient
+# atomics and pixel buffers, all of which grow with the accepted work).
+PROFILED_TRAFFIC = {
+    "gs_composite_forward": (12.000512e6 + 53.144832e6, 130426868),
+    "gs_composite_backward": (88.055040e6 + 4.032512e6, 130426868),
+}
+
+
+def traffic(name: str, counts: dict):
+    """Estimated DRAM bytes per launch of ``name`` (None when not profiled)."""
+    name = name.removesuffix("_split")
+    if name not in PROFILED_TRAFFIC:
+        return None
+    stage = "forward" if name.endswith("forward") else "backward"
+    accepts = counts.get(f"{stage}_accepts", 0)
+    bytes_small, accepts_small = PROFILED_TRAFFIC[name]
+    return bytes_small * accepts / accepts_small
+
+
 def count_work(fn, workload, values) -> dict:
     """Run one render + backward with the kernels' counters on; return event counts."""
     from . import rendering
