@@ -45,7 +45,8 @@ OWN_KERNELS = {"gs_project_forward": 1, "gs_project_backward": 1, "gs_bin_count"
                "gs_bin_sort": 4, "gs_composite_forward": 1, "gs_composite_backward": 1,
                "gs_composite_forward_split": 1, "gs_composite_backward_split": 1,
                "gs_sh_forward": 1, "gs_sh_backward": 1, "gs_pack_geometry": 1,
-               "gs_pack_rows": 1, "gs_unpack_geometry_grads": 1, "gs_unpack_rows": 1}
+               "gs_pack_rows": 1, "gs_unpack_geometry_grads": 1, "gs_unpack_rows": 1,
+               "gs_adam_step": 1}
 
 
 def parse():
@@ -61,6 +62,10 @@ def parse():
     p.add_argument("--surfels", type=int, default=None, help="override N (profiling cases)")
     p.add_argument("--cameras", type=int, default=None, help="override C (profiling cases)")
     p.add_argument("--scenes", type=int, default=None, help="override S (profiling cases)")
+    p.add_argument("--optimizer", choices=["none", "fused", "torch"], default="none",
+                   help="add an Adam step (lr 1e-3) over every parameter to each step: this\n"
+                        "build's fused kernel or torch.optim.Adam (the reference's loop);\n"
+                        "reported under 'optimizer' (the e2e leg is skipped)")
     p.add_argument("--split-cameras", action="store_true",
                    help="shard one workload over the ranks, splitting a scene's cameras "
                         "(gradient all-reduce) when there are more ranks than scenes")
@@ -171,9 +176,44 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def step(fn, job, calls):
-    """Render every call of this rank, backward with the batch-mean loss, and sum
-    parameter gradients over the camera-split group when the scene is split."""
+class OptimizerStep:
+    """The optional Adam step of a training step, timed with CUDA events."""
+
+    def __init__(self, kind, calls):
+        from diff_gabor_splatting_b200.optim import FusedAdam
+
+        self.kind = kind
+        self.params = [t for c in calls for t in c.values() if t.requires_grad]
+        cls = FusedAdam if kind == "fused" else torch.optim.Adam
+        self.optimizer = cls(self.params, lr=1e-3)
+        self.events = []
+        self.timing = False
+
+    def __call__(self):
+        if self.timing:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            self.optimizer.step()
+            end.record()
+            self.events.append((start, end))
+        else:
+            self.optimizer.step()
+
+    def summary(self, steps, hbm_gbs):
+        ms = sum(a.elapsed_time(b) for a, b in self.events) / max(len(self.events), 1)
+        numel = sum(t.numel() for t in self.params)
+        moved = 28 * numel   # read p, g, m, v; write p, m, v (float32)
+        gbs = moved / (ms * 1e-3) / 1e9
+        return {"impl": "fused gs_adam_step" if self.kind == "fused" else "torch.optim.Adam",
+                "params": numel, "tensors": len(self.params), "ms_per_step": ms,
+                "bytes_per_step": moved, "achieved_gbs": gbs, "peak_gbs": hbm_gbs,
+                "frac": gbs / hbm_gbs}
+
+
+def step(fn, job, calls, optimizer=None):
+    """Render every call of this rank, backward with the batch-mean loss, sum parameter
+    gradients over the camera-split group when the scene is split, and take the
+    optional optimizer step."""
     w = job.workload
     total = None
     for values in calls:
@@ -188,6 +228,8 @@ def step(fn, job, calls):
         for values in calls:
             params = [t for k, t in values.items() if k not in job.sharding.PER_CAMERA]
             job.sharding.allreduce_gradients(params, job.groups[job.shard.group_ranks])
+    if optimizer is not None:
+        optimizer()
     return total
 
 
@@ -327,8 +369,9 @@ def main():
     w = job.workload
     fn = rasterize_gabors if w.method == "classic" else rasterize_neural_gabors
     calls = job.inputs_on(device)
+    opt = OptimizerStep(args.optimizer, calls) if args.optimizer != "none" else None
     for _ in range(max(args.warmup, 3)):
-        step(fn, job, calls)
+        step(fn, job, calls, opt)
     torch.cuda.synchronize()
     counts = perfmodel.count_work(fn, w, calls[0])
     # timed region: K steps, inputs resident in HBM
@@ -336,9 +379,11 @@ def main():
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks, nat.StageTimer() as timer:
+        if opt is not None:
+            opt.timing = True
         start.record()
         for _ in range(args.steps):
-            step(fn, job, calls)
+            step(fn, job, calls, opt)
         end.record()
         torch.cuda.synchronize()
     barrier(world)
@@ -350,7 +395,7 @@ def main():
     value = pixels_all * args.steps / (ms * 1e-3) / 1e6
     # end to end: host (pinned) inputs copied in every step, loss read back
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and opt is None:
         host = [{k: v.pin_memory() for k, v in c.items()} for c in job.calls]
         h2d = sum(v.numel() * v.element_size() for c in host for v in c.values())
 
@@ -391,6 +436,9 @@ def main():
                 "roofline": roofline(stage, counts, w, args.steps, len(job.calls)),
                 "stages_ms_per_step": {k: v[1] / args.steps for k, v in stage.items()},
                 "work": counts, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary()}
+        if opt is not None:
+            line["optimizer"] = opt.summary(args.steps, peaks()[0]["hbm_gbs"])
+            line["config"]["step"] = "render + backward + Adam step (lr 1e-3) on every parameter"
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -19,7 +19,7 @@ from pathlib import Path
 
 PACKAGE = Path(__file__).resolve().parent
 ROOT = PACKAGE.parent
-SOURCES = ["capi.cu", "project.cu", "sh.cu", "binning.cu", "composite.cu"]
+SOURCES = ["capi.cu", "project.cu", "sh.cu", "binning.cu", "composite.cu", "adam.cu"]
 LIBRARY = PACKAGE / "libgabor_b200.so"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",

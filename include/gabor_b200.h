@@ -211,6 +211,21 @@ int gs_composite_backward_split(const float* records, const float* rows, int row
                                 float* grad_backgrounds, uint64_t* counters, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Fused Adam step.  Replaces torch.optim.Adam.step() in the reference's optimisation
+ * loop (examples/fit_texture.py:50-61; torch/optim/adam.py _multi_tensor_adam):
+ * for every tensor t with sizes[t] float32 elements, p += -(lr / (1 - beta1^step)) *
+ * m / (sqrt(v) / sqrt(1 - beta2^step) + eps) after m = lerp(m, g + wd p, 1 - beta1) and
+ * v = beta2 v + (1 - beta2) (g + wd p)^2, in one launch per 48 tensors.  The pointer
+ * arrays and sizes are host arrays; all device arrays are contiguous.  `step` is the
+ * step number after this update (1 for the first).  No counterpart in the reference's
+ * native module.
+ */
+int gs_adam_step(int tensors, float* const* params, const float* const* grads,
+                 float* const* exp_avgs, float* const* exp_avg_sqs, const int64_t* sizes,
+                 double lr, double beta1, double beta2, double eps, double weight_decay,
+                 int64_t step, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Layout converters for the reference-layout entry points (the `_C` mirror).
  * gs_pack_geometry: geometry[Q][17] + opacities[primitive_ids[q]] -> records[Q][20].
  * gs_pack_rows:     appearance[A][width] (18 or 57) -> rows[A][20 or 60].
