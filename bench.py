@@ -46,7 +46,7 @@ OWN_KERNELS = {"gs_project_forward": 1, "gs_project_backward": 1, "gs_bin_count"
                "gs_composite_forward_split": 1, "gs_composite_backward_split": 1,
                "gs_sh_forward": 1, "gs_sh_backward": 1, "gs_pack_geometry": 1,
                "gs_pack_rows": 1, "gs_unpack_geometry_grads": 1, "gs_unpack_rows": 1,
-               "gs_adam_step": 1}
+               "gs_adam_step": 1, "gs_bin_arena": 6}
 
 
 def parse():
@@ -66,6 +66,9 @@ def parse():
                    help="add an Adam step (lr 1e-3) over every parameter to each step: this\n"
                         "build's fused kernel or torch.optim.Adam (the reference's loop);\n"
                         "reported under 'optimizer' (the e2e leg is skipped)")
+    p.add_argument("--graph", action="store_true",
+                   help="also time the step captured as one CUDA graph (arena binning, no\n"
+                        "host sync): reported under 'graph' beside the eager value")
     p.add_argument("--split-cameras", action="store_true",
                    help="shard one workload over the ranks, splitting a scene's cameras "
                         "(gradient all-reduce) when there are more ranks than scenes")
@@ -419,6 +422,7 @@ def main():
         e2e = {"value": pixels_all * args.steps / (ems * 1e-3) / 1e6, "unit": "Mpix/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                "ms_per_step": ems / args.steps}
+    graph = graph_leg(args, job, fn, calls, device, world, pixels_all) if args.graph else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cores = os.cpu_count() or 1
@@ -436,12 +440,72 @@ def main():
                 "roofline": roofline(stage, counts, w, args.steps, len(job.calls)),
                 "stages_ms_per_step": {k: v[1] / args.steps for k, v in stage.items()},
                 "work": counts, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary()}
+        if graph is not None:
+            line["graph"] = graph
         if opt is not None:
             line["optimizer"] = opt.summary(args.steps, peaks()[0]["hbm_gbs"])
             line["config"]["step"] = "render + backward + Adam step (lr 1e-3) on every parameter"
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def graph_leg(args, job, fn, calls, device, world, pixels_all):
+    """The same step as one CUDA graph replay (``GraphedStep``: arena binning sized 1.25x
+    the live counts, no host synchronisation), timed like the eager loop, plus its
+    end-to-end form (host inputs copied into the captured tensors, loss read back)."""
+    from diff_gabor_splatting_b200.graphs import GraphedStep
+
+    if len(calls) != 1 or (job.shard is not None and job.shard.split):
+        return {"unavailable": "graph leg needs one render call per rank and no camera split"}
+    w = job.workload
+    static = calls[0]
+    # packing counts visible pairs on the host; images and gradients are the same dense
+    step_graph = GraphedStep(fn, static,
+                             lambda rgb, alpha, meta: loss_of(rgb, alpha, meta,
+                                                              w.depth_normal_loss),
+                             **dict(w.kwargs(), packed=False))
+    for _ in range(3):
+        step_graph.replay()
+    barrier(world)
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(args.steps):
+        step_graph.replay()
+    g1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    gms = max_over_ranks(g0.elapsed_time(g1), world, device)
+    out = {"value": pixels_all * args.steps / (gms * 1e-3) / 1e6, "unit": "Mpix/s",
+           "ms_per_step": gms / args.steps, "overflow": step_graph.arena.overflowed(),
+           "arena": [step_graph.arena.max_intersections, step_graph.arena.max_spans],
+           "packed": False}
+    host = {k: v.detach().cpu().pin_memory() for k, v in static.items()}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+
+    def e2e_replay():
+        with torch.no_grad():
+            for k, v in host.items():
+                static[k].copy_(v, non_blocking=True)
+        return step_graph.replay().item()
+
+    for _ in range(2):
+        e2e_replay()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_replay()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ems = max_over_ranks(e0.elapsed_time(e1), world, device)
+    out["e2e"] = {"value": pixels_all * args.steps / (ems * 1e-3) / 1e6, "unit": "Mpix/s",
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                  "ms_per_step": ems / args.steps}
+    return out
 
 
 def parallelism(job, world):

@@ -33,6 +33,8 @@ SIGNATURES = {
                      ctypes.POINTER(_l), _p],
     "gs_bin_sort_workspace": [_l, _l, _l, _l, _i, _i, ctypes.POINTER(_sz)],
     "gs_bin_sort": [_p, _i, _p, _p, _l, _l, _l, _i, _i, _i, _p, _sz, _p, _sz, _l, _l, _p, _p, _p],
+    "gs_bin_arena_workspace": [_l, _l, _l, _l, _i, _i, ctypes.POINTER(_sz)],
+    "gs_bin_arena": [_p, _i, _p, _p, _l, _l, _l, _i, _i, _i, _p, _sz, _l, _l, _p, _p, _p, _p],
     "gs_composite_forward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _l, _i, _i, _i, _i, _f,
                              _f, _p, _p, _p, _p, _p],
     "gs_composite_backward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _p, _p, _p, _l, _i, _i,

@@ -238,10 +238,11 @@ __global__ void spans_kernel(int64_t R, const float* __restrict__ records, int s
                              const int64_t* __restrict__ slot_end,
                              const int64_t* __restrict__ span_end,
                              const int64_t* __restrict__ image_ids, int64_t per_image, int tw,
-                             int th, bool tight, int64_t* __restrict__ item_end,
-                             uint32_t* __restrict__ item_tile, int* __restrict__ item_record) {
+                             int th, bool tight, const int64_t* __restrict__ limits,
+                             int64_t* __restrict__ item_end, uint32_t* __restrict__ item_tile,
+                             int* __restrict__ item_record) {
     const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= R) return;
+    if (i >= R || (limits && limits[1] == 0)) return;   // arena overflow: no spans
     const int64_t first_span = i ? span_end[i - 1] : 0;
     if (span_end[i] == first_span) return;
     const int r = order[i];
@@ -263,9 +264,16 @@ __global__ void spans_kernel(int64_t R, const float* __restrict__ records, int s
 
 // first_owner[b] = the span owning slot b * kExpandSlots: each span writes the entries
 // of the blocks whose first slot falls in its slot range.
-__global__ void first_owner_kernel(int64_t S, int64_t blocks, const int64_t* __restrict__ item_end,
+// limits (arena mode, else NULL): device [intersections, spans] of this binning, zero
+// when they exceed the arena; I and S are then the arena capacities.
+__global__ void first_owner_kernel(int64_t S, int64_t blocks, const int64_t* __restrict__ limits,
+                                   const int64_t* __restrict__ item_end,
                                    int64_t* __restrict__ first_owner) {
     const int64_t j = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (limits) {
+        S = limits[1];
+        blocks = (limits[0] + kExpandSlots - 1) / kExpandSlots;
+    }
     if (j >= S) return;
     const int64_t begin = j ? item_end[j - 1] : 0, end = item_end[j];
     for (int64_t b = (begin + kExpandSlots - 1) / kExpandSlots; b * kExpandSlots < end && b < blocks;
@@ -277,16 +285,30 @@ __global__ void first_owner_kernel(int64_t S, int64_t blocks, const int64_t* __r
 // slots and the spans covering them (at most 1024: every span holds a slot); it stages
 // their end slots, first tiles and records in shared memory, and each slot finds its
 // span by a shared binary search.  Writes are coalesced.
+// Arena mode (limits non-NULL): I is the arena capacity; slots from the live count up to
+// it get the last tile's id as a pad key, which the stable tile sort keeps behind every
+// real entry of that tile, past the live count the ranges are built from.
 __global__ __launch_bounds__(kBinThreads) void expand_kernel(
-    int64_t I, int64_t S, const int64_t* __restrict__ item_end,
-    const uint32_t* __restrict__ item_tile, const int* __restrict__ item_record,
-    const int64_t* __restrict__ first_owner, uint32_t* __restrict__ tile_keys,
-    int* __restrict__ values) {
+    int64_t I, int64_t S, const int64_t* __restrict__ limits, uint32_t pad_key,
+    const int64_t* __restrict__ item_end, const uint32_t* __restrict__ item_tile,
+    const int* __restrict__ item_record, const int64_t* __restrict__ first_owner,
+    uint32_t* __restrict__ tile_keys, int* __restrict__ values) {
     __shared__ int64_t s_end[kExpandSlots];
     __shared__ uint32_t s_tile[kExpandSlots];
     __shared__ int s_record[kExpandSlots];
     __shared__ int64_t s_first, s_last;
     const int64_t i0 = int64_t(blockIdx.x) * kExpandSlots;
+    if (limits) {
+        const int64_t capacity = I;
+        I = limits[0];
+        S = limits[1];
+        for (int64_t i = max(i0, I) + threadIdx.x; i < min(i0 + kExpandSlots, capacity);
+             i += kBinThreads) {
+            tile_keys[i] = pad_key;
+            values[i] = -1;
+        }
+        if (i0 >= I) return;
+    }
     const int64_t i1 = min(i0 + kExpandSlots, I) - 1;
     if (threadIdx.x == 0) s_first = first_owner[blockIdx.x];
     if (threadIdx.x == 32) {
@@ -326,7 +348,9 @@ __global__ __launch_bounds__(kBinThreads) void expand_kernel(
 // thread reads four consecutive ids with one 16-byte load plus the id before them.
 constexpr int kRangeItems = 4;
 
-__global__ void ranges_kernel(int64_t I, const uint32_t* __restrict__ keys, int2* __restrict__ ranges) {
+__global__ void ranges_kernel(int64_t I, const int64_t* __restrict__ limits,
+                              const uint32_t* __restrict__ keys, int2* __restrict__ ranges) {
+    if (limits) I = limits[0];   // arena: the live entries lead the sorted keys
     const int64_t i0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * kRangeItems;
     if (i0 >= I) return;
     uint32_t t[kRangeItems + 1];
@@ -381,6 +405,109 @@ extern "C" int gs_bin_count_workspace(int64_t records, size_t* bytes) {
     return GS_OK;
 }
 
+namespace gs {
+namespace {
+
+// Depth pre-sort, per-record tile and span counts, and their inclusive scans, into
+// workspace 1 (asynchronous: the totals stay on the device at slot_end/span_end[R-1]).
+int count_phase(const char* fn, const float* records, int record_stride, const int32_t* radii,
+                int64_t R, bool tight, int width, int height, void* workspace1,
+                size_t workspace1_bytes, cudaStream_t s) {
+    const CountLayout L = count_layout(R);
+    if (!workspace1 || workspace1_bytes < L.total)
+        return fail(GS_ERR_WORKSPACE, std::string(fn) + ": workspace too small");
+    auto* base = static_cast<char*>(workspace1);
+    auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
+    auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
+    auto* idx_in = reinterpret_cast<int*>(base + L.idx_in);
+    auto* idx_out = reinterpret_cast<int*>(base + L.idx_out);
+    auto* slots = reinterpret_cast<int64_t*>(base + L.slots);
+    auto* slot_end = reinterpret_cast<int64_t*>(base + L.slot_end);
+    auto* n_spans = reinterpret_cast<int64_t*>(base + L.spans);
+    auto* span_end = reinterpret_cast<int64_t*>(base + L.span_end);
+    void* temp = base + L.temp;
+    const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    depth_keys_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
+                                                            keys_in, idx_in);
+    GS_CHECK_LAUNCH("depth_keys_kernel");
+    size_t temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx_in, idx_out,
+                                            int(R), 0, 32, s));
+    tile_counts_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
+                                                             idx_out, tw, th, tight, slots, n_spans);
+    GS_CHECK_LAUNCH("tile_counts_kernel");
+    temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, slots, slot_end, int(R), s));
+    temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, n_spans, span_end, int(R), s));
+    return GS_OK;
+}
+
+// Spans, first-owner table, expansion, tile sort and ranges into workspace 2,
+// point_list and ranges.  I and S are the intersection and span counts, or with
+// `limits` (arena mode) the arena capacities, the live counts being read on the device.
+int sort_phase(const float* records, int record_stride, const int32_t* radii,
+               const int64_t* image_ids, int64_t R, int64_t records_per_image, int64_t images,
+               int width, int height, bool tight, const void* workspace1, void* workspace2,
+               int64_t I, int64_t spans, const int64_t* limits, int32_t* point_list,
+               int32_t* ranges, cudaStream_t s) {
+    const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    const int64_t n_tiles = images * tw * th;
+    const CountLayout C = count_layout(R);
+    const SortLayout L = sort_layout(I, spans, n_tiles);
+    const auto* base1 = static_cast<const char*>(workspace1);
+    const auto* order = reinterpret_cast<const int*>(base1 + C.idx_out);
+    const auto* slot_end = reinterpret_cast<const int64_t*>(base1 + C.slot_end);
+    const auto* span_end = reinterpret_cast<const int64_t*>(base1 + C.span_end);
+    auto* base = static_cast<char*>(workspace2);
+    auto* item_end = reinterpret_cast<int64_t*>(base + L.item_end);
+    auto* item_tile = reinterpret_cast<uint32_t*>(base + L.item_tile);
+    auto* item_record = reinterpret_cast<int*>(base + L.item_record);
+    auto* owners = reinterpret_cast<int64_t*>(base + L.owners);
+    auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
+    auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
+    auto* vals_in = reinterpret_cast<int*>(base + L.vals_in);
+    void* temp = base + L.temp;
+    spans_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii, order,
+                                                       slot_end, span_end, image_ids,
+                                                       records_per_image, tw, th, tight, limits,
+                                                       item_end, item_tile, item_record);
+    GS_CHECK_LAUNCH("spans_kernel");
+    const int64_t expand_blocks = (I + kExpandSlots - 1) / kExpandSlots;
+    first_owner_kernel<<<blocks_for(spans), kBinThreads, 0, s>>>(spans, expand_blocks, limits,
+                                                                 item_end, owners);
+    GS_CHECK_LAUNCH("first_owner_kernel");
+    expand_kernel<<<unsigned(expand_blocks), kBinThreads, 0, s>>>(
+        I, spans, limits, uint32_t(n_tiles - 1), item_end, item_tile, item_record, owners, keys_in,
+        vals_in);
+    GS_CHECK_LAUNCH("expand_kernel");
+    size_t temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, point_list,
+                                            int(I), 0, tile_bits(n_tiles), s));
+    ranges_kernel<<<blocks_for((I + kRangeItems - 1) / kRangeItems), kBinThreads, 0, s>>>(
+        I, limits, keys_out, reinterpret_cast<int2*>(ranges));
+    GS_CHECK_LAUNCH("ranges_kernel");
+    return GS_OK;
+}
+
+// Arena mode: report the live counts and zero them when they exceed the arena.
+__global__ void arena_limits_kernel(int64_t R, const int64_t* __restrict__ slot_end,
+                                    const int64_t* __restrict__ span_end, int64_t max_slots,
+                                    int64_t max_spans, int64_t* __restrict__ totals,
+                                    int64_t* __restrict__ limits) {
+    const int64_t I = R ? slot_end[R - 1] : 0, S = R ? span_end[R - 1] : 0;
+    if (totals) {
+        totals[0] = I;
+        totals[1] = S;
+    }
+    const bool fits = I <= max_slots && S <= max_spans;
+    limits[0] = fits ? I : 0;
+    limits[1] = fits ? S : 0;
+}
+
+}  // namespace
+}  // namespace gs
+
 extern "C" int gs_bin_count(const float* records, int record_stride, const int32_t* radii,
                             const int64_t* image_ids, int64_t R, int64_t records_per_image,
                             int64_t images, int width, int height, int flags, void* workspace1,
@@ -398,34 +525,14 @@ extern "C" int gs_bin_count(const float* records, int record_stride, const int32
     if (R == 0) return GS_OK;
     if (!image_ids && records_per_image < 1)
         return fail(GS_ERR_ARGUMENT, "gs_bin_count: records_per_image must be positive without image_ids");
-    const CountLayout L = count_layout(R);
-    if (!workspace1 || workspace1_bytes < L.total)
-        return fail(GS_ERR_WORKSPACE, "gs_bin_count: workspace too small");
-    auto* base = static_cast<char*>(workspace1);
-    auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
-    auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
-    auto* idx_in = reinterpret_cast<int*>(base + L.idx_in);
-    auto* idx_out = reinterpret_cast<int*>(base + L.idx_out);
-    auto* slots = reinterpret_cast<int64_t*>(base + L.slots);
-    auto* slot_end = reinterpret_cast<int64_t*>(base + L.slot_end);
-    auto* n_spans = reinterpret_cast<int64_t*>(base + L.spans);
-    auto* span_end = reinterpret_cast<int64_t*>(base + L.span_end);
-    void* temp = base + L.temp;
     auto s = as_stream(stream);
-    const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
-    depth_keys_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
-                                                            keys_in, idx_in);
-    GS_CHECK_LAUNCH("depth_keys_kernel");
-    size_t temp_bytes = L.temp_bytes;
-    GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx_in, idx_out,
-                                            int(R), 0, 32, s));
-    tile_counts_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
-                                                             idx_out, tw, th, tight, slots, n_spans);
-    GS_CHECK_LAUNCH("tile_counts_kernel");
-    temp_bytes = L.temp_bytes;
-    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, slots, slot_end, int(R), s));
-    temp_bytes = L.temp_bytes;
-    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, n_spans, span_end, int(R), s));
+    st = count_phase("gs_bin_count", records, record_stride, radii, R, tight, width, height,
+                     workspace1, workspace1_bytes, s);
+    if (st) return st;
+    const CountLayout L = count_layout(R);
+    const auto* base = static_cast<const char*>(workspace1);
+    const auto* slot_end = reinterpret_cast<const int64_t*>(base + L.slot_end);
+    const auto* span_end = reinterpret_cast<const int64_t*>(base + L.span_end);
     int64_t totals[2] = {0, 0};
     GS_CUDA(cudaMemcpyAsync(&totals[0], slot_end + R - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
     GS_CUDA(cudaMemcpyAsync(&totals[1], span_end + R - 1, sizeof(int64_t), cudaMemcpyDeviceToHost, s));
@@ -477,39 +584,96 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
     const SortLayout L = sort_layout(I, spans, n_tiles);
     if (!workspace2 || workspace2_bytes < L.total)
         return fail(GS_ERR_WORKSPACE, "gs_bin_sort: workspace 2 too small");
-    const auto* base1 = static_cast<const char*>(workspace1);
-    const auto* order = reinterpret_cast<const int*>(base1 + C.idx_out);
-    const auto* slot_end = reinterpret_cast<const int64_t*>(base1 + C.slot_end);
-    const auto* span_end = reinterpret_cast<const int64_t*>(base1 + C.span_end);
-    auto* base = static_cast<char*>(workspace2);
-    auto* item_end = reinterpret_cast<int64_t*>(base + L.item_end);
-    auto* item_tile = reinterpret_cast<uint32_t*>(base + L.item_tile);
-    auto* item_record = reinterpret_cast<int*>(base + L.item_record);
-    auto* owners = reinterpret_cast<int64_t*>(base + L.owners);
-    auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
-    auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
-    auto* vals_in = reinterpret_cast<int*>(base + L.vals_in);
-    void* temp = base + L.temp;
-    spans_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii, order,
-                                                       slot_end, span_end, image_ids,
-                                                       records_per_image, tw, th, tight, item_end,
-                                                       item_tile, item_record);
-    GS_CHECK_LAUNCH("spans_kernel");
-    const int64_t expand_blocks = (I + kExpandSlots - 1) / kExpandSlots;
-    first_owner_kernel<<<blocks_for(spans), kBinThreads, 0, s>>>(spans, expand_blocks, item_end,
-                                                                 owners);
-    GS_CHECK_LAUNCH("first_owner_kernel");
-    expand_kernel<<<unsigned(expand_blocks), kBinThreads, 0, s>>>(I, spans, item_end, item_tile,
-                                                                  item_record, owners, keys_in,
-                                                                  vals_in);
-    GS_CHECK_LAUNCH("expand_kernel");
-    size_t temp_bytes = L.temp_bytes;
-    GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, vals_in, point_list,
-                                            int(I), 0, tile_bits(n_tiles), s));
-    ranges_kernel<<<blocks_for((I + kRangeItems - 1) / kRangeItems), kBinThreads, 0, s>>>(
-        I, keys_out, reinterpret_cast<int2*>(ranges));
-    GS_CHECK_LAUNCH("ranges_kernel");
+    return sort_phase(records, record_stride, radii, image_ids, R, records_per_image, images, width,
+                      height, tight, workspace1, workspace2, I, spans, nullptr, point_list, ranges,
+                      s);
+}
+
+// ------------------------------------------------------------------------------
+// gs_bin_arena: binning without a host synchronisation.
+//
+// gs_bin_count reads the intersection and span counts back to the host to size the
+// sort (the reference does the same, rasterize.cu:466-468), which stalls the host and
+// keeps a render step out of CUDA graph capture.  Here the caller provides an arena
+// sized for at most max_intersections slots and max_spans row spans; every launch is
+// sized by those capacities and reads the live counts on the device.  Slots past the
+// live count carry a pad key the stable sort keeps at the end.  When a count exceeds
+// the arena nothing is binned (all tile ranges empty) and `totals` reports the counts
+// needed, for the caller to check after the fact and grow the arena.
+// ------------------------------------------------------------------------------
+namespace {
+
+struct ArenaLayout {
+    size_t count, sort, limits, total;
+};
+
+ArenaLayout arena_layout(int64_t R, int64_t max_slots, int64_t max_spans, int64_t n_tiles) {
+    ArenaLayout A{};
+    A.count = align_up(count_layout(R).total);
+    A.sort = align_up(sort_layout(max_slots, max_spans, n_tiles).total);
+    A.limits = A.count + A.sort;
+    A.total = A.limits + align_up(2 * sizeof(int64_t));
+    return A;
+}
+
+}  // namespace
+
+extern "C" int gs_bin_arena_workspace(int64_t records, int64_t max_intersections,
+                                      int64_t max_spans, int64_t images, int width, int height,
+                                      size_t* bytes) {
+    if (!bytes || records < 0 || max_intersections < 1 || max_spans < 1 ||
+        max_spans > max_intersections || images < 1 || width < 1 || height < 1)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_arena_workspace: invalid arguments");
+    if (records > INT_MAX) return fail(GS_ERR_LIMIT, "gs_bin_arena_workspace: too many records");
+    if (max_intersections > INT_MAX)
+        return fail(GS_ERR_LIMIT, "gs_bin_arena_workspace: arena beyond int32 intersections");
+    const int64_t tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    *bytes = arena_layout(records, max_intersections, max_spans, images * tw * th).total;
     return GS_OK;
+}
+
+extern "C" int gs_bin_arena(const float* records, int record_stride, const int32_t* radii,
+                            const int64_t* image_ids, int64_t R, int64_t records_per_image,
+                            int64_t images, int width, int height, int flags, void* workspace,
+                            size_t workspace_bytes, int64_t max_intersections, int64_t max_spans,
+                            int32_t* point_list, int32_t* ranges, int64_t* totals, void* stream) {
+    int st = check_common("gs_bin_arena", records, record_stride, radii, R, records_per_image,
+                          images, width, height);
+    if (st) return st;
+    const bool tight = flags & GS_BIN_TIGHT;
+    if (tight && record_stride < 18)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_arena: GS_BIN_TIGHT needs opacity in record slot 17");
+    if (max_intersections < 1 || max_spans < 1 || max_spans > max_intersections)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_arena: invalid arena capacities");
+    if (max_intersections > INT_MAX)
+        return fail(GS_ERR_LIMIT, "gs_bin_arena: arena beyond int32 intersections");
+    if (!ranges || !point_list) return fail(GS_ERR_ARGUMENT, "gs_bin_arena: NULL output");
+    if (!image_ids && records_per_image < 1 && R > 0)
+        return fail(GS_ERR_ARGUMENT, "gs_bin_arena: records_per_image must be positive without image_ids");
+    const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    const int64_t n_tiles = images * tw * th;
+    const ArenaLayout A = arena_layout(R, max_intersections, max_spans, n_tiles);
+    if (!workspace || workspace_bytes < A.total)
+        return fail(GS_ERR_WORKSPACE, "gs_bin_arena: workspace too small");
+    auto s = as_stream(stream);
+    GS_CUDA(cudaMemsetAsync(ranges, 0, sizeof(int2) * n_tiles, s));
+    if (R == 0) {
+        if (totals) GS_CUDA(cudaMemsetAsync(totals, 0, 2 * sizeof(int64_t), s));
+        return GS_OK;
+    }
+    char* base = static_cast<char*>(workspace);
+    st = count_phase("gs_bin_arena", records, record_stride, radii, R, tight, width, height, base,
+                     A.count, s);
+    if (st) return st;
+    const CountLayout C = count_layout(R);
+    auto* limits = reinterpret_cast<int64_t*>(base + A.limits);
+    arena_limits_kernel<<<1, 1, 0, s>>>(R, reinterpret_cast<const int64_t*>(base + C.slot_end),
+                                        reinterpret_cast<const int64_t*>(base + C.span_end),
+                                        max_intersections, max_spans, totals, limits);
+    GS_CHECK_LAUNCH("arena_limits_kernel");
+    return sort_phase(records, record_stride, radii, image_ids, R, records_per_image, images, width,
+                      height, tight, base, base + A.count, max_intersections, max_spans, limits,
+                      point_list, ranges, s);
 }
 
 // ------------------------------------------------------------------------------

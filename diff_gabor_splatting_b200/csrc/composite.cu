@@ -19,6 +19,10 @@
 //     fields instead of 5 per field), summed across the CTA's 8 warps in shared
 //     memory, and added to global memory once per (tile, record) -- 8x fewer
 //     global atomics than one per warp.
+#include <mutex>
+#include <set>
+#include <utility>
+
 #include "common.cuh"
 
 namespace gs {
@@ -772,8 +776,21 @@ int launch_backward(Params& P, int64_t images, int neural, uint64_t* counters, v
     P.counters = reinterpret_cast<unsigned long long*>(counters);
     const dim3 block(kTile, kTile);
     auto launch = [&](auto kernel, size_t smem) -> int {
-        GS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     int(smem)));
+        // the shared-memory opt-in is set once per kernel and device, so launches under
+        // CUDA graph capture make no attribute calls
+        int device = 0;
+        GS_CUDA(cudaGetDevice(&device));
+        static std::mutex mutex;
+        static std::set<std::pair<const void*, int>> configured;
+        {
+            std::lock_guard<std::mutex> lock(mutex);
+            const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), device);
+            if (!configured.count(key)) {
+                GS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(smem)));
+                configured.insert(key);
+            }
+        }
         kernel<<<unsigned(tiles), block, smem, s>>>(P);
         return GS_OK;
     };

@@ -339,10 +339,62 @@ class _Ptr:
         self.address, self.device = address, device
 
 
+class Arena:
+    """Capacities for binning without a host synchronisation (``gs_bin_arena``).
+
+    While installed as ``rendering.ARENA`` every render bins all its images in one
+    arena of ``max_intersections`` (record, tile) slots and ``max_spans`` row spans,
+    with no host read of the counts, so render steps can be captured in CUDA graphs.
+    ``totals`` (device int64[2]) holds the live counts of the latest binning; when they
+    exceed the capacities that binning produced empty tile lists (background only):
+    check with ``overflowed()`` (one host read) and grow the arena.
+    """
+
+    def __init__(self, max_intersections: int, max_spans: int, device=None):
+        if not (1 <= max_spans <= max_intersections <= INT32_MAX):
+            raise ValueError("arena capacities must satisfy 1 <= max_spans <= "
+                             "max_intersections <= 2^31 - 1")
+        self.max_intersections, self.max_spans = int(max_intersections), int(max_spans)
+        self.totals = torch.zeros(2, dtype=torch.int64,
+                                  device=device if device is not None else "cuda")
+
+    def overflowed(self) -> bool:
+        live = self.totals.tolist()
+        return live[0] > self.max_intersections or live[1] > self.max_spans
+
+    def needed(self) -> tuple[int, int]:
+        """Live (intersections, spans) of the latest binning (one host read)."""
+        return tuple(self.totals.tolist())
+
+
+ARENA = None
+
+
+def _bin_arena(arena, records, radii, images, surfels, width, height):
+    device = records.device
+    tw, th = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
+    whole = Chunk(0, images, surfels, True)
+    R = whole.record_count
+    nbytes = ctypes.c_size_t()
+    nat.call("gs_bin_arena_workspace", R, arena.max_intersections, arena.max_spans, images,
+             width, height, ctypes.byref(nbytes))
+    workspace = torch.empty((max(nbytes.value, 1),), device=device, dtype=torch.uint8)
+    whole.point_list = torch.empty((arena.max_intersections,), device=device, dtype=torch.int32)
+    whole.ranges = torch.empty((images * tw * th, 2), device=device, dtype=torch.int32)
+    nat.call("gs_bin_arena", nat.ptr(records), nat.RECORD_FLOATS, nat.ptr(radii), None, R,
+             surfels, images, width, height, _bin_flags(), nat.ptr(workspace), nbytes.value,
+             arena.max_intersections, arena.max_spans, nat.ptr(whole.point_list),
+             nat.ptr(whole.ranges), nat.ptr(arena.totals), nat.stream_of(device))
+    return [whole]
+
+
 def bin_chunks(records, radii, scenes, cameras, surfels, width, height):
-    """Bin the dense records of S scenes x C cameras x N surfels in image chunks."""
+    """Bin the dense records of S scenes x C cameras x N surfels in image chunks (one
+    arena-binned chunk when ``ARENA`` is set)."""
     device = records.device
     images = scenes * cameras
+    if ARENA is not None and records.shape[0] > 0:
+        return _bin_arena(ARENA, records, radii, images, surfels, width, height)
     whole = Chunk(0, images, surfels, True)
     if records.shape[0] == 0:
         whole.record_count = 0

@@ -128,6 +128,24 @@ int gs_bin_sort(const float* records, int record_stride, const int32_t* radii,
                 int64_t intersections, int64_t spans, int32_t* point_list, int32_t* ranges,
                 void* stream);
 
+/* Binning without a host synchronisation (so a render step can be captured in a CUDA
+ * graph): the caller sizes an arena for at most max_intersections (record, tile) slots
+ * and max_spans row spans (gs_bin_arena_workspace); every launch is sized by those
+ * capacities and the live counts stay on the device.  point_list holds
+ * max_intersections entries (those past the live count are padding); ranges as for
+ * gs_bin_sort.  totals (device int64[2], nullable) receives the live intersection and
+ * span counts; when either exceeds its capacity nothing is binned (every tile range
+ * empty) and totals says how large the arena must be.  Same order and flags as
+ * gs_bin_count + gs_bin_sort.  No counterpart in the reference, whose binning reads the
+ * count on the host (rasterize.cu:466-468). */
+int gs_bin_arena_workspace(int64_t records, int64_t max_intersections, int64_t max_spans,
+                           int64_t images, int width, int height, size_t* bytes);
+int gs_bin_arena(const float* records, int record_stride, const int32_t* radii,
+                 const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
+                 int64_t images, int width, int height, int flags, void* workspace,
+                 size_t workspace_bytes, int64_t max_intersections, int64_t max_spans,
+                 int32_t* point_list, int32_t* ranges, int64_t* totals, void* stream);
+
 /* No-allocation binning: gs_bin_count followed by gs_bin_sort with both workspaces
  * taken from a 32 MiB array compiled into the library (one per GPU, held until
  * exit), for callers that cannot allocate device memory (a host application that

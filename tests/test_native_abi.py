@@ -77,6 +77,10 @@ def test_invalid_arguments_fail_before_any_gpu_work():
                                            fake, planes_ptr, grad_strides_ptr, 1, 8, 8, 0, 0.2,
                                            100.0, None, None, None, fake, None, None) == 1
     assert b"negative stride" in lib.gs_last_error()
+    # arena binning: capacities checked before any GPU work
+    assert lib.gs_bin_arena_workspace(10, 0, 0, 1, 8, 8, ctypes.byref(size)) == 1
+    assert lib.gs_bin_arena_workspace(10, 5, 6, 1, 8, 8, ctypes.byref(size)) == 1   # spans > slots
+    assert lib.gs_bin_arena_workspace(10, 2**31, 6, 1, 8, 8, ctypes.byref(size)) == 2
     # fused Adam: table and hyper-parameter checks
     assert lib.gs_adam_step(-1, None, None, None, None, None, 0.1, 0.9, 0.999, 1e-8, 0.0, 1,
                             None) == 1
