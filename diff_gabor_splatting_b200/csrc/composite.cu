@@ -53,6 +53,14 @@ struct Params {
     int* contributors;
     const float* gin[5];
     int64_t gin_px[5], gin_ch[5];
+    // optional median depth (2DGS convention: the depth of the last contribution made
+    // while the transmittance before it exceeds 0.5), its list position (1-based within
+    // the tile range, 0 for none) and its gradient; NULL when not requested
+    float* median;
+    int64_t median_px;
+    int* median_index;
+    const float* gin_median;
+    int64_t gin_median_px;
     // backward outputs
     float* grad_records;
     float* grad_xy;
@@ -300,7 +308,7 @@ __device__ __forceinline__ void appearance_forward(const float* a, const float* 
     }
 }
 
-template <bool Neural, bool Count, bool Exact>
+template <bool Neural, bool Count, bool Exact, bool Median>
 __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params P) {
     unsigned tests = 0, accepts = 0;
     __shared__ Batch<Neural> batch;
@@ -312,7 +320,8 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
     const bool inside = x < P.width && y < P.height;
     bool done = !inside;
     const int64_t pixel = (int64_t(image) * P.height + y) * P.width + x;
-    float out[kMaps] = {}, T = 1, m1 = 0, m2 = 0;
+    float out[kMaps] = {}, T = 1, m1 = 0, m2 = 0, median = 0;
+    int median_at = 0;
     int last = 0;
     const int2 range = P.ranges[tile];
     const Directions dirs;
@@ -346,8 +355,12 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
             out[8] += w * (m * m * (1 - T) + m2 - 2 * m * m1);
             m1 += w * m;
             m2 += w * m * m;
-            T = next;
             last = start + j - range.x + 1;
+            if (Median && T > 0.5f) {   // transmittance before this contribution
+                median = v.depth;
+                median_at = last;
+            }
+            T = next;
         }
     }
     if (inside) {
@@ -364,6 +377,10 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
         P.state[pixel * 3 + 1] = m1;
         P.state[pixel * 3 + 2] = m2;
         P.contributors[pixel] = last;
+        if constexpr (Median) {
+            P.median[pixel * P.median_px] = median;
+            P.median_index[pixel] = median_at;
+        }
     }
     if constexpr (Count) add_counts(P.counters, tests, accepts);
 }
@@ -464,6 +481,9 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     const bool inside = x < P.width && y < P.height;
     const int64_t pixel = (int64_t(image) * P.height + y) * P.width + x;
     const int last = inside ? P.contributors[pixel] : 0;
+    // median depth gradient goes to the depth of the median contribution
+    const int median_at = inside && P.gin_median ? P.median_index[pixel] : 0;
+    const float go_median = median_at ? P.gin_median[pixel * P.gin_median_px] : 0.f;
     if (rank < 3) bg_acc[rank] = 0.f;
     int wmax = last;
 #pragma unroll
@@ -630,8 +650,9 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                     }
                 }
                 // geometry: rasterize.cu:359-385
-                const float gz = w * fmaf(depth_term * fmaf(m, total_a, -m1), inv_depth * inv_depth,
-                                          go[4]);
+                float gz = w * fmaf(depth_term * fmaf(m, total_a, -m1), inv_depth * inv_depth,
+                                    go[4]);
+                if (start - j == median_at) gz += go_median;
                 if (Neural || v.surface) {
                     gs[0] += gz * g[6];
                     gs[1] += gz * g[7];
@@ -757,7 +778,9 @@ int launch_forward(Params& P, int64_t images, int neural, int flags, uint64_t* c
     const dim3 block(kTile, kTile);
     const bool exact = flags & GS_COMPOSITE_EXACT;
     const unsigned grid = unsigned(tiles);
-#define GS_FWD(N, C, E) composite_forward_kernel<N, C, E><<<grid, block, 0, s>>>(P)
+#define GS_FWD(N, C, E)                                                                    \
+    (P.median ? composite_forward_kernel<N, C, E, true><<<grid, block, 0, s>>>(P)             \
+              : composite_forward_kernel<N, C, E, false><<<grid, block, 0, s>>>(P))
     if (neural) {
         if (counters) { if (exact) GS_FWD(true, true, true); else GS_FWD(true, true, false); }
         else { if (exact) GS_FWD(true, false, true); else GS_FWD(true, false, false); }
@@ -852,8 +875,10 @@ extern "C" int gs_composite_forward_split(const float* records, const float* row
                                           int64_t images, int width, int height, int neural,
                                           int flags, float near_plane, float far_plane,
                                           float* const* planes, const int64_t* plane_strides,
-                                          float* state, int32_t* contributors,
-                                          uint64_t* counters, void* stream) {
+                                          float* median_depth, int64_t median_stride,
+                                          int32_t* median_index, float* state,
+                                          int32_t* contributors, uint64_t* counters,
+                                          void* stream) {
     int st = check_composite("gs_composite_forward_split", records, rows, row_mode, primitive_ids,
                              cameras, surfels, records_count, backgrounds, ranges, images, width,
                              height);
@@ -869,6 +894,11 @@ extern "C" int gs_composite_forward_split(const float* records, const float* row
         P.out[g] = planes[g];
         P.out_px[g] = plane_strides[g];
     }
+    if (median_depth && (!median_index || median_stride < 1))
+        return fail(GS_ERR_ARGUMENT, "gs_composite_forward_split: median depth needs its index buffer");
+    P.median = median_depth;
+    P.median_px = median_stride;
+    P.median_index = median_index;
     P.state = state;
     P.contributors = contributors;
     return launch_forward(P, images, neural, flags, counters, stream);
@@ -916,7 +946,10 @@ extern "C" int gs_composite_backward_split(const float* records, const float* ro
                                            const int32_t* point_list, const int32_t* ranges,
                                            const float* state, const int32_t* contributors,
                                            const float* const* grad_planes,
-                                           const int64_t* grad_strides, int64_t images,
+                                           const int64_t* grad_strides,
+                                           const int32_t* median_index,
+                                           const float* grad_median, int64_t grad_median_stride,
+                                           int64_t images,
                                            int width, int height, int neural, float near_plane,
                                            float far_plane, float* grad_records, float* grad_xy,
                                            float* grad_rows, float* grad_backgrounds,
@@ -942,6 +975,11 @@ extern "C" int gs_composite_backward_split(const float* records, const float* ro
         P.gin_px[g] = grad_strides[2 * g];
         P.gin_ch[g] = grad_strides[2 * g + 1];
     }
+    if (grad_median && (!median_index || grad_median_stride < 0))
+        return fail(GS_ERR_ARGUMENT, "gs_composite_backward_split: median gradient needs its index buffer");
+    P.median_index = const_cast<int*>(median_index);
+    P.gin_median = grad_median;
+    P.gin_median_px = grad_median_stride;
     P.grad_records = grad_records;
     P.grad_xy = grad_xy;
     P.grad_rows = grad_rows;

@@ -140,10 +140,16 @@ class Composite(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, records, projected_means, rows, backgrounds, selected, chunks, row_mode,
-                cameras, surfels, images, width, height, neural, near_plane, far_plane):
+                cameras, surfels, images, width, height, neural, near_plane, far_plane,
+                median=False):
         device = records.device
         planes = [torch.empty((images, height, width, k), device=device, dtype=torch.float32)
                   for k in PLANES]
+        # optional median depth plane and the 1-based list position it came from
+        median_depth = torch.empty((images, height, width, 1) if median else (0,),
+                                   device=device, dtype=torch.float32)
+        median_index = torch.empty((images, height, width) if median else (0,), device=device,
+                                   dtype=torch.int32)
         state = torch.empty((images, height, width, 3), device=device, dtype=torch.float32)
         contributors = torch.empty((images, height, width), device=device, dtype=torch.int32)
         stream = nat.stream_of(device)
@@ -157,23 +163,30 @@ class Composite(torch.autograd.Function):
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
                      nat.ptr(ch.ranges), ch.images, width, height, int(neural),
                      _composite_flags(), near_plane, far_plane, outs_ptr, strides_ptr,
+                     _at(median_depth, a["pixel0"]), 1, _at(median_index, a["pixel0"]),
                      _at(state, a["pixel0"] * 3), _at(contributors, a["pixel0"]),
                      nat.ptr(_counters("forward", device)), stream)
-        ctx.save_for_backward(records, rows, backgrounds, selected, state, contributors)
+        ctx.save_for_backward(records, rows, backgrounds, selected, state, contributors,
+                              median_index)
         ctx.set_materialize_grads(False)   # an unused output's gradient stays None (zero)
         ctx.chunks = chunks
         ctx.options = (row_mode, cameras, surfels, images, width, height, neural, near_plane,
                        far_plane)
-        return tuple(planes)
+        return tuple(planes) + (median_depth,)
 
     @staticmethod
     @once_differentiable
-    def backward(ctx, *grad_planes):
-        records, rows, backgrounds, selected, state, contributors = ctx.saved_tensors
+    def backward(ctx, *grad_outputs):
+        records, rows, backgrounds, selected, state, contributors, median_index = \
+            ctx.saved_tensors
+        grad_planes, grad_median = grad_outputs[:5], grad_outputs[5]
+        if median_index.numel() == 0:
+            grad_median = None
         row_mode, cameras, surfels, images, width, height, neural, near_plane, far_plane = \
             ctx.options
         device = records.device
         grads = [_pixel_linear(g, height, width) for g in grad_planes]
+        g_median, median_px, _ = _pixel_linear(grad_median, height, width)
         g_records = torch.zeros_like(records)
         g_xy = torch.zeros((records.shape[0], 2), device=device, dtype=torch.float32)
         g_rows = torch.zeros_like(rows)
@@ -190,13 +203,15 @@ class Composite(torch.autograd.Function):
                      a["cameras"], surfels, ch.record_count, a["rows_count"],
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
                      nat.ptr(ch.ranges), _at(state, a["pixel0"] * 3),
-                     _at(contributors, a["pixel0"]), ins_ptr, strides_ptr, ch.images, width,
-                     height, int(neural), near_plane, far_plane,
+                     _at(contributors, a["pixel0"]), ins_ptr, strides_ptr,
+                     _at(median_index, a["pixel0"]) if g_median is not None else None,
+                     None if g_median is None else g_median.data_ptr() + a["pixel0"] * median_px * 4,
+                     median_px, ch.images, width, height, int(neural), near_plane, far_plane,
                      _at(g_records, ch.record0 * nat.RECORD_FLOATS), _at(g_xy, ch.record0 * 2),
                      _at(g_rows, a["row0"] * rows.shape[1]), _at(g_bg, ch.image0 * 3),
                      nat.ptr(_counters("backward", device)), stream)
         g_pm = g_xy if selected is None else g_xy[selected]
-        return (g_records, g_pm, g_rows, g_bg) + (None,) * 11
+        return (g_records, g_pm, g_rows, g_bg) + (None,) * 12
 
 
 def _pixel_linear(g, height, width):
@@ -584,7 +599,8 @@ def _check_sh(first, second, directions, degree):
 # render (rendering.py:241-400)
 # ----------------------------------------------------------------------------------
 def render(means, quaternions, scales, opacities, appearance, view_matrices, intrinsics, width,
-           height, backgrounds, packed, near_plane, far_plane, neural, sh_degree, validate):
+           height, backgrounds, packed, near_plane, far_plane, neural, sh_degree, validate,
+           median_depth=False):
     """Validate inputs, project scene/camera pairs, bin, and composite in one call."""
     if not isinstance(means, torch.Tensor) or means.ndim < 2 or means.shape[-1] != 3:
         raise ValueError("means must have shape [..., N, 3]")
@@ -632,6 +648,8 @@ def render(means, quaternions, scales, opacities, appearance, view_matrices, int
         tensors[name] = tensor, batch + (n,) + shape
     for name, (tensor, shape) in tensors.items():
         check_tensor(name, tensor, shape, device)
+    if type(median_depth) is not bool:
+        raise TypeError("median_depth must be bool")
     if type(validate) is not bool:
         raise TypeError("validate must be bool")
     if validate:
@@ -640,12 +658,12 @@ def render(means, quaternions, scales, opacities, appearance, view_matrices, int
     with torch.cuda.device(device):
         return _render(means, quaternions, scales, opacities, appearance, view_matrices,
                        intrinsics, width, height, backgrounds, packed, near_plane, far_plane,
-                       neural, sh_degree, batch, scenes, cameras, n)
+                       neural, sh_degree, batch, scenes, cameras, n, median_depth)
 
 
 def _render(means, quaternions, scales, opacities, appearance, view_matrices, intrinsics, width,
             height, backgrounds, packed, near_plane, far_plane, neural, sh_degree, batch, scenes,
-            cameras, n):
+            cameras, n, median_depth=False):
     device = means.device
     S, C, N = scenes, cameras, n
     P = S * C * N
@@ -674,11 +692,11 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
     if packed:
         selected = torch.nonzero(radii > 0).reshape(-1)
         projected_means = xy[selected]
+    outputs = Composite.apply(records, projected_means, rows, backgrounds.reshape(-1, 3),
+                              selected, chunks, row_mode, C, max(N, 1), images, width, height,
+                              neural, float(near_plane), float(far_plane), median_depth)
     rgb, alpha, depth, normals, distortion = (
-        plane.reshape(batch + (C, height, width, plane.shape[-1])) for plane in Composite.apply(
-            records, projected_means, rows, backgrounds.reshape(-1, 3), selected, chunks,
-            row_mode, C, max(N, 1), images, width, height, neural, float(near_plane),
-            float(far_plane)))
+        plane.reshape(batch + (C, height, width, plane.shape[-1])) for plane in outputs[:5])
     ids = selected if packed else torch.arange(P, device=device)
     meta = {
         "radii": radii[selected] if packed else radii.reshape(batch + (C, N)),
@@ -691,6 +709,8 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
         "normals": normals,
         "distortion": distortion,
     }
+    if median_depth:
+        meta["median_depth"] = outputs[5].reshape(batch + (C, height, width, 1))
     return rgb, alpha, meta
 
 
@@ -715,6 +735,7 @@ def rasterize_gabors(
     far_plane: float = 100.0,
     sh_degree: int | None = None,
     validate: bool = True,
+    median_depth: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor, dict[str, Any]]:
     """Render four-frequency Gabor surfaces over arbitrary scene and camera batches.
 
@@ -726,11 +747,17 @@ def rasterize_gabors(
     All tensors contiguous CUDA float32.  Returns RGB [..., C, H, W, 3], alpha
     [..., C, H, W, 1] and metadata (radii, projected_means, scene/camera/primitive
     ids, packed, accumulated_depth, normals, distortion).
+
+    ``median_depth=True`` (an addition: the reference lists median depth outside its
+    release) also returns ``meta["median_depth"]`` [..., C, H, W, 1]: per pixel the depth
+    of the last contribution made while the transmittance before it exceeded 0.5 (the
+    2DGS convention; 0 without contributions), differentiable through that
+    contribution's depth.
     """
     return render(means, quaternions, scales, opacities,
                   (colors, secondary_colors, frequency_weights, frequency_magnitudes, phases),
                   view_matrices, intrinsics, width, height, backgrounds, packed, near_plane,
-                  far_plane, False, sh_degree, validate)
+                  far_plane, False, sh_degree, validate, median_depth)
 
 
 def rasterize_neural_gabors(
@@ -752,14 +779,16 @@ def rasterize_neural_gabors(
     near_plane: float = 0.2,
     far_plane: float = 100.0,
     validate: bool = True,
+    median_depth: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor, dict[str, Any]]:
     """Render per-surface 5->6->3 SIRENs (sine frequency 30, sigmoid RGB).
 
     Same contract as the reference (rendering.py:459-502): per-primitive input
     weights/biases [..., N, 6, 5] / [..., N, 6], output weights/biases
     [..., N, 3, 6] / [..., N, 3]; network input (u/3, v/3, world view direction).
+    ``median_depth`` as for ``rasterize_gabors``.
     """
     return render(means, quaternions, scales, opacities,
                   (input_weights, input_biases, output_weights, output_biases),
                   view_matrices, intrinsics, width, height, backgrounds, packed, near_plane,
-                  far_plane, True, None, validate)
+                  far_plane, True, None, validate, median_depth)

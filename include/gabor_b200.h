@@ -208,22 +208,33 @@ int gs_composite_backward(const float* records, const float* rows, int row_mode,
  * zero gradient).  `planes`, `plane_strides`, `grad_planes` and `grad_strides` are
  * host arrays.  No counterpart in the reference, which writes one [..][9] array and
  * slices it: with separate planes a framework hands each output's gradient to the
- * kernel as it is, without assembling a full [..][9] gradient. */
+ * kernel as it is, without assembling a full [..][9] gradient.
+ * Median depth (optional, no counterpart in the reference, which lists it outside its
+ * release): with median_depth non-NULL the forward also writes, per pixel, the depth of
+ * the last contribution made while the transmittance before it exceeds 0.5 (the 2DGS
+ * convention; 0 without contributions) at median_depth + p * median_stride, and its
+ * 1-based position in the tile's list (0: none) in median_index[p]; the backward adds
+ * grad_median[p * grad_median_stride] (nullable; stride 0 broadcasts) to that
+ * contribution's depth gradient. */
 int gs_composite_forward_split(const float* records, const float* rows, int row_mode,
                                const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
                                int64_t records_count, int64_t rows_count,
                                const float* backgrounds, const int32_t* point_list,
                                const int32_t* ranges, int64_t images, int width, int height,
                                int neural, int flags, float near_plane, float far_plane,
-                               float* const* planes, const int64_t* plane_strides, float* state,
-                               int32_t* contributors, uint64_t* counters, void* stream);
+                               float* const* planes, const int64_t* plane_strides,
+                               float* median_depth, int64_t median_stride,
+                               int32_t* median_index, float* state, int32_t* contributors,
+                               uint64_t* counters, void* stream);
 int gs_composite_backward_split(const float* records, const float* rows, int row_mode,
                                 const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
                                 int64_t records_count, int64_t rows_count,
                                 const float* backgrounds, const int32_t* point_list,
                                 const int32_t* ranges, const float* state,
                                 const int32_t* contributors, const float* const* grad_planes,
-                                const int64_t* grad_strides, int64_t images, int width,
+                                const int64_t* grad_strides, const int32_t* median_index,
+                                const float* grad_median, int64_t grad_median_stride,
+                                int64_t images, int width,
                                 int height, int neural, float near_plane, float far_plane,
                                 float* grad_records, float* grad_xy, float* grad_rows,
                                 float* grad_backgrounds, uint64_t* counters, void* stream);

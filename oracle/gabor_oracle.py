@@ -335,6 +335,9 @@ def composite(geometry, appearance, opacities, primitive_ids, backgrounds, point
     out = [torch.zeros_like(T) for _ in range(MAP_SIZE)]
     done = ~inside
     last = torch.zeros((n, TILE * TILE), dtype=torch.int64)
+    # median depth: the depth of the last contribution made while the transmittance
+    # before it exceeds 0.5 (the 2DGS convention; an addition beyond the reference)
+    median = torch.zeros_like(T)
     max_len = int(lens.max()) if n else 0
     one = torch.ones((), dtype=dtype)
     for j in range(max_len):
@@ -385,6 +388,7 @@ def composite(geometry, appearance, opacities, primitive_ids, backgrounds, point
         out[8] = out[8] + w * (m * m * (1 - T) + m2 - 2 * m * m1)
         m1 = m1 + w * m
         m2 = m2 + w * m * m
+        median = torch.where(accept & (T > 0.5), dsafe, median)
         T = torch.where(accept, nxt, T)
         last = torch.where(accept, torch.full_like(last, j + 1), last)
     bg = backgrounds[image][:, None, :]
@@ -396,7 +400,9 @@ def composite(geometry, appearance, opacities, primitive_ids, backgrounds, point
     maps = torch.where(inside[..., None], maps, zero)
     state = torch.where(inside[..., None], torch.stack((T, m1, m2), -1), zero)
     contributors = torch.where(inside, last, torch.zeros_like(last)).to(torch.int32)
-    return dict(maps=maps, state=state, contributors=contributors, inside=inside, tiles=tiles)
+    median = torch.where(inside, median, zero)
+    return dict(maps=maps, state=state, contributors=contributors, inside=inside, tiles=tiles,
+                median_depth=median)
 
 
 def tiles_to_images(tile_values, images, width, height):
@@ -457,6 +463,8 @@ def render(means, quaternions, scales, opacities, appearance, view_matrices, int
         "accumulated_depth": maps[..., 4:5],
         "normals": maps[..., 5:8],
         "distortion": maps[..., 8:9],
+        "median_depth": tiles_to_images(comp["median_depth"], images, width, height).reshape(
+            batch + (cameras, height, width, 1)),
     }
     if return_internals:
         meta["_records"] = rec

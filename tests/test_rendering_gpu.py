@@ -260,3 +260,44 @@ def test_projected_means_receive_screen_gradient():
         assert grad is not None and grad.shape == meta["projected_means"].shape
         assert torch.isfinite(grad).all()
         assert np.asarray(meta["radii"].cpu()).size > 0
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_median_depth_matches_oracle(method):
+    """meta["median_depth"] (an addition: the depth of the last contribution made while
+    the transmittance before it exceeds 0.5, the 2DGS convention) against the float64
+    oracle's restatement, values and the gradient of a loss on it."""
+    from oracle import gabor_oracle as O
+    from helpers import random_scene
+
+    v = random_scene(method, scenes=1, cameras=2, n=200, width=40, height=30, conditioned=True)
+    fn = rasterize_gabors if method == "classic" else rasterize_neural_gabors
+    mine = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    rgb, alpha, meta = fn(**mine, width=40, height=30, median_depth=True)
+    median = meta["median_depth"]
+    assert median.shape == alpha.shape
+    cpu = {k: t.detach().cpu().double().requires_grad_() for k, t in ordered(v, method).items()}
+    names = ["means", "quaternions", "scales", "opacities"]
+    app = [cpu[k] for k in cpu if k not in names + ["view_matrices", "intrinsics", "backgrounds"]]
+    _, o_alpha, o_meta = O.render(cpu["means"], cpu["quaternions"], cpu["scales"],
+                                  cpu["opacities"], app, cpu["view_matrices"], cpu["intrinsics"],
+                                  40, 30, backgrounds=cpu["backgrounds"], neural=method == "neural",
+                                  dtype=torch.float64)
+    expected = o_meta["median_depth"]
+    close = torch.isclose(median.detach().cpu().double(), expected, rtol=1e-5, atol=1e-5)
+    assert close.double().mean().item() >= 0.99   # rare float32 threshold flips
+    # gradient of a weighted median-depth loss through the median contribution's depth
+    w = torch.linspace(0.5, 1.5, median.numel()).reshape(median.shape)
+    (median * w.cuda()).sum().backward()
+    (expected * w.double()).sum().backward()
+    reference_norm = cpu["means"].grad.norm().item()
+    for name in ("means", "quaternions", "scales"):
+        # a surface's depth at a pixel does not depend on its scales (the ray meets the
+        # same plane), so their exact gradient is zero: errors are measured against the
+        # means gradient's norm
+        a, e = mine[name].grad.cpu().double(), cpu[name].grad
+        rel = (a - e).norm().item() / max(e.norm().item(), reference_norm)
+        assert rel <= 2e-2, f"{name}: relative L2 {rel:.2e}"
+    # without the flag the key is absent and nothing changes
+    _, _, plain = fn(**{k: t.detach() for k, t in mine.items()}, width=40, height=30)
+    assert "median_depth" not in plain
