@@ -66,6 +66,9 @@ def parse():
                    help="add an Adam step (lr 1e-3) over every parameter to each step: this\n"
                         "build's fused kernel or torch.optim.Adam (the reference's loop);\n"
                         "reported under 'optimizer' (the e2e leg is skipped)")
+    p.add_argument("--pixels", type=int, default=None,
+                   help="render only this many seeded random pixels per camera (selected-\n"
+                        "pixel mode); the metric counts the selected pixels")
     p.add_argument("--graph", action="store_true",
                    help="also time the step captured as one CUDA graph (arena binning, no\n"
                         "host sync): reported under 'graph' beside the eager value")
@@ -119,6 +122,26 @@ class Job:
         self.calls = [{k: v[s:s + step] for k, v in part.items()} for s in range(0, S, step)]
         self.local_pixels = sum(c["view_matrices"].shape[0] * c["view_matrices"].shape[1]
                                 for c in self.calls) * full.width * full.height
+        self.pixel_count = args.pixels
+        self.pixels = None
+        if args.pixels:   # selected-pixel mode: the metric counts selected pixels
+            scale = args.pixels / (full.width * full.height)
+            self.total_pixels = round(self.total_pixels * scale)
+            self.local_pixels = round(self.local_pixels * scale)
+
+    def pixels_on(self, device, seed=0):
+        """Seeded random (x, y) per camera for every call (selected-pixel mode)."""
+        if not self.pixel_count:
+            return None
+        w = self.workload
+        g = torch.Generator().manual_seed(seed)
+        out = []
+        for c in self.calls:
+            shape = tuple(c["view_matrices"].shape[:-2]) + (self.pixel_count,)
+            xy = torch.stack((torch.randint(0, w.width, shape, generator=g),
+                              torch.randint(0, w.height, shape, generator=g)), -1)
+            out.append(xy.to(torch.int32).to(device))
+        return out
 
     def inputs_on(self, device):
         return [{k: v.to(device).contiguous().requires_grad_() for k, v in c.items()}
@@ -219,10 +242,11 @@ def step(fn, job, calls, optimizer=None):
     optional optimizer step."""
     w = job.workload
     total = None
-    for values in calls:
+    for i, values in enumerate(calls):
         for v in values.values():
             v.grad = None
-        rgb, alpha, meta = fn(**values, **w.kwargs(), validate=False)
+        extra = {} if job.pixels is None else {"pixels": job.pixels[i]}
+        rgb, alpha, meta = fn(**values, **w.kwargs(), **extra, validate=False)
         pixels = rgb.shape[:-1].numel()
         loss = loss_of(rgb, alpha, meta, w.depth_normal_loss) * (pixels / job.total_pixels)
         loss.backward()
@@ -372,6 +396,7 @@ def main():
     w = job.workload
     fn = rasterize_gabors if w.method == "classic" else rasterize_neural_gabors
     calls = job.inputs_on(device)
+    job.pixels = job.pixels_on(device)
     opt = OptimizerStep(args.optimizer, calls) if args.optimizer != "none" else None
     for _ in range(max(args.warmup, 3)):
         step(fn, job, calls, opt)
@@ -440,6 +465,10 @@ def main():
                 "roofline": roofline(stage, counts, w, args.steps, len(job.calls)),
                 "stages_ms_per_step": {k: v[1] / args.steps for k, v in stage.items()},
                 "work": counts, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary()}
+        if args.pixels:
+            line["config"]["selected_pixels_per_camera"] = args.pixels
+            line["config"]["pixels_per_step"] = pixels_all
+            line["roofline"]["note"] = "kernel work counted on a full render of the workload"
         if graph is not None:
             line["graph"] = graph
         if opt is not None:

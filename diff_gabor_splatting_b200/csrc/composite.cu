@@ -61,6 +61,11 @@ struct Params {
     int* median_index;
     const float* gin_median;
     int64_t gin_median_px;
+    // selected-pixel mode (NULL groups: whole tiles): one CTA per group of up to 256
+    // selected pixels of one tile, groups[b] = (tile, first, count, -); selected pixel
+    // i = (x, y, output index, -); outputs and gradients are indexed by output index
+    const int4* groups;
+    const int4* selected;
     // backward outputs
     float* grad_records;
     float* grad_xy;
@@ -69,6 +74,39 @@ struct Params {
     // optional work counters: [0] samples tested, [1] contributions accepted
     unsigned long long* counters;
 };
+
+// The pixel a thread composites: in tile mode pixel (rank % 16, rank / 16) of tile
+// blockIdx.x, output index (image H + y) W + x; in selected-pixel mode the rank-th pixel
+// of group blockIdx.x (threads past the group's count are outside).
+struct PixelSlot {
+    int tile, image, x, y;
+    int64_t pixel;
+    bool inside;
+};
+
+__device__ __forceinline__ PixelSlot pixel_slot(const Params& P, int rank) {
+    PixelSlot q;
+    const int tiles_per_image = P.tw * P.th;
+    if (P.groups) {
+        const int4 group = P.groups[blockIdx.x];
+        q.tile = group.x;
+        q.image = q.tile / tiles_per_image;
+        q.inside = rank < group.z;
+        const int4 sel = P.selected[group.y + (q.inside ? rank : 0)];
+        q.x = sel.x;
+        q.y = sel.y;
+        q.pixel = sel.z;
+    } else {
+        q.tile = blockIdx.x;
+        q.image = q.tile / tiles_per_image;
+        const int local = q.tile % tiles_per_image;
+        q.x = (local % P.tw) * kTile + rank % kTile;
+        q.y = (local / P.tw) * kTile + rank / kTile;
+        q.inside = q.x < P.width && q.y < P.height;
+        q.pixel = (int64_t(q.image) * P.height + q.y) * P.width + q.x;
+    }
+    return q;
+}
 
 // First map channel and channel count of plane g (rgb, alpha, depth, normals, distortion).
 __host__ __device__ constexpr int plane_first(int g) {
@@ -312,14 +350,12 @@ template <bool Neural, bool Count, bool Exact, bool Median>
 __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params P) {
     unsigned tests = 0, accepts = 0;
     __shared__ Batch<Neural> batch;
-    const int tiles_per_image = P.tw * P.th;
-    const int tile = blockIdx.x;
-    const int image = tile / tiles_per_image, local = tile % tiles_per_image;
-    const int x = (local % P.tw) * kTile + threadIdx.x, y = (local / P.tw) * kTile + threadIdx.y;
     const int rank = threadIdx.y * kTile + threadIdx.x;
-    const bool inside = x < P.width && y < P.height;
+    const PixelSlot slot = pixel_slot(P, rank);
+    const int tile = slot.tile, image = slot.image, x = slot.x, y = slot.y;
+    const bool inside = slot.inside;
+    const int64_t pixel = slot.pixel;
     bool done = !inside;
-    const int64_t pixel = (int64_t(image) * P.height + y) * P.width + x;
     float out[kMaps] = {}, T = 1, m1 = 0, m2 = 0, median = 0;
     int median_at = 0;
     int last = 0;
@@ -473,13 +509,11 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     float* bg_acc = sh.bg;
     const int lane = (threadIdx.y * kTile + threadIdx.x) & 31;
     const int warp = (threadIdx.y * kTile + threadIdx.x) >> 5;
-    const int tiles_per_image = P.tw * P.th;
-    const int tile = blockIdx.x;
-    const int image = tile / tiles_per_image, local = tile % tiles_per_image;
-    const int x = (local % P.tw) * kTile + threadIdx.x, y = (local / P.tw) * kTile + threadIdx.y;
     const int rank = threadIdx.y * kTile + threadIdx.x;
-    const bool inside = x < P.width && y < P.height;
-    const int64_t pixel = (int64_t(image) * P.height + y) * P.width + x;
+    const PixelSlot slot = pixel_slot(P, rank);
+    const int tile = slot.tile, image = slot.image, x = slot.x, y = slot.y;
+    const bool inside = slot.inside;
+    const int64_t pixel = slot.pixel;
     const int last = inside ? P.contributors[pixel] : 0;
     // median depth gradient goes to the depth of the median contribution
     const int median_at = inside && P.gin_median ? P.median_index[pixel] : 0;
@@ -771,8 +805,9 @@ Params common_params(const float* records, const float* rows, int row_mode,
 }
 
 int launch_forward(Params& P, int64_t images, int neural, int flags, uint64_t* counters,
-                   void* stream) {
-    const int64_t tiles = images * P.tw * P.th;
+                   void* stream, int64_t group_count = -1) {
+    const int64_t tiles = group_count >= 0 ? group_count : images * P.tw * P.th;
+    if (tiles == 0) return GS_OK;
     auto s = as_stream(stream);
     P.counters = reinterpret_cast<unsigned long long*>(counters);
     const dim3 block(kTile, kTile);
@@ -793,9 +828,11 @@ int launch_forward(Params& P, int64_t images, int neural, int flags, uint64_t* c
     return GS_OK;
 }
 
-int launch_backward(Params& P, int64_t images, int neural, uint64_t* counters, void* stream) {
+int launch_backward(Params& P, int64_t images, int neural, uint64_t* counters, void* stream,
+                    int64_t group_count = -1) {
     auto s = as_stream(stream);
-    const int64_t tiles = images * P.tw * P.th;
+    const int64_t tiles = group_count >= 0 ? group_count : images * P.tw * P.th;
+    if (tiles == 0) return GS_OK;
     P.counters = reinterpret_cast<unsigned long long*>(counters);
     const dim3 block(kTile, kTile);
     auto launch = [&](auto kernel, size_t smem) -> int {
@@ -876,9 +913,10 @@ extern "C" int gs_composite_forward_split(const float* records, const float* row
                                           int flags, float near_plane, float far_plane,
                                           float* const* planes, const int64_t* plane_strides,
                                           float* median_depth, int64_t median_stride,
-                                          int32_t* median_index, float* state,
-                                          int32_t* contributors, uint64_t* counters,
-                                          void* stream) {
+                                          int32_t* median_index, const int32_t* selected,
+                                          const int32_t* groups, int64_t group_count,
+                                          float* state, int32_t* contributors,
+                                          uint64_t* counters, void* stream) {
     int st = check_composite("gs_composite_forward_split", records, rows, row_mode, primitive_ids,
                              cameras, surfels, records_count, backgrounds, ranges, images, width,
                              height);
@@ -901,7 +939,11 @@ extern "C" int gs_composite_forward_split(const float* records, const float* row
     P.median_index = median_index;
     P.state = state;
     P.contributors = contributors;
-    return launch_forward(P, images, neural, flags, counters, stream);
+    if (bool(selected) != bool(groups) || (groups && group_count < 0) || group_count > INT_MAX)
+        return fail(GS_ERR_ARGUMENT, "gs_composite_forward_split: bad selected-pixel groups");
+    P.selected = reinterpret_cast<const int4*>(selected);
+    P.groups = reinterpret_cast<const int4*>(groups);
+    return launch_forward(P, images, neural, flags, counters, stream, groups ? group_count : -1);
 }
 
 extern "C" int gs_composite_backward(const float* records, const float* rows, int row_mode,
@@ -949,7 +991,8 @@ extern "C" int gs_composite_backward_split(const float* records, const float* ro
                                            const int64_t* grad_strides,
                                            const int32_t* median_index,
                                            const float* grad_median, int64_t grad_median_stride,
-                                           int64_t images,
+                                           const int32_t* selected, const int32_t* groups,
+                                           int64_t group_count, int64_t images,
                                            int width, int height, int neural, float near_plane,
                                            float far_plane, float* grad_records, float* grad_xy,
                                            float* grad_rows, float* grad_backgrounds,
@@ -980,9 +1023,13 @@ extern "C" int gs_composite_backward_split(const float* records, const float* ro
     P.median_index = const_cast<int*>(median_index);
     P.gin_median = grad_median;
     P.gin_median_px = grad_median_stride;
+    if (bool(selected) != bool(groups) || (groups && group_count < 0) || group_count > INT_MAX)
+        return fail(GS_ERR_ARGUMENT, "gs_composite_backward_split: bad selected-pixel groups");
+    P.selected = reinterpret_cast<const int4*>(selected);
+    P.groups = reinterpret_cast<const int4*>(groups);
     P.grad_records = grad_records;
     P.grad_xy = grad_xy;
     P.grad_rows = grad_rows;
     P.grad_backgrounds = grad_backgrounds;
-    return launch_backward(P, images, neural, counters, stream);
+    return launch_backward(P, images, neural, counters, stream, groups ? group_count : -1);
 }

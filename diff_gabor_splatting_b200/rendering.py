@@ -125,6 +125,54 @@ class Projection(torch.autograd.Function):
 PLANES = (3, 1, 1, 3, 1)
 
 
+class Selection:
+    """Selected pixels of every image, grouped for the compositor's selected-pixel mode.
+
+    ``pixels`` [images, P, 2] integer (x, y) inside the image.  Pixels are sorted
+    (stably) by tile and cut into groups of at most 256 pixels of one tile; the kernels
+    write each pixel's outputs at its original index image * P + p.
+    """
+
+    def __init__(self, pixels: torch.Tensor, width: int, height: int):
+        images, count = pixels.shape[0], pixels.shape[1]
+        device = pixels.device
+        self.count = count
+        self.tw, self.th = (width + TILE - 1) // TILE, (height + TILE - 1) // TILE
+        tiles_per_image = self.tw * self.th
+        x = pixels[..., 0].reshape(-1).long()
+        y = pixels[..., 1].reshape(-1).long()
+        image = torch.arange(images, device=device).repeat_interleave(count)
+        tile = image * tiles_per_image + (y // TILE) * self.tw + x // TILE
+        order = torch.argsort(tile, stable=True)
+        ordered_tiles = tile[order]
+        n = ordered_tiles.numel()
+        index = torch.arange(n, device=device)
+        run_start = torch.ones(n, dtype=torch.bool, device=device)
+        run_start[1:] = ordered_tiles[1:] != ordered_tiles[:-1]
+        first_of_run = torch.cummax(torch.where(run_start, index, torch.zeros_like(index)), 0)[0]
+        new_group = run_start | ((index - first_of_run) % (TILE * TILE) == 0)
+        firsts = torch.nonzero(new_group).reshape(-1)
+        counts = torch.diff(firsts, append=torch.tensor([n], device=device))
+        self.tiles_per_image = tiles_per_image
+        self.group_tile = ordered_tiles[firsts]
+        self.group_first = firsts
+        self.group_count = counts
+        self.sel_xy = torch.stack((x[order], y[order]), -1)
+        self.sel_index = order
+
+    def for_images(self, image0: int, images: int):
+        """(selected int32 [n, 4], groups int32 [g, 4]) for images [image0, image0 + images),
+        with chunk-local tiles and output indices."""
+        low, high = image0 * self.tiles_per_image, (image0 + images) * self.tiles_per_image
+        keep = (self.group_tile >= low) & (self.group_tile < high)
+        groups = torch.stack((self.group_tile[keep] - low, self.group_first[keep],
+                              self.group_count[keep], torch.zeros_like(self.group_first[keep])),
+                             -1).to(torch.int32).contiguous()
+        selected = torch.cat((self.sel_xy, (self.sel_index - image0 * self.count)[:, None],
+                              torch.zeros_like(self.sel_index)[:, None]), -1)
+        return selected.to(torch.int32).contiguous(), groups
+
+
 class Composite(torch.autograd.Function):
     """Tile compositor forward/backward (rasterize.cu:229-399) over binned records.
 
@@ -135,41 +183,53 @@ class Composite(torch.autograd.Function):
     reference's.  The maps come out as the five planes of ``PLANES`` (the reference
     slices one [..][9] array into the same five outputs): each output's gradient goes
     to the kernel as autograd delivers it -- broadcast, strided or absent -- with no
-    [..][9] gradient assembled.
+    [..][9] gradient assembled.  With a ``Selection`` only the selected pixels are
+    composited and every per-pixel output is [images, P, ...].
     """
 
     @staticmethod
     def forward(ctx, records, projected_means, rows, backgrounds, selected, chunks, row_mode,
                 cameras, surfels, images, width, height, neural, near_plane, far_plane,
-                median=False):
+                median=False, selection=None):
         device = records.device
-        planes = [torch.empty((images, height, width, k), device=device, dtype=torch.float32)
+        pixel_shape = (height, width) if selection is None else (selection.count,)
+        per_image = math.prod(pixel_shape)
+        planes = [torch.empty((images,) + pixel_shape + (k,), device=device, dtype=torch.float32)
                   for k in PLANES]
         # optional median depth plane and the 1-based list position it came from
-        median_depth = torch.empty((images, height, width, 1) if median else (0,),
+        median_depth = torch.empty((images,) + pixel_shape + (1,) if median else (0,),
                                    device=device, dtype=torch.float32)
-        median_index = torch.empty((images, height, width) if median else (0,), device=device,
+        median_index = torch.empty((images,) + pixel_shape if median else (0,), device=device,
                                    dtype=torch.int32)
-        state = torch.empty((images, height, width, 3), device=device, dtype=torch.float32)
-        contributors = torch.empty((images, height, width), device=device, dtype=torch.int32)
+        state = torch.empty((images,) + pixel_shape + (3,), device=device, dtype=torch.float32)
+        contributors = torch.empty((images,) + pixel_shape, device=device, dtype=torch.int32)
         stream = nat.stream_of(device)
         strides, strides_ptr = nat.host_array(ctypes.c_int64, PLANES)
+        chunk_selection = []
         for ch in chunks:
             a = _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height)
+            pixel0 = ch.image0 * per_image
+            sel = selection.for_images(ch.image0, ch.images) if selection is not None else None
+            chunk_selection.append(sel)
             outs, outs_ptr = nat.host_array(
-                ctypes.c_void_p, [_at(t, a["pixel0"] * k) for t, k in zip(planes, PLANES)])
+                ctypes.c_void_p, [_at(t, pixel0 * k) for t, k in zip(planes, PLANES)])
             nat.call("gs_composite_forward_split", a["records"], a["rows"], row_mode, None,
                      a["cameras"], surfels, ch.record_count, a["rows_count"],
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
                      nat.ptr(ch.ranges), ch.images, width, height, int(neural),
                      _composite_flags(), near_plane, far_plane, outs_ptr, strides_ptr,
-                     _at(median_depth, a["pixel0"]), 1, _at(median_index, a["pixel0"]),
-                     _at(state, a["pixel0"] * 3), _at(contributors, a["pixel0"]),
+                     _at(median_depth, pixel0), 1, _at(median_index, pixel0),
+                     None if sel is None else nat.ptr(sel[0]),
+                     None if sel is None else nat.ptr(sel[1]),
+                     0 if sel is None else sel[1].shape[0],
+                     _at(state, pixel0 * 3), _at(contributors, pixel0),
                      nat.ptr(_counters("forward", device)), stream)
         ctx.save_for_backward(records, rows, backgrounds, selected, state, contributors,
                               median_index)
         ctx.set_materialize_grads(False)   # an unused output's gradient stays None (zero)
         ctx.chunks = chunks
+        ctx.chunk_selection = chunk_selection
+        ctx.pixel_shape = pixel_shape
         ctx.options = (row_mode, cameras, surfels, images, width, height, neural, near_plane,
                        far_plane)
         return tuple(planes) + (median_depth,)
@@ -185,8 +245,10 @@ class Composite(torch.autograd.Function):
         row_mode, cameras, surfels, images, width, height, neural, near_plane, far_plane = \
             ctx.options
         device = records.device
-        grads = [_pixel_linear(g, height, width) for g in grad_planes]
-        g_median, median_px, _ = _pixel_linear(grad_median, height, width)
+        pixel_shape = ctx.pixel_shape
+        per_image = math.prod(pixel_shape)
+        grads = [_pixel_linear(g, pixel_shape) for g in grad_planes]
+        g_median, median_px, _ = _pixel_linear(grad_median, pixel_shape)
         g_records = torch.zeros_like(records)
         g_xy = torch.zeros((records.shape[0], 2), device=device, dtype=torch.float32)
         g_rows = torch.zeros_like(rows)
@@ -194,28 +256,32 @@ class Composite(torch.autograd.Function):
         stream = nat.stream_of(device)
         strides, strides_ptr = nat.host_array(
             ctypes.c_int64, [x for _, px, ch in grads for x in (px, ch)])
-        for ch in ctx.chunks:
+        for ch, sel in zip(ctx.chunks, ctx.chunk_selection):
             a = _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height)
+            pixel0 = ch.image0 * per_image
             ins, ins_ptr = nat.host_array(
-                ctypes.c_void_p, [None if g is None else g.data_ptr() + a["pixel0"] * px * 4
+                ctypes.c_void_p, [None if g is None else g.data_ptr() + pixel0 * px * 4
                                   for g, px, _ in grads])
             nat.call("gs_composite_backward_split", a["records"], a["rows"], row_mode, None,
                      a["cameras"], surfels, ch.record_count, a["rows_count"],
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
-                     nat.ptr(ch.ranges), _at(state, a["pixel0"] * 3),
-                     _at(contributors, a["pixel0"]), ins_ptr, strides_ptr,
-                     _at(median_index, a["pixel0"]) if g_median is not None else None,
-                     None if g_median is None else g_median.data_ptr() + a["pixel0"] * median_px * 4,
-                     median_px, ch.images, width, height, int(neural), near_plane, far_plane,
+                     nat.ptr(ch.ranges), _at(state, pixel0 * 3),
+                     _at(contributors, pixel0), ins_ptr, strides_ptr,
+                     _at(median_index, pixel0) if g_median is not None else None,
+                     None if g_median is None else g_median.data_ptr() + pixel0 * median_px * 4,
+                     median_px, None if sel is None else nat.ptr(sel[0]),
+                     None if sel is None else nat.ptr(sel[1]),
+                     0 if sel is None else sel[1].shape[0], ch.images, width, height,
+                     int(neural), near_plane, far_plane,
                      _at(g_records, ch.record0 * nat.RECORD_FLOATS), _at(g_xy, ch.record0 * 2),
                      _at(g_rows, a["row0"] * rows.shape[1]), _at(g_bg, ch.image0 * 3),
                      nat.ptr(_counters("backward", device)), stream)
         g_pm = g_xy if selected is None else g_xy[selected]
-        return (g_records, g_pm, g_rows, g_bg) + (None,) * 12
+        return (g_records, g_pm, g_rows, g_bg) + (None,) * 13
 
 
-def _pixel_linear(g, height, width):
-    """(tensor, pixel stride, channel stride) of a map-plane gradient [images, H, W, k].
+def _pixel_linear(g, pixel_shape):
+    """(tensor, pixel stride, channel stride) of a per-pixel gradient [images, *pixel_shape, k].
 
     The kernel reads element (pixel p, channel c) at p * pixel_stride + c * channel_stride,
     which fits a contiguous gradient and a broadcast one (all strides 0, as a mean's
@@ -226,14 +292,21 @@ def _pixel_linear(g, height, width):
         return None, 0, 0
     if g.dtype != torch.float32:
         g = g.float()
-    images, k = g.shape[0], g.shape[3]
-    s0, s1, s2, s3 = g.stride()
-    px = s2
-    fits = ((images == 1 or s0 == height * width * px) and (height == 1 or s1 == width * px))
+    k = g.shape[-1]
+    dims = (g.shape[0],) + tuple(pixel_shape)
+    strides = g.stride()
+    px = strides[len(dims) - 1]
+    fits, expect = True, px
+    for size, stride in zip(reversed(dims), reversed(strides[:len(dims)])):
+        if size != 1 and stride != expect:
+            fits = False
+            break
+        expect = expect * size
+    ch = strides[-1]
     if not fits:
         g = g.contiguous()
-        px, s3 = k, 1
-    return g, px, (s3 if k > 1 else 0)
+        px, ch = k, 1
+    return g, px, (ch if k > 1 else 0)
 
 
 def _at(t: torch.Tensor, offset: int) -> int | None:
@@ -600,7 +673,7 @@ def _check_sh(first, second, directions, degree):
 # ----------------------------------------------------------------------------------
 def render(means, quaternions, scales, opacities, appearance, view_matrices, intrinsics, width,
            height, backgrounds, packed, near_plane, far_plane, neural, sh_degree, validate,
-           median_depth=False):
+           median_depth=False, pixels=None):
     """Validate inputs, project scene/camera pairs, bin, and composite in one call."""
     if not isinstance(means, torch.Tensor) or means.ndim < 2 or means.shape[-1] != 3:
         raise ValueError("means must have shape [..., N, 3]")
@@ -650,6 +723,16 @@ def render(means, quaternions, scales, opacities, appearance, view_matrices, int
         check_tensor(name, tensor, shape, device)
     if type(median_depth) is not bool:
         raise TypeError("median_depth must be bool")
+    if pixels is not None:
+        if (not isinstance(pixels, torch.Tensor) or pixels.dtype not in (torch.int32, torch.int64)
+                or pixels.device != device or pixels.ndim < 2 or pixels.shape[-1] != 2
+                or tuple(pixels.shape[:-2]) != batch + (cameras,)):
+            raise ValueError("pixels must be an integer tensor [..., C, P, 2] on the scene's "
+                             "device")
+        if pixels.numel() and bool(((pixels[..., 0] < 0) | (pixels[..., 0] >= width)
+                                    | (pixels[..., 1] < 0) | (pixels[..., 1] >= height))
+                                   .any()):
+            raise ValueError("pixels must lie inside the image")
     if type(validate) is not bool:
         raise TypeError("validate must be bool")
     if validate:
@@ -658,12 +741,12 @@ def render(means, quaternions, scales, opacities, appearance, view_matrices, int
     with torch.cuda.device(device):
         return _render(means, quaternions, scales, opacities, appearance, view_matrices,
                        intrinsics, width, height, backgrounds, packed, near_plane, far_plane,
-                       neural, sh_degree, batch, scenes, cameras, n, median_depth)
+                       neural, sh_degree, batch, scenes, cameras, n, median_depth, pixels)
 
 
 def _render(means, quaternions, scales, opacities, appearance, view_matrices, intrinsics, width,
             height, backgrounds, packed, near_plane, far_plane, neural, sh_degree, batch, scenes,
-            cameras, n, median_depth=False):
+            cameras, n, median_depth=False, pixels=None):
     device = means.device
     S, C, N = scenes, cameras, n
     P = S * C * N
@@ -692,11 +775,17 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
     if packed:
         selected = torch.nonzero(radii > 0).reshape(-1)
         projected_means = xy[selected]
+    selection = None
+    pixel_shape = (height, width)
+    if pixels is not None:
+        selection = Selection(pixels.reshape(images, -1, 2), width, height)
+        pixel_shape = (selection.count,)
     outputs = Composite.apply(records, projected_means, rows, backgrounds.reshape(-1, 3),
                               selected, chunks, row_mode, C, max(N, 1), images, width, height,
-                              neural, float(near_plane), float(far_plane), median_depth)
+                              neural, float(near_plane), float(far_plane), median_depth,
+                              selection)
     rgb, alpha, depth, normals, distortion = (
-        plane.reshape(batch + (C, height, width, plane.shape[-1])) for plane in outputs[:5])
+        plane.reshape(batch + (C,) + pixel_shape + (plane.shape[-1],)) for plane in outputs[:5])
     ids = selected if packed else torch.arange(P, device=device)
     meta = {
         "radii": radii[selected] if packed else radii.reshape(batch + (C, N)),
@@ -710,7 +799,7 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
         "distortion": distortion,
     }
     if median_depth:
-        meta["median_depth"] = outputs[5].reshape(batch + (C, height, width, 1))
+        meta["median_depth"] = outputs[5].reshape(batch + (C,) + pixel_shape + (1,))
     return rgb, alpha, meta
 
 
@@ -736,6 +825,7 @@ def rasterize_gabors(
     sh_degree: int | None = None,
     validate: bool = True,
     median_depth: bool = False,
+    pixels: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, dict[str, Any]]:
     """Render four-frequency Gabor surfaces over arbitrary scene and camera batches.
 
@@ -752,12 +842,15 @@ def rasterize_gabors(
     release) also returns ``meta["median_depth"]`` [..., C, H, W, 1]: per pixel the depth
     of the last contribution made while the transmittance before it exceeded 0.5 (the
     2DGS convention; 0 without contributions), differentiable through that
-    contribution's depth.
+    contribution's depth.  ``pixels`` (also an addition: selected-pixel rendering is
+    outside the reference's release), integer [..., C, P, 2] (x, y) inside the image,
+    composites only those pixels: every per-pixel output is then [..., C, P, k], with
+    values identical to the same pixels of a full render.
     """
     return render(means, quaternions, scales, opacities,
                   (colors, secondary_colors, frequency_weights, frequency_magnitudes, phases),
                   view_matrices, intrinsics, width, height, backgrounds, packed, near_plane,
-                  far_plane, False, sh_degree, validate, median_depth)
+                  far_plane, False, sh_degree, validate, median_depth, pixels)
 
 
 def rasterize_neural_gabors(
@@ -780,15 +873,16 @@ def rasterize_neural_gabors(
     far_plane: float = 100.0,
     validate: bool = True,
     median_depth: bool = False,
+    pixels: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, dict[str, Any]]:
     """Render per-surface 5->6->3 SIRENs (sine frequency 30, sigmoid RGB).
 
     Same contract as the reference (rendering.py:459-502): per-primitive input
     weights/biases [..., N, 6, 5] / [..., N, 6], output weights/biases
     [..., N, 3, 6] / [..., N, 3]; network input (u/3, v/3, world view direction).
-    ``median_depth`` as for ``rasterize_gabors``.
+    ``median_depth`` and ``pixels`` as for ``rasterize_gabors``.
     """
     return render(means, quaternions, scales, opacities,
                   (input_weights, input_biases, output_weights, output_biases),
                   view_matrices, intrinsics, width, height, backgrounds, packed, near_plane,
-                  far_plane, True, None, validate, median_depth)
+                  far_plane, True, None, validate, median_depth, pixels)

@@ -215,7 +215,14 @@ int gs_composite_backward(const float* records, const float* rows, int row_mode,
  * convention; 0 without contributions) at median_depth + p * median_stride, and its
  * 1-based position in the tile's list (0: none) in median_index[p]; the backward adds
  * grad_median[p * grad_median_stride] (nullable; stride 0 broadcasts) to that
- * contribution's depth gradient. */
+ * contribution's depth gradient.
+ * Selected pixels (optional; no counterpart in the reference, which lists
+ * selected-pixel rendering outside its release): with groups non-NULL only listed
+ * pixels are composited, one CTA per group: groups[4g..4g+3] = (tile, first, count, 0)
+ * with count <= 256, every listed pixel of the group inside that tile, and
+ * selected[4i..4i+3] = (x, y, output index, 0) for i in [first, first + count).  All
+ * per-pixel arrays (planes, state, contributors, median, gradients) are then indexed by
+ * output index instead of (image H + y) W + x. */
 int gs_composite_forward_split(const float* records, const float* rows, int row_mode,
                                const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
                                int64_t records_count, int64_t rows_count,
@@ -224,8 +231,9 @@ int gs_composite_forward_split(const float* records, const float* rows, int row_
                                int neural, int flags, float near_plane, float far_plane,
                                float* const* planes, const int64_t* plane_strides,
                                float* median_depth, int64_t median_stride,
-                               int32_t* median_index, float* state, int32_t* contributors,
-                               uint64_t* counters, void* stream);
+                               int32_t* median_index, const int32_t* selected,
+                               const int32_t* groups, int64_t group_count, float* state,
+                               int32_t* contributors, uint64_t* counters, void* stream);
 int gs_composite_backward_split(const float* records, const float* rows, int row_mode,
                                 const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
                                 int64_t records_count, int64_t rows_count,
@@ -234,7 +242,8 @@ int gs_composite_backward_split(const float* records, const float* rows, int row
                                 const int32_t* contributors, const float* const* grad_planes,
                                 const int64_t* grad_strides, const int32_t* median_index,
                                 const float* grad_median, int64_t grad_median_stride,
-                                int64_t images, int width,
+                                const int32_t* selected, const int32_t* groups,
+                                int64_t group_count, int64_t images, int width,
                                 int height, int neural, float near_plane, float far_plane,
                                 float* grad_records, float* grad_xy, float* grad_rows,
                                 float* grad_backgrounds, uint64_t* counters, void* stream);

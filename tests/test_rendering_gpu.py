@@ -301,3 +301,46 @@ def test_median_depth_matches_oracle(method):
     # without the flag the key is absent and nothing changes
     _, _, plain = fn(**{k: t.detach() for k, t in mine.items()}, width=40, height=30)
     assert "median_depth" not in plain
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_selected_pixels_match_full_render(method):
+    """``pixels=`` composites only listed pixels (duplicates allowed): values equal the
+    full render's at those pixels, and gradients of a loss on them equal the full
+    render's gradients under the matching per-pixel weights."""
+    from helpers import assert_grads_close, random_scene
+
+    Wd, Hd, P = 70, 45, 600
+    v = random_scene(method, scenes=2, cameras=2, n=300, width=Wd, height=Hd, conditioned=True)
+    fn = rasterize_gabors if method == "classic" else rasterize_neural_gabors
+    g = torch.Generator(device="cuda").manual_seed(9)
+    xs = torch.randint(0, Wd, (2, 2, P), device="cuda", generator=g)
+    ys = torch.randint(0, Hd, (2, 2, P), device="cuda", generator=g)
+    xs[..., :20] = xs[..., 20:40]   # duplicated pixels
+    ys[..., :20] = ys[..., 20:40]
+    pixels = torch.stack((xs, ys), -1).to(torch.int32)
+    weights = torch.rand((2, 2, P, 3), device="cuda", generator=g)
+
+    sel = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    rgb, alpha, meta = fn(**sel, width=Wd, height=Hd, pixels=pixels, median_depth=True)
+    assert rgb.shape == (2, 2, P, 3) and alpha.shape == (2, 2, P, 1)
+    full = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    f_rgb, f_alpha, f_meta = fn(**full, width=Wd, height=Hd, median_depth=True)
+    s, c = torch.meshgrid(torch.arange(2, device="cuda"), torch.arange(2, device="cuda"),
+                          indexing="ij")
+    pick = (lambda t: t[s[..., None], c[..., None], ys.long(), xs.long()])
+    assert torch.equal(rgb, pick(f_rgb))
+    assert torch.equal(alpha, pick(f_alpha))
+    for key in ("accumulated_depth", "normals", "distortion", "median_depth"):
+        assert torch.equal(meta[key], pick(f_meta[key])), key
+    # the same loss through both paths: scatter the selected weights onto the image
+    ((rgb * weights).sum() + meta["distortion"].sum()).backward()
+    dense = torch.zeros_like(f_rgb)
+    dense.index_put_((s[..., None].expand_as(xs), c[..., None].expand_as(xs), ys.long(),
+                      xs.long()), weights, accumulate=True)
+    count = torch.zeros_like(f_meta["distortion"])
+    count.index_put_((s[..., None].expand_as(xs), c[..., None].expand_as(xs), ys.long(),
+                      xs.long()), torch.ones_like(weights[..., :1]), accumulate=True)
+    ((f_rgb * dense).sum() + (f_meta["distortion"] * count).sum()).backward()
+    for name in sel:
+        assert_grads_close(sel[name].grad, full[name].grad, name, elementwise=1e-4)
