@@ -28,6 +28,10 @@ SIGNATURES = {
                            _f, _p, _p, _p, _p, _p],
     "gs_project_backward": [_p, _p, _p, _p, _p, _p, _p, _i, _l, _l, _l, _p, _p, _p, _p, _p, _p,
                             _p, _p, _p, _p, _p, _p, _p, _p, _p],
+    "gs_project_forward_ragged": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _l, _l, _p, _l,
+                                  _i, _i, _f, _f, _p, _p, _p, _p, _p],
+    "gs_project_backward_ragged": [_p, _p, _p, _p, _p, _p, _p, _i, _l, _l, _p, _l, _l, _p, _p, _p,
+                                   _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p],
     "gs_bin_count_workspace": [_l, ctypes.POINTER(_sz)],
     "gs_bin_count": [_p, _i, _p, _p, _l, _l, _l, _i, _i, _i, _p, _sz, ctypes.POINTER(_l),
                      ctypes.POINTER(_l), _p],

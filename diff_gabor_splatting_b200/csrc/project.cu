@@ -207,13 +207,17 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
     const float* __restrict__ views, const float* __restrict__ intr,
     const float* __restrict__ sh_first, const float* __restrict__ sh_second,
     const float* __restrict__ fweights, const float* __restrict__ fmags,
-    const float* __restrict__ fphases, int64_t C, int64_t N, int tw, int th,
-    float near_plane, float far_plane, float4* __restrict__ records, float2* __restrict__ xy_out,
-    float4* __restrict__ app_rows, int* __restrict__ radii) {
+    const float* __restrict__ fphases, int64_t C, int64_t N, const int64_t* __restrict__ offsets,
+    int tw, int th, float near_plane, float far_plane, float4* __restrict__ records,
+    float2* __restrict__ xy_out, float4* __restrict__ app_rows, int* __restrict__ radii) {
     const int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t s = blockIdx.y;
+    // ragged batches: scene s owns surfels [offsets[s], offsets[s+1]) and its pairs
+    // start at C * offsets[s], camera-major like the dense layout
+    const int64_t base = offsets ? offsets[s] : s * N;
+    if (offsets) N = offsets[s + 1] - base;
     if (n >= N) return;
-    const int64_t sn = s * N + n;
+    const int64_t sn = base + n;
     Surfel v;
     load_surfel(v, means, quats, scales, sn);
     const float opacity = opacities[sn];
@@ -229,7 +233,7 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
         load_camera(cam, views, intr, s * C + c);
         Pair p;
         setup_pair(p, v, cam);
-        const int64_t pid = (s * C + c) * N + n;
+        const int64_t pid = C * base + c * N + n;
         float4* rec = records + pid * (kRec / 4);
         rec[0] = make_float4(p.T[0][0], p.T[0][1], p.T[0][2], p.T[1][0]);
         rec[1] = make_float4(p.T[1][1], p.T[1][2], p.T[2][0], p.T[2][1]);
@@ -278,7 +282,7 @@ __global__ __launch_bounds__(kProjThreads) void project_backward_kernel(
     float* __restrict__ g_quats, float* __restrict__ g_scales, float* __restrict__ g_opac,
     float* __restrict__ g_views, float* __restrict__ g_intr, float* __restrict__ g_sh1,
     float* __restrict__ g_sh2, float* __restrict__ g_w, float* __restrict__ g_m,
-    float* __restrict__ g_p, int64_t chunks) {
+    float* __restrict__ g_p, int64_t chunks, const int64_t* __restrict__ offsets) {
     extern __shared__ float cam_acc[];   // [C][kCamGrads], C <= kMaxSharedCameras
     const int lane = threadIdx.x & 31;
     const int64_t s = blockIdx.y;
@@ -288,16 +292,18 @@ __global__ __launch_bounds__(kProjThreads) void project_backward_kernel(
         __syncthreads();
     }
     constexpr int K = Degree >= 0 ? (Degree + 1) * (Degree + 1) : 1;
+    const int64_t base = offsets ? offsets[s] : s * N;   // ragged batches as in the forward
+    if (offsets) N = offsets[s + 1] - base;
     for (int64_t chunk = blockIdx.x; chunk < chunks; chunk += gridDim.x) {
         const int64_t n = chunk * blockDim.x + threadIdx.x;
         const bool live = n < N;
-        const int64_t sn = s * N + (live ? n : 0);
+        const int64_t sn = base + (live ? n : 0);
         Surfel v;
         load_surfel(v, means, quats, scales, sn);
         float gR[3][3] = {}, gmean[3] = {}, gscale[2] = {}, gop = 0.f;
         float gw[4] = {}, gm[4] = {}, gph[4] = {};
         for (int64_t c = 0; c < C; ++c) {
-            const int64_t pid = (s * C + c) * N + (live ? n : 0);
+            const int64_t pid = C * base + c * N + (live ? n : 0);
             float gr[kRec], gxy[2], gcol[6] = {};
             if (live) {
                 const float4* g4 = reinterpret_cast<const float4*>(grad_records) + pid * (kRec / 4);
@@ -473,7 +479,7 @@ __global__ __launch_bounds__(kProjThreads) void project_backward_kernel(
 #pragma unroll
                     for (int k = 0; k < K; ++k) { coef[k] = __ldg(cf + k * 3 + ch); acc[k] = 0.f; }
                     for (int64_t c = 0; c < C; ++c) {
-                        const int64_t pid = (s * C + c) * N + n;
+                        const int64_t pid = C * base + c * N + n;
                         const float g = grad_rows[pid * GS_CLASSIC_ROW_FLOATS + set * 3 + ch];
                         if (g == 0.f) continue;
                         Camera cam;
@@ -548,7 +554,8 @@ __global__ __launch_bounds__(kProjThreads) void project_backward_kernel(
 
 using namespace gs;
 
-extern "C" int gs_project_forward(const float* means, const float* quaternions, const float* scales,
+static int project_forward_impl(const char* fn, const int64_t* offsets, const float* means,
+                                const float* quaternions, const float* scales,
                                   const float* opacities, const float* view_matrices,
                                   const float* intrinsics, const float* sh_first,
                                   const float* sh_second, const float* frequency_weights,
@@ -558,13 +565,13 @@ extern "C" int gs_project_forward(const float* means, const float* quaternions, 
                                   float* records, float* xy, float* app_rows, int32_t* radii,
                                   void* stream) {
     if (scenes < 1 || cameras < 1 || surfels < 0 || width < 1 || height < 1)
-        return fail(GS_ERR_ARGUMENT, "gs_project_forward: invalid sizes");
-    if (sh_degree > 3) return fail(GS_ERR_ARGUMENT, "gs_project_forward: SH degree must be 0-3");
-    if (scenes > 65535) return fail(GS_ERR_LIMIT, "gs_project_forward: more than 65535 scenes");
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": invalid sizes");
+    if (sh_degree > 3) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": SH degree must be 0-3");
+    if (scenes > 65535) return fail(GS_ERR_LIMIT, std::string(fn) + ": more than 65535 scenes");
     if (surfels == 0) return GS_OK;
     if (sh_degree >= 0 && (!sh_first || !sh_second || !frequency_weights || !frequency_magnitudes ||
                            !phases || !app_rows))
-        return fail(GS_ERR_ARGUMENT, "gs_project_forward: SH mode needs coefficient and row buffers");
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": SH mode needs coefficient and row buffers");
     const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
     dim3 grid(unsigned((surfels + kProjThreads - 1) / kProjThreads), unsigned(scenes));
     auto s = as_stream(stream);
@@ -574,8 +581,8 @@ extern "C" int gs_project_forward(const float* means, const float* quaternions, 
 #define GS_PROJ(D)                                                                            \
     project_forward_kernel<D><<<grid, kProjThreads, 0, s>>>(                                  \
         means, quaternions, scales, opacities, view_matrices, intrinsics, sh_first, sh_second, \
-        frequency_weights, frequency_magnitudes, phases, cameras, surfels, tw, th, near_plane,  \
-        far_plane, rec, xy2, rows, radii)
+        frequency_weights, frequency_magnitudes, phases, cameras, surfels, offsets, tw, th,     \
+        near_plane, far_plane, rec, xy2, rows, radii)
     switch (sh_degree) {
         case 0: GS_PROJ(0); break;
         case 1: GS_PROJ(1); break;
@@ -588,7 +595,43 @@ extern "C" int gs_project_forward(const float* means, const float* quaternions, 
     return GS_OK;
 }
 
-extern "C" int gs_project_backward(const float* means, const float* quaternions, const float* scales,
+extern "C" int gs_project_forward(const float* means, const float* quaternions, const float* scales,
+                                  const float* opacities, const float* view_matrices,
+                                  const float* intrinsics, const float* sh_first,
+                                  const float* sh_second, const float* frequency_weights,
+                                  const float* frequency_magnitudes, const float* phases,
+                                  int sh_degree, int64_t scenes, int64_t cameras, int64_t surfels,
+                                  int width, int height, float near_plane, float far_plane,
+                                  float* records, float* xy, float* app_rows, int32_t* radii,
+                                  void* stream) {
+    return project_forward_impl("gs_project_forward", nullptr, means, quaternions, scales,
+                                opacities, view_matrices, intrinsics, sh_first, sh_second,
+                                frequency_weights, frequency_magnitudes, phases, sh_degree, scenes,
+                                cameras, surfels, width, height, near_plane, far_plane, records, xy,
+                                app_rows, radii, stream);
+}
+
+extern "C" int gs_project_forward_ragged(const float* means, const float* quaternions,
+                                         const float* scales, const float* opacities,
+                                         const float* view_matrices, const float* intrinsics,
+                                         const float* sh_first, const float* sh_second,
+                                         const float* frequency_weights,
+                                         const float* frequency_magnitudes, const float* phases,
+                                         int sh_degree, int64_t scenes, int64_t cameras,
+                                         const int64_t* scene_offsets, int64_t max_surfels,
+                                         int width, int height, float near_plane,
+                                         float far_plane, float* records, float* xy,
+                                         float* app_rows, int32_t* radii, void* stream) {
+    if (!scene_offsets) return fail(GS_ERR_ARGUMENT, "gs_project_forward_ragged: NULL offsets");
+    return project_forward_impl("gs_project_forward_ragged", scene_offsets, means, quaternions,
+                                scales, opacities, view_matrices, intrinsics, sh_first, sh_second,
+                                frequency_weights, frequency_magnitudes, phases, sh_degree, scenes,
+                                cameras, max_surfels, width, height, near_plane, far_plane, records,
+                                xy, app_rows, radii, stream);
+}
+
+static int project_backward_impl(const char* fn, const int64_t* offsets, int64_t total_surfels,
+                                 const float* means, const float* quaternions, const float* scales,
                                    const float* view_matrices, const float* intrinsics,
                                    const float* sh_first, const float* sh_second, int sh_degree,
                                    int64_t scenes, int64_t cameras, int64_t surfels,
@@ -601,13 +644,13 @@ extern "C" int gs_project_backward(const float* means, const float* quaternions,
                                    float* grad_frequency_magnitudes, float* grad_phases,
                                    void* stream) {
     if (scenes < 1 || cameras < 1 || surfels < 0)
-        return fail(GS_ERR_ARGUMENT, "gs_project_backward: invalid sizes");
-    if (sh_degree > 3) return fail(GS_ERR_ARGUMENT, "gs_project_backward: SH degree must be 0-3");
-    if (scenes > 65535) return fail(GS_ERR_LIMIT, "gs_project_backward: more than 65535 scenes");
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": invalid sizes");
+    if (sh_degree > 3) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": SH degree must be 0-3");
+    if (scenes > 65535) return fail(GS_ERR_LIMIT, std::string(fn) + ": more than 65535 scenes");
     auto s = as_stream(stream);
     GS_CUDA(cudaMemsetAsync(grad_view_matrices, 0, sizeof(float) * 16 * scenes * cameras, s));
     GS_CUDA(cudaMemsetAsync(grad_intrinsics, 0, sizeof(float) * 9 * scenes * cameras, s));
-    const int64_t sn = scenes * surfels;
+    const int64_t sn = offsets ? total_surfels : scenes * surfels;
     if (sh_degree >= 0) {
         const int64_t K = int64_t(sh_degree + 1) * (sh_degree + 1);
         GS_CUDA(cudaMemsetAsync(grad_sh_first, 0, sizeof(float) * sn * K * 3, s));
@@ -628,7 +671,8 @@ extern "C" int gs_project_backward(const float* means, const float* quaternions,
         means, quaternions, scales, view_matrices, intrinsics, sh_first, sh_second, cameras,   \
         surfels, grad_records, grad_xy, grad_app_rows, grad_means, grad_quaternions,           \
         grad_scales, grad_opacities, grad_view_matrices, grad_intrinsics, grad_sh_first,       \
-        grad_sh_second, grad_frequency_weights, grad_frequency_magnitudes, grad_phases, chunks)
+        grad_sh_second, grad_frequency_weights, grad_frequency_magnitudes, grad_phases, chunks, \
+        offsets)
     switch (sh_degree) {
         case 0: GS_PROJ_BWD(0); break;
         case 1: GS_PROJ_BWD(1); break;
@@ -639,4 +683,45 @@ extern "C" int gs_project_backward(const float* means, const float* quaternions,
 #undef GS_PROJ_BWD
     GS_CHECK_LAUNCH("project_backward_kernel");
     return GS_OK;
+}
+
+extern "C" int gs_project_backward(const float* means, const float* quaternions, const float* scales,
+                                   const float* view_matrices, const float* intrinsics,
+                                   const float* sh_first, const float* sh_second, int sh_degree,
+                                   int64_t scenes, int64_t cameras, int64_t surfels,
+                                   const float* grad_records, const float* grad_xy,
+                                   const float* grad_app_rows, float* grad_means,
+                                   float* grad_quaternions, float* grad_scales,
+                                   float* grad_opacities, float* grad_view_matrices,
+                                   float* grad_intrinsics, float* grad_sh_first,
+                                   float* grad_sh_second, float* grad_frequency_weights,
+                                   float* grad_frequency_magnitudes, float* grad_phases,
+                                   void* stream) {
+    return project_backward_impl("gs_project_backward", nullptr, 0, means, quaternions, scales,
+                                 view_matrices, intrinsics, sh_first, sh_second, sh_degree, scenes,
+                                 cameras, surfels, grad_records, grad_xy, grad_app_rows, grad_means,
+                                 grad_quaternions, grad_scales, grad_opacities, grad_view_matrices,
+                                 grad_intrinsics, grad_sh_first, grad_sh_second,
+                                 grad_frequency_weights, grad_frequency_magnitudes, grad_phases,
+                                 stream);
+}
+
+extern "C" int gs_project_backward_ragged(
+    const float* means, const float* quaternions, const float* scales, const float* view_matrices,
+    const float* intrinsics, const float* sh_first, const float* sh_second, int sh_degree,
+    int64_t scenes, int64_t cameras, const int64_t* scene_offsets, int64_t max_surfels,
+    int64_t total_surfels, const float* grad_records, const float* grad_xy,
+    const float* grad_app_rows, float* grad_means, float* grad_quaternions, float* grad_scales,
+    float* grad_opacities, float* grad_view_matrices, float* grad_intrinsics,
+    float* grad_sh_first, float* grad_sh_second, float* grad_frequency_weights,
+    float* grad_frequency_magnitudes, float* grad_phases, void* stream) {
+    if (!scene_offsets || total_surfels < 0)
+        return fail(GS_ERR_ARGUMENT, "gs_project_backward_ragged: invalid offsets");
+    return project_backward_impl("gs_project_backward_ragged", scene_offsets, total_surfels, means,
+                                 quaternions, scales, view_matrices, intrinsics, sh_first,
+                                 sh_second, sh_degree, scenes, cameras, max_surfels, grad_records,
+                                 grad_xy, grad_app_rows, grad_means, grad_quaternions, grad_scales,
+                                 grad_opacities, grad_view_matrices, grad_intrinsics,
+                                 grad_sh_first, grad_sh_second, grad_frequency_weights,
+                                 grad_frequency_magnitudes, grad_phases, stream);
 }

@@ -190,7 +190,7 @@ class Composite(torch.autograd.Function):
     @staticmethod
     def forward(ctx, records, projected_means, rows, backgrounds, selected, chunks, row_mode,
                 cameras, surfels, images, width, height, neural, near_plane, far_plane,
-                median=False, selection=None):
+                median=False, selection=None, row_ids=None):
         device = records.device
         pixel_shape = (height, width) if selection is None else (selection.count,)
         per_image = math.prod(pixel_shape)
@@ -213,7 +213,8 @@ class Composite(torch.autograd.Function):
             chunk_selection.append(sel)
             outs, outs_ptr = nat.host_array(
                 ctypes.c_void_p, [_at(t, pixel0 * k) for t, k in zip(planes, PLANES)])
-            nat.call("gs_composite_forward_split", a["records"], a["rows"], row_mode, None,
+            nat.call("gs_composite_forward_split", a["records"], a["rows"], row_mode,
+                     _at(row_ids, ch.record0),
                      a["cameras"], surfels, ch.record_count, a["rows_count"],
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
                      nat.ptr(ch.ranges), ch.images, width, height, int(neural),
@@ -228,6 +229,7 @@ class Composite(torch.autograd.Function):
                               median_index)
         ctx.set_materialize_grads(False)   # an unused output's gradient stays None (zero)
         ctx.chunks = chunks
+        ctx.row_ids = row_ids
         ctx.chunk_selection = chunk_selection
         ctx.pixel_shape = pixel_shape
         ctx.options = (row_mode, cameras, surfels, images, width, height, neural, near_plane,
@@ -262,7 +264,8 @@ class Composite(torch.autograd.Function):
             ins, ins_ptr = nat.host_array(
                 ctypes.c_void_p, [None if g is None else g.data_ptr() + pixel0 * px * 4
                                   for g, px, _ in grads])
-            nat.call("gs_composite_backward_split", a["records"], a["rows"], row_mode, None,
+            nat.call("gs_composite_backward_split", a["records"], a["rows"], row_mode,
+                     _at(ctx.row_ids, ch.record0),
                      a["cameras"], surfels, ch.record_count, a["rows_count"],
                      _at(backgrounds, ch.image0 * 3), nat.ptr(ch.point_list),
                      nat.ptr(ch.ranges), _at(state, pixel0 * 3),
@@ -277,7 +280,7 @@ class Composite(torch.autograd.Function):
                      _at(g_rows, a["row0"] * rows.shape[1]), _at(g_bg, ch.image0 * 3),
                      nat.ptr(_counters("backward", device)), stream)
         g_pm = g_xy if selected is None else g_xy[selected]
-        return (g_records, g_pm, g_rows, g_bg) + (None,) * 13
+        return (g_records, g_pm, g_rows, g_bg) + (None,) * 14
 
 
 def _pixel_linear(g, pixel_shape):

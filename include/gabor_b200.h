@@ -94,6 +94,35 @@ int gs_project_backward(const float* means, const float* quaternions, const floa
                         float* grad_frequency_magnitudes, float* grad_phases,
                         void* stream);
 
+/* Ragged scene batches (no counterpart in the reference, which lists them outside its
+ * release): scene s owns surfels [scene_offsets[s], scene_offsets[s+1]) of the
+ * concatenated per-surfel arrays (scene_offsets: device int64[S+1], starting at 0);
+ * its pairs are records [C * scene_offsets[s], C * scene_offsets[s+1]), camera-major
+ * (pair C*o_s + c*N_s + n).  max_surfels is the largest N_s, total_surfels
+ * scene_offsets[S].  Otherwise as gs_project_forward / gs_project_backward. */
+int gs_project_forward_ragged(const float* means, const float* quaternions, const float* scales,
+                              const float* opacities, const float* view_matrices,
+                              const float* intrinsics, const float* sh_first,
+                              const float* sh_second, const float* frequency_weights,
+                              const float* frequency_magnitudes, const float* phases,
+                              int sh_degree, int64_t scenes, int64_t cameras,
+                              const int64_t* scene_offsets, int64_t max_surfels, int width,
+                              int height, float near_plane, float far_plane, float* records,
+                              float* xy, float* app_rows, int32_t* radii, void* stream);
+int gs_project_backward_ragged(const float* means, const float* quaternions,
+                               const float* scales, const float* view_matrices,
+                               const float* intrinsics, const float* sh_first,
+                               const float* sh_second, int sh_degree, int64_t scenes,
+                               int64_t cameras, const int64_t* scene_offsets,
+                               int64_t max_surfels, int64_t total_surfels,
+                               const float* grad_records, const float* grad_xy,
+                               const float* grad_app_rows, float* grad_means,
+                               float* grad_quaternions, float* grad_scales,
+                               float* grad_opacities, float* grad_view_matrices,
+                               float* grad_intrinsics, float* grad_sh_first,
+                               float* grad_sh_second, float* grad_frequency_weights,
+                               float* grad_frequency_magnitudes, float* grad_phases, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Tile binning (rasterize.cu:23-69, 454-493).  Two phases around the one host
  * synchronisation the reference also has (rasterize.cu:466-468):
