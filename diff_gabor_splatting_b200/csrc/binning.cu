@@ -379,6 +379,280 @@ __global__ void ranges_kernel(int64_t I, const int64_t* __restrict__ limits,
 
 unsigned blocks_for(int64_t n) { return unsigned((n + kBinThreads - 1) / kBinThreads); }
 
+// ------------------------------------------------------------------------------
+// Tile lists from row spans, without sorting the slots.
+//
+// Every (record, tile) slot belongs to one row span (a record's tiles in one tile row),
+// and the spans come out of spans_kernel in depth order.  A stable sort of the S spans
+// by tile row (S is several times smaller than the slot count I) leaves each row's
+// spans in depth order; then, per chunk of kRowChunk consecutive spans of one row, a
+// warp counts the spans covering each tile column, an exclusive scan over a row's
+// chunks gives every chunk its starting position in each tile, and the warp writes its
+// spans' records at those positions with ranks taken in span order.  The lists are the
+// stable tile sort's lists exactly: within a tile, records in depth order.
+// ------------------------------------------------------------------------------
+constexpr int kRowChunk = 64;         // spans per chunk (one warp)
+constexpr int kRowStage = 1024;       // slots of a chunk staged in shared memory
+constexpr int kRowStageColumns = 256; // widest rows whose chunks are staged (8-bit columns)
+constexpr int kRowWarps = 8;          // warps (chunks) per block
+constexpr int kRowMaxColumns = 1024;  // tile columns this path handles (wider: slot sort)
+
+inline bool rows_path(int tw) { return tw <= kRowMaxColumns; }
+
+struct RowLayout {
+    size_t item_end, item_tile, item_record, keys_in, keys_out, idx_in, idx_out, row_first,
+        row_end, chunk_base, chunk_counts, chunk_prefix, tile_count, tile_start, temp, temp_bytes,
+        total;
+    int64_t rows, chunks_cap;
+};
+
+RowLayout row_layout(int64_t spans, int64_t images, int tw, int th) {
+    RowLayout L{};
+    L.rows = images * th;
+    L.chunks_cap = spans / kRowChunk + L.rows + 1;
+    const int64_t n_tiles = images * tw * th;
+    size_t sort_bytes = 0, scan_rows = 0, scan_tiles = 0;
+    cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, (const uint32_t*)nullptr, (uint32_t*)nullptr,
+                                    (const uint64_t*)nullptr, (uint64_t*)nullptr, int(spans), 0,
+                                    tile_bits(L.rows));
+    cub::DeviceScan::InclusiveSum(nullptr, scan_rows, (const int*)nullptr, (int*)nullptr,
+                                  int(L.rows));
+    cub::DeviceScan::ExclusiveSum(nullptr, scan_tiles, (const int*)nullptr, (int*)nullptr,
+                                  int(n_tiles));
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t at = off; off += align_up(bytes); return at; };
+    L.item_end = take(sizeof(int64_t) * spans);
+    L.item_tile = take(sizeof(uint32_t) * spans);
+    L.item_record = take(sizeof(int) * spans);
+    L.keys_in = take(sizeof(uint32_t) * spans);
+    L.keys_out = take(sizeof(uint32_t) * spans);
+    L.idx_in = take(sizeof(uint64_t) * spans);
+    L.idx_out = take(sizeof(uint64_t) * spans);
+    L.row_first = take(sizeof(int) * L.rows);
+    L.row_end = take(sizeof(int) * L.rows);
+    L.chunk_base = take(sizeof(int) * (L.rows + 1));
+    L.chunk_counts = take(sizeof(int) * L.chunks_cap * tw);
+    L.chunk_prefix = take(sizeof(int) * L.chunks_cap * tw);
+    L.tile_count = take(sizeof(int) * n_tiles);
+    L.tile_start = take(sizeof(int) * n_tiles);
+    L.temp_bytes = std::max(sort_bytes, std::max(scan_rows, scan_tiles));
+    L.temp = take(L.temp_bytes);
+    L.total = off;
+    return L;
+}
+
+// A span packed for the row sort: first column (16 bits), tile count (16 bits), record.
+__device__ __forceinline__ uint64_t pack_span(int x0, int len, int record) {
+    return uint64_t(uint32_t(x0) | uint32_t(len) << 16) | uint64_t(uint32_t(record)) << 32;
+}
+
+__device__ __forceinline__ void unpack_span(uint64_t v, int& x0, int& x1, int& record) {
+    x0 = int(v & 0xffffu);
+    x1 = x0 + int((v >> 16) & 0xffffu);
+    record = int(v >> 32);
+}
+
+__global__ void row_keys_kernel(int64_t S, const int64_t* __restrict__ item_end,
+                                const uint32_t* __restrict__ item_tile,
+                                const int* __restrict__ item_record, int tw,
+                                uint32_t* __restrict__ keys, uint64_t* __restrict__ spans) {
+    const int64_t k = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k >= S) return;
+    const uint32_t tile = item_tile[k];
+    const uint32_t row = tile / uint32_t(tw);
+    keys[k] = row;
+    spans[k] = pack_span(int(tile - row * uint32_t(tw)),
+                         int(item_end[k] - (k ? item_end[k - 1] : 0)), item_record[k]);
+}
+
+// [row_first, row_end) of each tile row in the row-sorted span list (both zeroed first)
+__global__ void row_bounds_kernel(int64_t S, const uint32_t* __restrict__ rows,
+                                  int* __restrict__ row_first, int* __restrict__ row_end) {
+    const int64_t k = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k >= S) return;
+    const uint32_t r = rows[k];
+    if (k == 0 || rows[k - 1] != r) row_first[r] = int(k);
+    if (k == S - 1 || rows[k + 1] != r) row_end[r] = int(k + 1);
+}
+
+// chunks of each row, into chunk_base[1 + row] (inclusive-scanned afterwards)
+__global__ void row_chunks_kernel(int64_t rows, const int* __restrict__ row_first,
+                                  const int* __restrict__ row_end, int* __restrict__ chunks) {
+    const int64_t r = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (r >= rows) return;
+    chunks[r] = (row_end[r] - row_first[r] + kRowChunk - 1) / kRowChunk;
+}
+
+struct RowChunk {
+    int row, begin, end;   // spans [begin, end) of the row-sorted list
+};
+
+// The chunk of a global chunk id (false past the last chunk): the row whose chunk range
+// holds it, by binary search over chunk_base[0..rows].
+__device__ __forceinline__ bool row_chunk(int64_t chunk, int64_t rows,
+                                          const int* __restrict__ chunk_base,
+                                          const int* __restrict__ row_first,
+                                          const int* __restrict__ row_end, RowChunk& c) {
+    if (chunk >= chunk_base[rows]) return false;
+    int64_t lo = 0, hi = rows - 1;   // last row with chunk_base[row] <= chunk
+    while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (chunk_base[mid] <= chunk) lo = mid; else hi = mid - 1;
+    }
+    c.row = int(lo);
+    c.begin = row_first[lo] + int(chunk - chunk_base[lo]) * kRowChunk;
+    c.end = min(c.begin + kRowChunk, row_end[lo]);
+    return true;
+}
+
+// Per chunk: how many of its spans cover each tile column (warp-private counters).
+__global__ __launch_bounds__(kRowWarps * 32) void row_count_kernel(
+    int64_t rows, int tw, const int* __restrict__ chunk_base, const int* __restrict__ row_first,
+    const int* __restrict__ row_end, const uint64_t* __restrict__ spans_by_row,
+    int* __restrict__ chunk_counts) {
+    extern __shared__ int row_smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int* count = row_smem + warp * tw;
+    RowChunk c;
+    const int64_t chunk = int64_t(blockIdx.x) * kRowWarps + warp;
+    if (!row_chunk(chunk, rows, chunk_base, row_first, row_end, c)) return;
+    for (int x = lane; x < tw; x += 32) count[x] = 0;
+    __syncwarp();
+    for (int g = c.begin + lane; g < c.end; g += 32) {
+        int x0, x1, record;
+        unpack_span(spans_by_row[g], x0, x1, record);
+        for (int x = x0; x < x1; ++x) atomicAdd(count + x, 1);
+    }
+    __syncwarp();
+    for (int x = lane; x < tw; x += 32) chunk_counts[chunk * tw + x] = count[x];
+}
+
+// Per (row, column): exclusive scan of the chunk counts over the row's chunks; the
+// total is the tile's entry count.
+__global__ void row_scan_kernel(int64_t rows, int tw, const int* __restrict__ chunk_base,
+                                const int* __restrict__ chunk_counts,
+                                int* __restrict__ chunk_prefix, int* __restrict__ tile_count) {
+    const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= rows * tw) return;
+    const int64_t row = t / tw, x = t % tw;
+    int sum = 0;
+    for (int64_t c = chunk_base[row]; c < chunk_base[row + 1]; ++c) {
+        chunk_prefix[c * tw + x] = sum;
+        sum += chunk_counts[c * tw + x];
+    }
+    tile_count[t] = sum;
+}
+
+__global__ void tile_ranges_kernel(int64_t n_tiles, const int* __restrict__ tile_count,
+                                   const int* __restrict__ tile_start, int2* __restrict__ ranges) {
+    const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= n_tiles) return;
+    const int n = tile_count[t];
+    ranges[t] = n ? make_int2(tile_start[t], tile_start[t] + n) : make_int2(0, 0);
+}
+
+// Per chunk: write each span's record into every tile it covers.  Lanes take 32 spans
+// at a time in list (depth) order; a tile's rank among them is the number of lower
+// lanes covering it (a per-column lane mask built with shared atomics), so the order
+// within a tile follows the list whatever the lanes' timing.  Chunks of rows up to
+// kRowStageColumns tiles wide with at most kRowStage slots are assembled in shared
+// memory column by column and copied out in runs (each column's slots of a chunk are
+// adjacent in the point list); others write every slot directly.
+__device__ __forceinline__ void rank_group(int x0, int x1, unsigned* lanes, int lane) {
+    for (int x = x0; x < x1; ++x) atomicOr(lanes + x, 1u << lane);
+    __syncwarp();
+}
+
+__device__ __forceinline__ void advance_group(int x0, int x1, unsigned* lanes, int* cursor,
+                                              unsigned below) {
+    __syncwarp();
+    for (int x = x0; x < x1; ++x)   // the lowest covering lane advances the column
+        if ((lanes[x] & below) == 0u) cursor[x] += __popc(lanes[x]);
+    __syncwarp();
+    for (int x = x0; x < x1; ++x) lanes[x] = 0u;
+    __syncwarp();
+}
+
+__global__ __launch_bounds__(kRowWarps * 32) void row_write_kernel(
+    int64_t rows, int tw, const int* __restrict__ chunk_base, const int* __restrict__ row_first,
+    const int* __restrict__ row_end, const uint64_t* __restrict__ spans_by_row,
+    const int* __restrict__ chunk_counts, const int* __restrict__ chunk_prefix,
+    const int* __restrict__ tile_start, int* __restrict__ point_list) {
+    extern __shared__ int row_smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool staged_rows = tw <= kRowStageColumns;
+    int* base = row_smem + warp * (staged_rows ? 3 * tw + kRowStage + kRowStage / 4 : 2 * tw);
+    unsigned* lanes = reinterpret_cast<unsigned*>(base + tw);
+    RowChunk c;
+    const int64_t chunk = int64_t(blockIdx.x) * kRowWarps + warp;
+    if (!row_chunk(chunk, rows, chunk_base, row_first, row_end, c)) return;
+    const unsigned below = (1u << lane) - 1u;
+    // slots of this chunk: its per-column counts summed
+    int total = 0;
+    for (int x = lane; x < tw; x += 32) total += chunk_counts[chunk * tw + x];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (staged_rows && total <= kRowStage) {
+        int* cursor = base + 2 * tw;                  // local offset of each column's run
+        int* staged = base + 3 * tw;                  // records, column by column
+        auto* column = reinterpret_cast<uint8_t*>(staged + kRowStage);   // their columns
+        // exclusive scan of the chunk's column counts (columns in blocks of `per` a lane)
+        const int per = (tw + 31) / 32;
+        int run = 0;
+        for (int i = 0; i < per; ++i) {
+            const int x = lane * per + i;
+            if (x < tw) run += chunk_counts[chunk * tw + x];
+        }
+        int prefix = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, prefix, o);
+            if (lane >= o) prefix += v;
+        }
+        prefix -= run;
+        for (int i = 0; i < per; ++i) {
+            const int x = lane * per + i;
+            if (x < tw) {
+                cursor[x] = prefix;
+                // global position of local slot l of column x: base[x] + l
+                base[x] = tile_start[int64_t(c.row) * tw + x] + chunk_prefix[chunk * tw + x] -
+                          prefix;
+                lanes[x] = 0u;
+                prefix += chunk_counts[chunk * tw + x];
+            }
+        }
+        __syncwarp();
+        for (int g0 = c.begin; g0 < c.end; g0 += 32) {
+            const int g = g0 + lane;
+            int x0 = 0, x1 = 0, record = 0;
+            if (g < c.end) unpack_span(spans_by_row[g], x0, x1, record);
+            rank_group(x0, x1, lanes, lane);
+            for (int x = x0; x < x1; ++x) {
+                const int local = cursor[x] + __popc(lanes[x] & below);
+                staged[local] = record;
+                column[local] = uint8_t(x);
+            }
+            advance_group(x0, x1, lanes, cursor, below);
+        }
+        __syncwarp();
+        for (int e = lane; e < total; e += 32) point_list[base[column[e]] + e] = staged[e];
+        return;
+    }
+    for (int x = lane; x < tw; x += 32) {
+        base[x] = tile_start[int64_t(c.row) * tw + x] + chunk_prefix[chunk * tw + x];
+        lanes[x] = 0u;
+    }
+    __syncwarp();
+    for (int g0 = c.begin; g0 < c.end; g0 += 32) {
+        const int g = g0 + lane;
+        int x0 = 0, x1 = 0, record = 0;
+        if (g < c.end) unpack_span(spans_by_row[g], x0, x1, record);
+        rank_group(x0, x1, lanes, lane);
+        for (int x = x0; x < x1; ++x) point_list[base[x] + __popc(lanes[x] & below)] = record;
+        advance_group(x0, x1, lanes, base, below);
+    }
+}
+
 int check_common(const char* fn, const float* records, int stride, const int32_t* radii,
                  int64_t R, int64_t per_image, int64_t images, int width, int height) {
     if (!records && R > 0) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": records is NULL");
@@ -490,6 +764,88 @@ int sort_phase(const float* records, int record_stride, const int32_t* radii,
     return GS_OK;
 }
 
+// gs_bin_sort's path for images up to kRowMaxColumns tiles wide: spans, then tile lists
+// from the row-sorted spans (row_count / row_scan / row_write) instead of the slot
+// expansion and the slot sort.
+int sort_phase_rows(const float* records, int record_stride, const int32_t* radii,
+                    const int64_t* image_ids, int64_t R, int64_t records_per_image,
+                    int64_t images, int width, int height, bool tight, const void* workspace1,
+                    void* workspace2, int64_t I, int64_t S, int32_t* point_list, int32_t* ranges,
+                    cudaStream_t s) {
+    const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    const int64_t n_tiles = images * tw * th;
+    const CountLayout C = count_layout(R);
+    const RowLayout L = row_layout(S, images, tw, th);
+    const auto* base1 = static_cast<const char*>(workspace1);
+    const auto* order = reinterpret_cast<const int*>(base1 + C.idx_out);
+    const auto* slot_end = reinterpret_cast<const int64_t*>(base1 + C.slot_end);
+    const auto* span_end = reinterpret_cast<const int64_t*>(base1 + C.span_end);
+    auto* base = static_cast<char*>(workspace2);
+    auto* item_end = reinterpret_cast<int64_t*>(base + L.item_end);
+    auto* item_tile = reinterpret_cast<uint32_t*>(base + L.item_tile);
+    auto* item_record = reinterpret_cast<int*>(base + L.item_record);
+    auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
+    auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
+    auto* idx_in = reinterpret_cast<uint64_t*>(base + L.idx_in);
+    auto* idx_out = reinterpret_cast<uint64_t*>(base + L.idx_out);
+    auto* row_first = reinterpret_cast<int*>(base + L.row_first);
+    auto* row_end = reinterpret_cast<int*>(base + L.row_end);
+    auto* chunk_base = reinterpret_cast<int*>(base + L.chunk_base);
+    auto* chunk_counts = reinterpret_cast<int*>(base + L.chunk_counts);
+    auto* tile_count = reinterpret_cast<int*>(base + L.tile_count);
+    auto* tile_start = reinterpret_cast<int*>(base + L.tile_start);
+    void* temp = base + L.temp;
+    spans_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii, order,
+                                                       slot_end, span_end, image_ids,
+                                                       records_per_image, tw, th, tight, nullptr,
+                                                       item_end, item_tile, item_record);
+    GS_CHECK_LAUNCH("spans_kernel");
+    row_keys_kernel<<<blocks_for(S), kBinThreads, 0, s>>>(S, item_end, item_tile, item_record, tw,
+                                                          keys_in, idx_in);
+    GS_CHECK_LAUNCH("row_keys_kernel");
+    size_t temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx_in, idx_out,
+                                            int(S), 0, tile_bits(L.rows), s));
+    GS_CUDA(cudaMemsetAsync(row_first, 0, sizeof(int) * L.rows, s));
+    GS_CUDA(cudaMemsetAsync(row_end, 0, sizeof(int) * L.rows, s));
+    row_bounds_kernel<<<blocks_for(S), kBinThreads, 0, s>>>(S, keys_out, row_first, row_end);
+    GS_CHECK_LAUNCH("row_bounds_kernel");
+    // chunks per row (staged in tile_count), inclusive-scanned into chunk_base[1..rows]
+    row_chunks_kernel<<<blocks_for(L.rows), kBinThreads, 0, s>>>(L.rows, row_first, row_end,
+                                                                 tile_count);
+    GS_CHECK_LAUNCH("row_chunks_kernel");
+    GS_CUDA(cudaMemsetAsync(chunk_base, 0, sizeof(int), s));
+    temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, tile_count, chunk_base + 1,
+                                          int(L.rows), s));
+    const unsigned chunk_blocks = unsigned((L.chunks_cap + kRowWarps - 1) / kRowWarps);
+    const size_t count_smem = sizeof(int) * kRowWarps * tw;
+    row_count_kernel<<<chunk_blocks, kRowWarps * 32, count_smem, s>>>(
+        L.rows, tw, chunk_base, row_first, row_end, idx_out, chunk_counts);
+    GS_CHECK_LAUNCH("row_count_kernel");
+    auto* chunk_prefix = reinterpret_cast<int*>(base + L.chunk_prefix);
+    row_scan_kernel<<<blocks_for(L.rows * tw), kBinThreads, 0, s>>>(
+        L.rows, tw, chunk_base, chunk_counts, chunk_prefix, tile_count);
+    GS_CHECK_LAUNCH("row_scan_kernel");
+    temp_bytes = L.temp_bytes;
+    GS_CUDA(cub::DeviceScan::ExclusiveSum(temp, temp_bytes, tile_count, tile_start, int(n_tiles), s));
+    tile_ranges_kernel<<<blocks_for(n_tiles), kBinThreads, 0, s>>>(
+        n_tiles, tile_count, tile_start, reinterpret_cast<int2*>(ranges));
+    GS_CHECK_LAUNCH("tile_ranges_kernel");
+    const size_t write_smem =
+        sizeof(int) * kRowWarps *
+        (tw <= kRowStageColumns ? 3 * tw + kRowStage + kRowStage / 4 : 2 * tw);
+    if (write_smem > 48 * 1024)
+        GS_CUDA(cudaFuncSetAttribute(row_write_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     int(write_smem)));
+    row_write_kernel<<<chunk_blocks, kRowWarps * 32, write_smem, s>>>(
+        L.rows, tw, chunk_base, row_first, row_end, idx_out, chunk_counts, chunk_prefix,
+        tile_start, point_list);
+    GS_CHECK_LAUNCH("row_write_kernel");
+    (void)I;
+    return GS_OK;
+}
+
 // Arena mode: report the live counts and zero them when they exceed the arena.
 __global__ void arena_limits_kernel(int64_t R, const int64_t* __restrict__ slot_end,
                                     const int64_t* __restrict__ span_end, int64_t max_slots,
@@ -552,7 +908,12 @@ extern "C" int gs_bin_sort_workspace(int64_t records, int64_t intersections, int
     if (intersections > INT_MAX)
         return fail(GS_ERR_LIMIT, "gs_bin_sort_workspace: tile intersection count exceeds int32");
     const int64_t tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
-    *bytes = intersections ? sort_layout(intersections, spans, images * tw * th).total : 0;
+    if (!intersections)
+        *bytes = 0;
+    else if (rows_path(int(tw)))
+        *bytes = row_layout(spans, images, int(tw), int(th)).total;
+    else
+        *bytes = sort_layout(intersections, spans, images * tw * th).total;
     return GS_OK;
 }
 
@@ -581,9 +942,14 @@ extern "C" int gs_bin_sort(const float* records, int record_stride, const int32_
     const CountLayout C = count_layout(R);
     if (!workspace1 || workspace1_bytes < C.total)
         return fail(GS_ERR_WORKSPACE, "gs_bin_sort: workspace 1 too small");
-    const SortLayout L = sort_layout(I, spans, n_tiles);
-    if (!workspace2 || workspace2_bytes < L.total)
+    const size_t needed = rows_path(tw) ? row_layout(spans, images, tw, th).total
+                                        : sort_layout(I, spans, n_tiles).total;
+    if (!workspace2 || workspace2_bytes < needed)
         return fail(GS_ERR_WORKSPACE, "gs_bin_sort: workspace 2 too small");
+    if (rows_path(tw))
+        return sort_phase_rows(records, record_stride, radii, image_ids, R, records_per_image,
+                               images, width, height, tight, workspace1, workspace2, I, spans,
+                               point_list, ranges, s);
     return sort_phase(records, record_stride, radii, image_ids, R, records_per_image, images, width,
                       height, tight, workspace1, workspace2, I, spans, nullptr, point_list, ranges,
                       s);
