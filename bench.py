@@ -42,7 +42,7 @@ PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # my kernels launched per C entry point (CUB library kernels are not counted)
 OWN_KERNELS = {"gs_project_forward": 1, "gs_project_backward": 1, "gs_bin_count": 2,
-               "gs_bin_sort": 4, "gs_composite_forward": 1, "gs_composite_backward": 1,
+               "gs_bin_sort": 8, "gs_composite_forward": 1, "gs_composite_backward": 1,
                "gs_composite_forward_split": 1, "gs_composite_backward_split": 1,
                "gs_sh_forward": 1, "gs_sh_backward": 1, "gs_pack_geometry": 1,
                "gs_pack_rows": 1, "gs_unpack_geometry_grads": 1, "gs_unpack_rows": 1,

@@ -93,15 +93,12 @@ def stage_model(name: str, counts: dict, w) -> dict:
                     basis=f"{TEST_FLOP} flop/test x tests + {BACKWARD_ACCEPT_FLOP[w.method]} "
                           "flop/accept x accepts (kernel counters)")
     if name == "gs_bin_sort":
-        # spans: 16 B written per span (end, tile, record) and read back twice (owner
-        # table, expand); expand writes key+value 8 B/slot; each 8-bit radix pass of the
-        # tile sort reads and writes key+value 16 B/slot (+4 B/slot for the histograms,
-        # once); ranges read the sorted keys 4 B/slot
-        P = counts.get("sort_passes", 2 * I)
+        # per row span: 16 B written by the span writer, read and packed (16 + 12 B),
+        # sorted by row over 2 passes of 12 B read + written, read by the count and write
+        # kernels (8 B each); per intersection the 4-byte point-list entry
         Sp = counts.get("spans", 0)
-        return dict(bound="hbm", unit="GB/s", work=Sp * 48 + I * (8 + 4 + 4) + 16 * P,
-                    basis="48 B per row span + 16 B per intersection + 16 B per intersection"
-                          " and radix pass")
+        return dict(bound="hbm", unit="GB/s", work=Sp * (16 + 28 + 48 + 16) + I * 4,
+                    basis="108 B per row span + 4 B per intersection")
     if name == "gs_bin_count":
         # depth keys 8 B written/record; 32-bit key-value depth sort, 4 passes of 16 B +
         # 4 B histogram read; tile and span counts 16 B written; two scans 32 B
