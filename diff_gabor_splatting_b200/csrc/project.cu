@@ -242,26 +242,50 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
         rec[4] = make_float4(p.dir[2], opacity, 0.f, 0.f);
         xy_out[pid] = make_float2(p.xy[0], p.xy[1]);
         radii[pid] = pair_radius(p, tw, th, near_plane, far_plane);
-        if constexpr (Degree >= 0) {
-            float basis[K];
-            sh_basis<Degree>(p.dir[0], p.dir[1], p.dir[2], basis);
-            float col[6];
-            const float* coeffs[2] = {sh_first + sn * K * 3, sh_second + sn * K * 3};
+        if constexpr (Degree >= 0) {   // wave parameters; the colours follow per set
+            float4* row = app_rows + pid * (GS_CLASSIC_ROW_FLOATS / 4);
+            reinterpret_cast<float2*>(row + 1)[1] = make_float2(wv.x, wv.y);
+            row[2] = make_float4(wv.z, wv.w, mv.x, mv.y);
+            row[3] = make_float4(mv.z, mv.w, pv.x, pv.y);
+            row[4] = make_float4(pv.z, pv.w, 0.f, 0.f);
+        }
+    }
+    if constexpr (Degree >= 0) {
+        // Both clamped SH colours, one coefficient set at a time: the set's 3K
+        // coefficients are read once into registers (16-byte loads when the layout
+        // allows), then evaluated for every camera; the direction is recomputed with
+        // the same rounded operations as setup_pair.
+#pragma unroll 1
+        for (int set = 0; set < 2; ++set) {
+            const float* src = (set == 0 ? sh_first : sh_second) + sn * K * 3;
+            float coef[K * 3];
+            if constexpr ((K * 3) % 4 == 0) {
 #pragma unroll
-            for (int set = 0; set < 2; ++set)
+                for (int i = 0; i < K * 3 / 4; ++i) {
+                    const float4 q = __ldg(reinterpret_cast<const float4*>(src) + i);
+                    coef[4 * i] = q.x; coef[4 * i + 1] = q.y;
+                    coef[4 * i + 2] = q.z; coef[4 * i + 3] = q.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < K * 3; ++i) coef[i] = __ldg(src + i);
+            }
+            for (int64_t c = 0; c < C; ++c) {
+                Camera cam;
+                load_camera(cam, views, intr, s * C + c);
+                float dir[3], basis[K];
+                view_direction(v, cam, dir);
+                sh_basis<Degree>(dir[0], dir[1], dir[2], basis);
+                float* row = reinterpret_cast<float*>(app_rows) +
+                             (C * base + c * N + n) * GS_CLASSIC_ROW_FLOATS + set * 3;
 #pragma unroll
                 for (int ch = 0; ch < 3; ++ch) {
                     float raw = 0.5f;
 #pragma unroll
-                    for (int k = 0; k < K; ++k) raw += basis[k] * __ldg(coeffs[set] + k * 3 + ch);
-                    col[set * 3 + ch] = fmaxf(raw, 0.f);
+                    for (int k = 0; k < K; ++k) raw += basis[k] * coef[k * 3 + ch];
+                    row[ch] = fmaxf(raw, 0.f);
                 }
-            float4* row = app_rows + pid * (GS_CLASSIC_ROW_FLOATS / 4);
-            row[0] = make_float4(col[0], col[1], col[2], col[3]);
-            row[1] = make_float4(col[4], col[5], wv.x, wv.y);
-            row[2] = make_float4(wv.z, wv.w, mv.x, mv.y);
-            row[3] = make_float4(mv.z, mv.w, pv.x, pv.y);
-            row[4] = make_float4(pv.z, pv.w, 0.f, 0.f);
+            }
         }
     }
 }
