@@ -203,36 +203,8 @@ __global__ void depth_keys_kernel(int64_t R, const float* __restrict__ records, 
     idx[r] = int(r);
 }
 
-// Per record (depth order): tiles (slots) and non-empty tile rows (spans).
-__global__ void tile_counts_kernel(int64_t R, const float* __restrict__ records, int stride,
-                                   const int* __restrict__ radii, const int* __restrict__ order,
-                                   int tw, int th, bool tight, int64_t* __restrict__ slots,
-                                   int64_t* __restrict__ spans) {
-    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= R) return;
-    const int r = order[i];
-    const int radius = radii[r];
-    int64_t n_slots = 0, n_spans = 0;
-    if (radius > 0) {
-        const Region G = record_region(records + int64_t(r) * stride, radius, tw, th, tight);
-        if (G.rect.z > G.rect.x) {
-            if (!G.exact) {
-                n_spans = G.rect.w - G.rect.y;
-                n_slots = n_spans * (G.rect.z - G.rect.x);
-            } else {
-                for (int ty = G.rect.y; ty < G.rect.w; ++ty) {
-                    const int2 sp = row_span(G, ty);
-                    if (sp.y > sp.x) { n_slots += sp.y - sp.x; ++n_spans; }
-                }
-            }
-        }
-    }
-    slots[i] = n_slots;
-    spans[i] = n_spans;
-}
-
 // Write each record's spans (depth order) with their end slot (inclusive scan value),
-// first tile id and record.
+// first tile id and record (the slot path).
 __global__ void spans_kernel(int64_t R, const float* __restrict__ records, int stride,
                              const int* __restrict__ radii, const int* __restrict__ order,
                              const int64_t* __restrict__ slot_end,
@@ -259,6 +231,165 @@ __global__ void spans_kernel(int64_t R, const float* __restrict__ records, int s
         item_tile[k] = base + uint32_t(ty * tw + sp.x);
         item_record[k] = r;
         ++k;
+    }
+}
+
+// A span packed for the row sort: first column (16 bits), tile count (16 bits), record.
+__device__ __forceinline__ uint64_t pack_span(int x0, int len, int record) {
+    return uint64_t(uint32_t(x0) | uint32_t(len) << 16) | uint64_t(uint32_t(record)) << 32;
+}
+
+// Per record (depth order): tiles (slots) and non-empty tile rows (spans), and the row
+// path's span writer, load-balanced for tight regions, whose rows each cost an exact
+// double-precision evaluation: a warp takes 32
+// consecutive records (depth order), each lane sets up its record's region and parks it
+// in shared memory, and the warp's lanes then evaluate the 32 records' tile rows as one
+// list, 32 rows at a time, so a record with many rows no longer idles the other lanes.
+// A row's record is the last lane whose first row index is not past it.
+constexpr int kBalancedWarps = kBinThreads / 32;
+
+struct PaddedRegion {
+    Region G;
+    double pad;   // 136-byte stride: lanes reading different records' fields spread over banks
+};
+
+struct BalancedShared {
+    PaddedRegion region[kBalancedWarps][32];
+    int first[kBalancedWarps][33];      // exclusive prefix of the lanes' row counts
+    int slots[kBalancedWarps][32];      // per record: tiles, non-empty rows (counting)
+    int spans[kBalancedWarps][32];
+    int64_t out[kBalancedWarps][32];    // per record: next span index (writing)
+    int64_t end[kBalancedWarps][32];    // per record: end of its span range
+    uint32_t row_base[kBalancedWarps][32];   // per record: image * th
+    int record[kBalancedWarps][32];
+};
+
+__device__ __forceinline__ int owner_lane(const int* first, int t) {
+    int lo = 0;
+#pragma unroll
+    for (int step = 16; step >= 1; step >>= 1)
+        if (first[lo + step] <= t) lo += step;
+    return lo;
+}
+
+__global__ __launch_bounds__(kBinThreads, 2) void tile_counts_balanced_kernel(
+    int64_t R, const float* __restrict__ records, int stride, const int* __restrict__ radii,
+    const int* __restrict__ order, int tw, int th, bool tight, int64_t* __restrict__ slots,
+    int64_t* __restrict__ spans) {
+    __shared__ BalancedShared sh;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    int rows = 0;
+    int64_t n_slots = 0, n_spans = 0;
+    if (i < R) {
+        const int r = order[i];
+        const int radius = radii[r];
+        if (radius > 0) {
+            const Region G = record_region(records + int64_t(r) * stride, radius, tw, th, tight);
+            if (G.rect.z > G.rect.x) {
+                if (G.exact) {
+                    rows = max(G.rect.w - G.rect.y, 0);
+                    sh.region[warp][lane].G = G;
+                } else {
+                    n_spans = G.rect.w - G.rect.y;
+                    n_slots = n_spans * (G.rect.z - G.rect.x);
+                }
+            }
+        }
+    }
+    int incl = rows;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    int* first = sh.first[warp];
+    first[lane] = incl - rows;
+    if (lane == 31) first[32] = incl;
+    sh.slots[warp][lane] = 0;
+    sh.spans[warp][lane] = 0;
+    __syncwarp();
+    const int total = first[32];
+    for (int t = lane; t < total; t += 32) {
+        const int o = owner_lane(first, t);
+        const Region& G = sh.region[warp][o].G;
+        const int2 sp = row_span(G, G.rect.y + (t - first[o]));
+        if (sp.y > sp.x) {
+            atomicAdd(&sh.slots[warp][o], sp.y - sp.x);
+            atomicAdd(&sh.spans[warp][o], 1);
+        }
+    }
+    __syncwarp();
+    if (i >= R) return;
+    if (rows) {
+        n_slots = sh.slots[warp][lane];
+        n_spans = sh.spans[warp][lane];
+    }
+    slots[i] = n_slots;
+    spans[i] = n_spans;
+}
+
+// Row-path spans (as spans_kernel<true>), balanced: a row's output index is its record's
+// first span plus the non-empty rows before it, counted across passes per record and
+// within a pass with a ballot over the lanes holding rows of the same record.
+__global__ __launch_bounds__(kBinThreads, 2) void spans_rows_balanced_kernel(
+    int64_t R, const float* __restrict__ records, int stride, const int* __restrict__ radii,
+    const int* __restrict__ order, const int64_t* __restrict__ span_end,
+    const int64_t* __restrict__ image_ids, int64_t per_image, int tw, int th, bool tight,
+    uint32_t* __restrict__ row_keys, uint64_t* __restrict__ row_spans) {
+    __shared__ BalancedShared sh;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    int rows = 0;
+    if (i < R) {
+        const int64_t first_span = i ? span_end[i - 1] : 0;
+        if (span_end[i] != first_span) {
+            const int r = order[i];
+            const Region G = record_region(records + int64_t(r) * stride, radii[r], tw, th, tight);
+            rows = max(G.rect.w - G.rect.y, 0);
+            sh.region[warp][lane].G = G;
+            sh.out[warp][lane] = first_span;
+            sh.end[warp][lane] = span_end[i];
+            const int64_t image = image_ids ? image_ids[r] : r / per_image;
+            sh.row_base[warp][lane] = uint32_t(image * th);
+            sh.record[warp][lane] = r;
+        }
+    }
+    int incl = rows;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    int* first = sh.first[warp];
+    first[lane] = incl - rows;
+    if (lane == 31) first[32] = incl;
+    __syncwarp();
+    const int total = first[32];
+    const unsigned below = (1u << lane) - 1u;
+    for (int t0 = 0; t0 < total; t0 += 32) {
+        const int t = t0 + lane;
+        const bool live = t < total;
+        int o = 0;
+        int2 sp = make_int2(0, 0);
+        if (live) {
+            o = owner_lane(first, t);
+            const Region& G = sh.region[warp][o].G;
+            sp = row_span(G, G.rect.y + (t - first[o]));
+        }
+        const bool keep = live && sp.y > sp.x;
+        const unsigned same = __match_any_sync(0xffffffffu, live ? o : -1);
+        const unsigned kept = __ballot_sync(0xffffffffu, keep) & same;
+        const int64_t k = keep ? sh.out[warp][o] + __popc(kept & below) : 0;
+        if (keep && k < sh.end[warp][o]) {   // the count pass's range, which the rows match
+            const int ty = sh.region[warp][o].G.rect.y + (t - first[o]);
+            row_keys[k] = sh.row_base[warp][o] + uint32_t(ty);
+            row_spans[k] = pack_span(sp.x, sp.y - sp.x, sh.record[warp][o]);
+        }
+        __syncwarp();
+        // the group's highest lane moves its record's next index past this pass's rows
+        if (live && (same >> lane) == 1u) sh.out[warp][o] += __popc(kept);
+        __syncwarp();
     }
 }
 
@@ -400,9 +531,8 @@ constexpr int kRowMaxColumns = 1024;  // tile columns this path handles (wider: 
 inline bool rows_path(int tw) { return tw <= kRowMaxColumns; }
 
 struct RowLayout {
-    size_t item_end, item_tile, item_record, keys_in, keys_out, idx_in, idx_out, row_first,
-        row_end, chunk_base, chunk_counts, chunk_prefix, tile_count, tile_start, temp, temp_bytes,
-        total;
+    size_t keys_in, keys_out, idx_in, idx_out, row_first, row_end, chunk_base, chunk_row,
+        chunk_counts, chunk_prefix, tile_count, tile_start, temp, temp_bytes, total;
     int64_t rows, chunks_cap;
 };
 
@@ -421,9 +551,6 @@ RowLayout row_layout(int64_t spans, int64_t images, int tw, int th) {
                                   int(n_tiles));
     size_t off = 0;
     auto take = [&](size_t bytes) { size_t at = off; off += align_up(bytes); return at; };
-    L.item_end = take(sizeof(int64_t) * spans);
-    L.item_tile = take(sizeof(uint32_t) * spans);
-    L.item_record = take(sizeof(int) * spans);
     L.keys_in = take(sizeof(uint32_t) * spans);
     L.keys_out = take(sizeof(uint32_t) * spans);
     L.idx_in = take(sizeof(uint64_t) * spans);
@@ -431,6 +558,7 @@ RowLayout row_layout(int64_t spans, int64_t images, int tw, int th) {
     L.row_first = take(sizeof(int) * L.rows);
     L.row_end = take(sizeof(int) * L.rows);
     L.chunk_base = take(sizeof(int) * (L.rows + 1));
+    L.chunk_row = take(sizeof(int) * L.chunks_cap);
     L.chunk_counts = take(sizeof(int) * L.chunks_cap * tw);
     L.chunk_prefix = take(sizeof(int) * L.chunks_cap * tw);
     L.tile_count = take(sizeof(int) * n_tiles);
@@ -441,28 +569,10 @@ RowLayout row_layout(int64_t spans, int64_t images, int tw, int th) {
     return L;
 }
 
-// A span packed for the row sort: first column (16 bits), tile count (16 bits), record.
-__device__ __forceinline__ uint64_t pack_span(int x0, int len, int record) {
-    return uint64_t(uint32_t(x0) | uint32_t(len) << 16) | uint64_t(uint32_t(record)) << 32;
-}
-
 __device__ __forceinline__ void unpack_span(uint64_t v, int& x0, int& x1, int& record) {
     x0 = int(v & 0xffffu);
     x1 = x0 + int((v >> 16) & 0xffffu);
     record = int(v >> 32);
-}
-
-__global__ void row_keys_kernel(int64_t S, const int64_t* __restrict__ item_end,
-                                const uint32_t* __restrict__ item_tile,
-                                const int* __restrict__ item_record, int tw,
-                                uint32_t* __restrict__ keys, uint64_t* __restrict__ spans) {
-    const int64_t k = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (k >= S) return;
-    const uint32_t tile = item_tile[k];
-    const uint32_t row = tile / uint32_t(tw);
-    keys[k] = row;
-    spans[k] = pack_span(int(tile - row * uint32_t(tw)),
-                         int(item_end[k] - (k ? item_end[k - 1] : 0)), item_record[k]);
 }
 
 // [row_first, row_end) of each tile row in the row-sorted span list (both zeroed first)
@@ -483,39 +593,44 @@ __global__ void row_chunks_kernel(int64_t rows, const int* __restrict__ row_firs
     chunks[r] = (row_end[r] - row_first[r] + kRowChunk - 1) / kRowChunk;
 }
 
+// chunk_row[c] = the row of chunk c, one warp per row writing its chunks' entries
+__global__ void chunk_rows_kernel(int64_t rows, const int* __restrict__ chunk_base,
+                                  int* __restrict__ chunk_row) {
+    const int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    for (int c = chunk_base[r] + lane; c < chunk_base[r + 1]; c += 32) chunk_row[c] = int(r);
+}
+
 struct RowChunk {
     int row, begin, end;   // spans [begin, end) of the row-sorted list
 };
 
-// The chunk of a global chunk id (false past the last chunk): the row whose chunk range
-// holds it, by binary search over chunk_base[0..rows].
+// The chunk of a global chunk id (false past the last chunk).
 __device__ __forceinline__ bool row_chunk(int64_t chunk, int64_t rows,
                                           const int* __restrict__ chunk_base,
+                                          const int* __restrict__ chunk_row,
                                           const int* __restrict__ row_first,
                                           const int* __restrict__ row_end, RowChunk& c) {
     if (chunk >= chunk_base[rows]) return false;
-    int64_t lo = 0, hi = rows - 1;   // last row with chunk_base[row] <= chunk
-    while (lo < hi) {
-        const int64_t mid = (lo + hi + 1) >> 1;
-        if (chunk_base[mid] <= chunk) lo = mid; else hi = mid - 1;
-    }
-    c.row = int(lo);
-    c.begin = row_first[lo] + int(chunk - chunk_base[lo]) * kRowChunk;
-    c.end = min(c.begin + kRowChunk, row_end[lo]);
+    const int row = chunk_row[chunk];
+    c.row = row;
+    c.begin = row_first[row] + int(chunk - chunk_base[row]) * kRowChunk;
+    c.end = min(c.begin + kRowChunk, row_end[row]);
     return true;
 }
 
 // Per chunk: how many of its spans cover each tile column (warp-private counters).
 __global__ __launch_bounds__(kRowWarps * 32) void row_count_kernel(
-    int64_t rows, int tw, const int* __restrict__ chunk_base, const int* __restrict__ row_first,
-    const int* __restrict__ row_end, const uint64_t* __restrict__ spans_by_row,
-    int* __restrict__ chunk_counts) {
+    int64_t rows, int tw, const int* __restrict__ chunk_base, const int* __restrict__ chunk_row,
+    const int* __restrict__ row_first, const int* __restrict__ row_end,
+    const uint64_t* __restrict__ spans_by_row, int* __restrict__ chunk_counts) {
     extern __shared__ int row_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int* count = row_smem + warp * tw;
     RowChunk c;
     const int64_t chunk = int64_t(blockIdx.x) * kRowWarps + warp;
-    if (!row_chunk(chunk, rows, chunk_base, row_first, row_end, c)) return;
+    if (!row_chunk(chunk, rows, chunk_base, chunk_row, row_first, row_end, c)) return;
     for (int x = lane; x < tw; x += 32) count[x] = 0;
     __syncwarp();
     for (int g = c.begin + lane; g < c.end; g += 32) {
@@ -574,9 +689,10 @@ __device__ __forceinline__ void advance_group(int x0, int x1, unsigned* lanes, i
 }
 
 __global__ __launch_bounds__(kRowWarps * 32) void row_write_kernel(
-    int64_t rows, int tw, const int* __restrict__ chunk_base, const int* __restrict__ row_first,
-    const int* __restrict__ row_end, const uint64_t* __restrict__ spans_by_row,
-    const int* __restrict__ chunk_counts, const int* __restrict__ chunk_prefix,
+    int64_t rows, int tw, const int* __restrict__ chunk_base, const int* __restrict__ chunk_row,
+    const int* __restrict__ row_first, const int* __restrict__ row_end,
+    const uint64_t* __restrict__ spans_by_row, const int* __restrict__ chunk_counts,
+    const int* __restrict__ chunk_prefix,
     const int* __restrict__ tile_start, int* __restrict__ point_list) {
     extern __shared__ int row_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -585,7 +701,7 @@ __global__ __launch_bounds__(kRowWarps * 32) void row_write_kernel(
     unsigned* lanes = reinterpret_cast<unsigned*>(base + tw);
     RowChunk c;
     const int64_t chunk = int64_t(blockIdx.x) * kRowWarps + warp;
-    if (!row_chunk(chunk, rows, chunk_base, row_first, row_end, c)) return;
+    if (!row_chunk(chunk, rows, chunk_base, chunk_row, row_first, row_end, c)) return;
     const unsigned below = (1u << lane) - 1u;
     // slots of this chunk: its per-column counts summed
     int total = 0;
@@ -707,9 +823,9 @@ int count_phase(const char* fn, const float* records, int record_stride, const i
     size_t temp_bytes = L.temp_bytes;
     GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx_in, idx_out,
                                             int(R), 0, 32, s));
-    tile_counts_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii,
-                                                             idx_out, tw, th, tight, slots, n_spans);
-    GS_CHECK_LAUNCH("tile_counts_kernel");
+    tile_counts_balanced_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(
+        R, records, record_stride, radii, idx_out, tw, th, tight, slots, n_spans);
+    GS_CHECK_LAUNCH("tile_counts_balanced_kernel");
     temp_bytes = L.temp_bytes;
     GS_CUDA(cub::DeviceScan::InclusiveSum(temp, temp_bytes, slots, slot_end, int(R), s));
     temp_bytes = L.temp_bytes;
@@ -778,12 +894,8 @@ int sort_phase_rows(const float* records, int record_stride, const int32_t* radi
     const RowLayout L = row_layout(S, images, tw, th);
     const auto* base1 = static_cast<const char*>(workspace1);
     const auto* order = reinterpret_cast<const int*>(base1 + C.idx_out);
-    const auto* slot_end = reinterpret_cast<const int64_t*>(base1 + C.slot_end);
     const auto* span_end = reinterpret_cast<const int64_t*>(base1 + C.span_end);
     auto* base = static_cast<char*>(workspace2);
-    auto* item_end = reinterpret_cast<int64_t*>(base + L.item_end);
-    auto* item_tile = reinterpret_cast<uint32_t*>(base + L.item_tile);
-    auto* item_record = reinterpret_cast<int*>(base + L.item_record);
     auto* keys_in = reinterpret_cast<uint32_t*>(base + L.keys_in);
     auto* keys_out = reinterpret_cast<uint32_t*>(base + L.keys_out);
     auto* idx_in = reinterpret_cast<uint64_t*>(base + L.idx_in);
@@ -795,14 +907,10 @@ int sort_phase_rows(const float* records, int record_stride, const int32_t* radi
     auto* tile_count = reinterpret_cast<int*>(base + L.tile_count);
     auto* tile_start = reinterpret_cast<int*>(base + L.tile_start);
     void* temp = base + L.temp;
-    spans_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(R, records, record_stride, radii, order,
-                                                       slot_end, span_end, image_ids,
-                                                       records_per_image, tw, th, tight, nullptr,
-                                                       item_end, item_tile, item_record);
-    GS_CHECK_LAUNCH("spans_kernel");
-    row_keys_kernel<<<blocks_for(S), kBinThreads, 0, s>>>(S, item_end, item_tile, item_record, tw,
-                                                          keys_in, idx_in);
-    GS_CHECK_LAUNCH("row_keys_kernel");
+    spans_rows_balanced_kernel<<<blocks_for(R), kBinThreads, 0, s>>>(
+        R, records, record_stride, radii, order, span_end, image_ids, records_per_image, tw, th,
+        tight, keys_in, idx_in);
+    GS_CHECK_LAUNCH("spans_rows_balanced_kernel");
     size_t temp_bytes = L.temp_bytes;
     GS_CUDA(cub::DeviceRadixSort::SortPairs(temp, temp_bytes, keys_in, keys_out, idx_in, idx_out,
                                             int(S), 0, tile_bits(L.rows), s));
@@ -820,8 +928,11 @@ int sort_phase_rows(const float* records, int record_stride, const int32_t* radi
                                           int(L.rows), s));
     const unsigned chunk_blocks = unsigned((L.chunks_cap + kRowWarps - 1) / kRowWarps);
     const size_t count_smem = sizeof(int) * kRowWarps * tw;
+    auto* chunk_row = reinterpret_cast<int*>(base + L.chunk_row);
+    chunk_rows_kernel<<<blocks_for(L.rows * 32), kBinThreads, 0, s>>>(L.rows, chunk_base, chunk_row);
+    GS_CHECK_LAUNCH("chunk_rows_kernel");
     row_count_kernel<<<chunk_blocks, kRowWarps * 32, count_smem, s>>>(
-        L.rows, tw, chunk_base, row_first, row_end, idx_out, chunk_counts);
+        L.rows, tw, chunk_base, chunk_row, row_first, row_end, idx_out, chunk_counts);
     GS_CHECK_LAUNCH("row_count_kernel");
     auto* chunk_prefix = reinterpret_cast<int*>(base + L.chunk_prefix);
     row_scan_kernel<<<blocks_for(L.rows * tw), kBinThreads, 0, s>>>(
@@ -839,8 +950,8 @@ int sort_phase_rows(const float* records, int record_stride, const int32_t* radi
         GS_CUDA(cudaFuncSetAttribute(row_write_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      int(write_smem)));
     row_write_kernel<<<chunk_blocks, kRowWarps * 32, write_smem, s>>>(
-        L.rows, tw, chunk_base, row_first, row_end, idx_out, chunk_counts, chunk_prefix,
-        tile_start, point_list);
+        L.rows, tw, chunk_base, chunk_row, row_first, row_end, idx_out, chunk_counts,
+        chunk_prefix, tile_start, point_list);
     GS_CHECK_LAUNCH("row_write_kernel");
     (void)I;
     return GS_OK;
