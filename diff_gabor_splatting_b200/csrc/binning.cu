@@ -102,33 +102,45 @@ SortLayout sort_layout(int64_t I, int64_t spans, int64_t n_tiles) {
 // o exp(-min(rho3, rho2)/2) >= 1/255, so min(rho3, rho2) <= thr = 2 ln(255 o): it lies in
 // the image of the local disc u^2 + v^2 <= thr -- an ellipse, the same conic the
 // reference bounds for its 3-sigma disc (rendering.py:189-196) with 9 replaced by thr
-// -- or within sqrt(thr/2) pixels of the centre (the rho2 branch).  Per row band, the
-// x-range of a convex region is taken where its boundary is extreme: the ellipse's
-// leftmost/rightmost point, or the band edge nearest to it.  The level is widened by
-// 5% + 0.05 and every range by 2 pixels, so float rounding in the per-pixel test
-// cannot reach a dropped tile; records whose conic is not a bounded ellipse keep full
-// rows.  Arithmetic in double.
+// -- or within sqrt(thr/2) pixels of the centre (the rho2 branch).  The level is widened
+// by 5% + 0.05, so float rounding in the per-pixel test cannot reach a dropped tile.
+//
+// The conic is set up per record in double (its adjugate cancels badly in float) and
+// reduced to centred form: with Y = y - cy, the boundary is x = cx + a Y -/+ sqrt(p Y^2
+// + q) (p < 0 < q), its leftmost point at Y = yl and its rightmost at -yl, its height
+// |Y| <= ey.  Per row band, the x-range of the convex region is taken where its
+// boundary is extreme: at yl (or -yl) clamped into the band.  The rows evaluate that in
+// single precision with every operation's rounding explicit (no contraction), so the
+// counting and writing passes get identical rows; each range is widened by `margin` =
+// 2 pixels plus a bound on the float error of that evaluation (and each band by a bound
+// on the error of Y, so no row the double evaluation keeps is lost).  Records whose conic is
+// not a bounded ellipse, or whose centred form does not fit float, keep full rows.
 struct Region {
-    int4 rect;         // [x0, y0, x1, y1) tiles
-    bool exact;        // per-row spans from the ellipse and disc
-    double m00, m01, m02, m11, m12, m22;   // ellipse interior: (x y 1) M (x y 1)^T <= 0
-    double y_lo, y_hi, y_left, y_right;    // ellipse y-range, y of its leftmost/rightmost points
-    double cx, cy, rd;                     // low-pass disc
-};
+    int4 rect;            // [x0, y0, x1, y1) tiles
+    int exact;            // per-row spans from the ellipse and disc
+    float cx, cy;         // ellipse centre
+    float a, p, q;        // boundary x = cx + a Y -/+ sqrt(p Y^2 + q)
+    float yl, ey;         // Y of the leftmost point; half height
+    float margin;         // pixels added on both sides of each row's range
+    float dcx, dcy, rd;   // low-pass disc
+    float yerr;           // bound on the float error of Y, added to both band edges
+};   // 72 bytes: a warp reading the fields of different records spreads over the banks
 
-__device__ __forceinline__ Region record_region(const float* g, int radius, int tw, int th,
-                                               bool tight) {
+__device__ __noinline__ void record_region(const float* g, int radius, int tw, int th,
+                                           bool tight, Region* out) {
     Region R;
     R.rect = tile_rect(g[9], g[10], radius, tw, th);
-    R.exact = false;
+    R.exact = 0;
     const int4 b = R.rect;
-    if (!tight || b.z <= b.x || b.w <= b.y) return R;
+    if (!tight || b.z <= b.x || b.w <= b.y) { *out = R; return; }
     const double o = g[17];
     if (!(o * 255.0 >= 1.0 - 1e-6)) {   // alpha <= o < 1/255: never accepted
         R.rect = make_int4(b.x, b.y, b.x, b.y);
-        return R;
+        *out = R;
+        return;
     }
-    const double thr = (2.0 * log(255.0 * o)) * 1.05 + 0.05;
+    // the level's 5% widening dwarfs the single-precision logarithm's error
+    const double thr = double(2.f * __logf(255.f * g[17])) * 1.05 + 0.05;
     double T[9];
 #pragma unroll
     for (int k = 0; k < 9; ++k) T[k] = g[k];
@@ -138,57 +150,69 @@ __device__ __forceinline__ Region record_region(const float* g, int radius, int 
     };
     const double c00 = dual(0, 0), c01 = dual(0, 1), c02 = dual(0, 2), c11 = dual(1, 1),
                  c12 = dual(1, 2), c22 = dual(2, 2);
-    if (!(c22 < 0.0)) return R;   // not a bounded ellipse in front of the camera
-    const double cx = c02 / c22, cy = c12 / c22;
-    const double ex2 = cx * cx - c00 / c22, ey2 = cy * cy - c11 / c22;
-    if (!(ex2 > 0.0 && ey2 > 0.0)) return R;
-    const double ex = sqrt(ex2), ey = sqrt(ey2);
+    *out = R;
+    if (!(c22 < 0.0)) return;   // not a bounded ellipse in front of the camera
+    const double inv22 = 1.0 / c22;
+    const double cx = c02 * inv22, cy = c12 * inv22;   // centre: pole of the line at infinity
     // primal conic: adjugate of the dual, signed so the interior is negative
     double m00 = c11 * c22 - c12 * c12, m01 = c02 * c12 - c01 * c22, m02 = c01 * c12 - c02 * c11;
     double m11 = c00 * c22 - c02 * c02, m12 = c01 * c02 - c00 * c12, m22 = c00 * c11 - c01 * c01;
-    const double centre = m00 * cx * cx + 2 * m01 * cx * cy + 2 * m02 * cx + m11 * cy * cy +
-                          2 * m12 * cy + m22;
-    if (centre > 0) { m00 = -m00; m01 = -m01; m02 = -m02; m11 = -m11; m12 = -m12; m22 = -m22; }
-    if (!(m00 > 0.0) || !isfinite(m00 + m01 + m02 + m11 + m12 + m22)) return R;
-    // tangent points of the vertical tangents x = cx -/+ ex: P = C (1, 0, -x)
-    const double xl = cx - ex, xr = cx + ex;
-    const double y_left = (c01 - xl * c12) / (c02 - xl * c22);
-    const double y_right = (c01 - xr * c12) / (c02 - xr * c22);
-    if (!isfinite(y_left) || !isfinite(y_right) || !isfinite(cx) || !isfinite(cy)) return R;
-    R.m00 = m00; R.m01 = m01; R.m02 = m02; R.m11 = m11; R.m12 = m12; R.m22 = m22;
-    R.y_lo = cy - ey; R.y_hi = cy + ey; R.y_left = y_left; R.y_right = y_right;
-    R.cx = g[9]; R.cy = g[10]; R.rd = sqrt(fmax(thr * 0.5, 0.0));
-    R.exact = true;
-    return R;
+    double k = m00 * cx * cx + 2 * m01 * cx * cy + 2 * m02 * cx + m11 * cy * cy + 2 * m12 * cy + m22;
+    if (k > 0) { m00 = -m00; m01 = -m01; m11 = -m11; k = -k; }
+    if (!(m00 > 0.0)) return;
+    // m00 X^2 + 2 m01 X Y + m11 Y^2 + k = 0 solved for X
+    const double inv00 = 1.0 / m00;
+    const double a = -m01 * inv00;
+    const double pd = (m01 * m01 - m00 * m11) * (inv00 * inv00), qd = -k * inv00;
+    if (!(pd < 0.0 && qd > 0.0)) return;
+    const double inv_p = 1.0 / pd;
+    const double ey = sqrt(-qd * inv_p);
+    const double yl = -a * sqrt(qd * inv_p / (pd - a * a));
+    // Float error of a row's evaluation, each term at least twice its bound: Y = y - cy
+    // is off by at most 2^-24 (|cy| + |Y|) < ey_err; D = p Y^2 + q by 2^-22 q from the
+    // roundings of p, q, p Y and the fma, plus 2 |p Y| ey_err <= 2 (q / ey) ey_err, and
+    // near the tips (D ~ 0) sqrt(D) inherits sqrt of that whole; a Y + cx and the final
+    // sums add relative errors of their magnitudes.
+    const double ey_err = 0x1p-23 * (fabs(cy) + ey + 64.0);
+    const double margin = 2.0 + 0x1p-10 * sqrt(qd) + sqrt(4.0 * (qd / ey) * ey_err) +
+                          2.0 * fabs(a) * ey_err + 0x1p-20 * (fabs(cx) + fabs(a) * (fabs(cy) + ey));
+    R.cx = float(cx); R.cy = float(cy);
+    R.a = float(a); R.p = float(pd); R.q = float(qd);
+    R.yl = float(yl); R.ey = float(ey);
+    R.margin = float(margin);
+    R.yerr = float(2.0 * ey_err);
+    R.dcx = g[9]; R.dcy = g[10]; R.rd = float(sqrt(fmax(thr * 0.5, 0.0)));
+    const float all = R.cx + R.cy + R.a + R.p + R.q + R.yl + R.ey + R.margin + R.rd + R.yerr;
+    if (!isfinite(all) || !(R.p < 0.f) || !(R.q > 0.f)) return;
+    R.exact = 1;
+    *out = R;
 }
 
 // Tiles [x0, x1) of tile row ty (x1 <= x0: none).
 __device__ __forceinline__ int2 row_span(const Region& R, int ty) {
     if (!R.exact) return make_int2(R.rect.x, R.rect.z);
-    const double y0 = double(ty) * kTile - 2.0, y1 = double(ty) * kTile + (kTile - 1) + 2.0;
-    double lo = 1e300, hi = -1e300;
-    const double ya = fmax(y0, R.y_lo), yb = fmin(y1, R.y_hi);
+    const float y0 = float(ty * kTile - 2), y1 = float(ty * kTile + kTile + 1);
+    float lo = INFINITY, hi = -INFINITY;
+    const float ya = fmaxf(__fsub_rn(__fsub_rn(y0, R.cy), R.yerr), -R.ey);
+    const float yb = fminf(__fadd_rn(__fsub_rn(y1, R.cy), R.yerr), R.ey);
     if (ya <= yb) {
-        // x roots of m00 x^2 + 2 (m01 y + m02) x + (m11 y^2 + 2 m12 y + m22) = 0
-        auto root = [&](double y, double side) {
-            const double b = R.m01 * y + R.m02;
-            const double c = (R.m11 * y + 2.0 * R.m12) * y + R.m22;
-            const double d = fmax(b * b - R.m00 * c, 0.0);
-            return (-b + side * sqrt(d)) / R.m00;
-        };
-        lo = root(fmin(fmax(R.y_left, ya), yb), -1.0);
-        hi = root(fmin(fmax(R.y_right, ya), yb), 1.0);
+        float y = fminf(fmaxf(R.yl, ya), yb);
+        float d = fmaxf(__fmaf_rn(__fmul_rn(R.p, y), y, R.q), 0.f);
+        lo = __fsub_rn(__fmaf_rn(R.a, y, R.cx), __fsqrt_rn(d));
+        y = fminf(fmaxf(-R.yl, ya), yb);
+        d = fmaxf(__fmaf_rn(__fmul_rn(R.p, y), y, R.q), 0.f);
+        hi = __fadd_rn(__fmaf_rn(R.a, y, R.cx), __fsqrt_rn(d));
     }
-    const double dy = fmax(fmax(y0 - R.cy, R.cy - y1), 0.0);
+    const float dy = fmaxf(fmaxf(__fsub_rn(y0, R.dcy), __fsub_rn(R.dcy, y1)), 0.f);
     if (dy <= R.rd) {
-        const double hw = sqrt(R.rd * R.rd - dy * dy);
-        lo = fmin(lo, R.cx - hw);
-        hi = fmax(hi, R.cx + hw);
+        const float hw = __fsqrt_rn(__fmaf_rn(-dy, dy, __fmul_rn(R.rd, R.rd)));
+        lo = fminf(lo, __fsub_rn(R.dcx, hw));
+        hi = fmaxf(hi, __fadd_rn(R.dcx, hw));
     }
     if (!(lo <= hi)) return make_int2(R.rect.x, R.rect.x);
-    const double lim = 1e9;
-    const int x0 = int(floor(fmin(fmax(lo - 2.0, -lim), lim) / kTile));
-    const int x1 = int(floor(fmin(fmax(hi + 2.0, -lim), lim) / kTile)) + 1;
+    const float lim = 1e9f;
+    const int x0 = int(floorf(__fmul_rn(fminf(fmaxf(__fsub_rn(lo, R.margin), -lim), lim), 1.f / kTile)));
+    const int x1 = int(floorf(__fmul_rn(fminf(fmaxf(__fadd_rn(hi, R.margin), -lim), lim), 1.f / kTile))) + 1;
     return make_int2(max(R.rect.x, x0), min(R.rect.z, x1));
 }
 
@@ -220,7 +244,8 @@ __global__ void spans_kernel(int64_t R, const float* __restrict__ records, int s
     const int r = order[i];
     int64_t slot = i ? slot_end[i - 1] : 0;
     int64_t k = first_span;
-    const Region G = record_region(records + int64_t(r) * stride, radii[r], tw, th, tight);
+    Region G;
+    record_region(records + int64_t(r) * stride, radii[r], tw, th, tight, &G);
     const int64_t image = image_ids ? image_ids[r] : r / per_image;
     const uint32_t base = uint32_t(image * tw * th);
     for (int ty = G.rect.y; ty < G.rect.w; ++ty) {
@@ -248,13 +273,8 @@ __device__ __forceinline__ uint64_t pack_span(int x0, int len, int record) {
 // A row's record is the last lane whose first row index is not past it.
 constexpr int kBalancedWarps = kBinThreads / 32;
 
-struct PaddedRegion {
-    Region G;
-    double pad;   // 136-byte stride: lanes reading different records' fields spread over banks
-};
-
 struct BalancedShared {
-    PaddedRegion region[kBalancedWarps][32];
+    Region region[kBalancedWarps][32];
     int first[kBalancedWarps][33];      // exclusive prefix of the lanes' row counts
     int slots[kBalancedWarps][32];      // per record: tiles, non-empty rows (counting)
     int spans[kBalancedWarps][32];
@@ -285,11 +305,11 @@ __global__ __launch_bounds__(kBinThreads, 2) void tile_counts_balanced_kernel(
         const int r = order[i];
         const int radius = radii[r];
         if (radius > 0) {
-            const Region G = record_region(records + int64_t(r) * stride, radius, tw, th, tight);
+            Region& G = sh.region[warp][lane];
+            record_region(records + int64_t(r) * stride, radius, tw, th, tight, &G);
             if (G.rect.z > G.rect.x) {
                 if (G.exact) {
                     rows = max(G.rect.w - G.rect.y, 0);
-                    sh.region[warp][lane].G = G;
                 } else {
                     n_spans = G.rect.w - G.rect.y;
                     n_slots = n_spans * (G.rect.z - G.rect.x);
@@ -312,7 +332,7 @@ __global__ __launch_bounds__(kBinThreads, 2) void tile_counts_balanced_kernel(
     const int total = first[32];
     for (int t = lane; t < total; t += 32) {
         const int o = owner_lane(first, t);
-        const Region& G = sh.region[warp][o].G;
+        const Region& G = sh.region[warp][o];
         const int2 sp = row_span(G, G.rect.y + (t - first[o]));
         if (sp.y > sp.x) {
             atomicAdd(&sh.slots[warp][o], sp.y - sp.x);
@@ -345,9 +365,9 @@ __global__ __launch_bounds__(kBinThreads, 2) void spans_rows_balanced_kernel(
         const int64_t first_span = i ? span_end[i - 1] : 0;
         if (span_end[i] != first_span) {
             const int r = order[i];
-            const Region G = record_region(records + int64_t(r) * stride, radii[r], tw, th, tight);
+            Region& G = sh.region[warp][lane];
+            record_region(records + int64_t(r) * stride, radii[r], tw, th, tight, &G);
             rows = max(G.rect.w - G.rect.y, 0);
-            sh.region[warp][lane].G = G;
             sh.out[warp][lane] = first_span;
             sh.end[warp][lane] = span_end[i];
             const int64_t image = image_ids ? image_ids[r] : r / per_image;
@@ -374,7 +394,7 @@ __global__ __launch_bounds__(kBinThreads, 2) void spans_rows_balanced_kernel(
         int2 sp = make_int2(0, 0);
         if (live) {
             o = owner_lane(first, t);
-            const Region& G = sh.region[warp][o].G;
+            const Region& G = sh.region[warp][o];
             sp = row_span(G, G.rect.y + (t - first[o]));
         }
         const bool keep = live && sp.y > sp.x;
@@ -382,7 +402,7 @@ __global__ __launch_bounds__(kBinThreads, 2) void spans_rows_balanced_kernel(
         const unsigned kept = __ballot_sync(0xffffffffu, keep) & same;
         const int64_t k = keep ? sh.out[warp][o] + __popc(kept & below) : 0;
         if (keep && k < sh.end[warp][o]) {   // the count pass's range, which the rows match
-            const int ty = sh.region[warp][o].G.rect.y + (t - first[o]);
+            const int ty = sh.region[warp][o].rect.y + (t - first[o]);
             row_keys[k] = sh.row_base[warp][o] + uint32_t(ty);
             row_spans[k] = pack_span(sp.x, sp.y - sp.x, sh.record[warp][o]);
         }
