@@ -93,17 +93,20 @@ def stage_model(name: str, counts: dict, w) -> dict:
                     basis=f"{TEST_FLOP} flop/test x tests + {BACKWARD_ACCEPT_FLOP[w.method]} "
                           "flop/accept x accepts (kernel counters)")
     if name == "gs_bin_sort":
-        # per row span: 16 B written by the span writer, read and packed (16 + 12 B),
-        # sorted by row over 2 passes of 12 B read + written, read by the count and write
-        # kernels (8 B each); per intersection the 4-byte point-list entry
+        # per record: the span writer reads the fields its region uses (T, xy, opacity:
+        # 48 B), radius, depth order and span offset (16 B); per row span: 12 B written
+        # (row key + packed span), sorted by row over 2 passes of 12 B read + written,
+        # read by the count and write kernels (8 B each); per intersection the 4-byte
+        # point-list entry
         Sp = counts.get("spans", 0)
-        return dict(bound="hbm", unit="GB/s", work=Sp * (16 + 28 + 48 + 16) + I * 4,
-                    basis="108 B per row span + 4 B per intersection")
+        return dict(bound="hbm", unit="GB/s", work=R * 64 + Sp * (12 + 48 + 16) + I * 4,
+                    basis="64 B per record + 76 B per row span + 4 B per intersection")
     if name == "gs_bin_count":
         # depth keys 8 B written/record; 32-bit key-value depth sort, 4 passes of 16 B +
-        # 4 B histogram read; tile and span counts 16 B written; two scans 32 B
-        return dict(bound="hbm", unit="GB/s", work=R * (8 + 4 * 16 + 4 + 16 + 32),
-                    basis="124 B per record (keys, 4-pass depth sort, counts, scans)")
+        # 4 B histogram read; tile counting reads the record fields its region uses and
+        # the radius (52 B) and writes tile and span counts (16 B); two scans 32 B
+        return dict(bound="hbm", unit="GB/s", work=R * (8 + 4 * 16 + 4 + 52 + 16 + 32),
+                    basis="176 B per record (keys, 4-pass depth sort, region fields, counts, scans)")
     surfel_in = 4 * (3 + 4 + 2 + 1 + (2 * K * 3 + 12 if K else 0))
     if name == "gs_project_forward":
         pair_out = 4 * (20 + 2 + 1 + (20 if K else 0))
