@@ -296,7 +296,9 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
 constexpr int kCamGrads = 21;   // Rc (9), t (3), K (9)
 
 template <int Degree>
-__global__ __launch_bounds__(kProjThreads) void project_backward_kernel(
+// Two blocks per SM (128 registers, a few spilled): the per-pair gathers need the
+// extra warps in flight more than the registers.
+__global__ __launch_bounds__(kProjThreads, 2) void project_backward_kernel(
     const float* __restrict__ means, const float* __restrict__ quats,
     const float* __restrict__ scales, const float* __restrict__ views,
     const float* __restrict__ intr, const float* __restrict__ sh_first,

@@ -38,39 +38,43 @@ __device__ __forceinline__ void sh_basis(float x, float y, float z, float* b) {
     }
 }
 
+// gdir += sum_k h_k grad(basis_k)(x, y, z): the basis derivatives of the table above
+// contracted with per-coefficient weights h as they are formed, so the 3K derivatives
+// are never held at once.
 template <int Degree>
-__device__ __forceinline__ void sh_basis_grad(float x, float y, float z, float* dx, float* dy,
-                                              float* dz) {
-    constexpr int K = (Degree + 1) * (Degree + 1);
-#pragma unroll
-    for (int k = 0; k < K; ++k) dx[k] = dy[k] = dz[k] = 0.f;
+__device__ __forceinline__ void sh_basis_grad_dot(float x, float y, float z, const float* h,
+                                                  float* gdir) {
+    float gx = 0.f, gy = 0.f, gz = 0.f;
     if constexpr (Degree > 0) {
         constexpr float c1 = 0.4886025119029199f;
-        dy[1] = -c1;
-        dz[2] = c1;
-        dx[3] = -c1;
+        gy -= c1 * h[1];
+        gz += c1 * h[2];
+        gx -= c1 * h[3];
     }
     if constexpr (Degree > 1) {
         constexpr float a = 1.0925484305920792f, c = 0.31539156525252005f,
                         d = 0.5462742152960396f;
-        dx[4] = a * y; dy[4] = a * x;
-        dy[5] = -a * z; dz[5] = -a * y;
-        dx[6] = -2 * c * x; dy[6] = -2 * c * y; dz[6] = 4 * c * z;
-        dx[7] = -a * z; dz[7] = -a * x;
-        dx[8] = 2 * d * x; dy[8] = -2 * d * y;
+        gx += a * y * h[4] - a * z * h[7] - 2 * c * x * h[6] + 2 * d * x * h[8];
+        gy += a * x * h[4] - a * z * h[5] - 2 * c * y * h[6] - 2 * d * y * h[8];
+        gz += -a * y * h[5] + 4 * c * z * h[6] - a * x * h[7];
     }
     if constexpr (Degree > 2) {
         constexpr float a = -0.5900435899266435f, b1 = 2.890611442640554f,
                         c = -0.4570457994644658f, d = 0.3731763325901154f,
                         e = 1.445305721320277f;
-        dx[9] = 6 * a * x * y; dy[9] = 3 * a * (x * x - y * y);
-        dx[10] = b1 * y * z; dy[10] = b1 * x * z; dz[10] = b1 * x * y;
-        dx[11] = -2 * c * x * y; dy[11] = c * (4 * z * z - x * x - 3 * y * y); dz[11] = 8 * c * y * z;
-        dx[12] = -6 * d * x * z; dy[12] = -6 * d * y * z; dz[12] = d * (6 * z * z - 3 * x * x - 3 * y * y);
-        dx[13] = c * (4 * z * z - 3 * x * x - y * y); dy[13] = -2 * c * x * y; dz[13] = 8 * c * x * z;
-        dx[14] = 2 * e * x * z; dy[14] = -2 * e * y * z; dz[14] = e * (x * x - y * y);
-        dx[15] = 3 * a * (x * x - y * y); dy[15] = -6 * a * x * y;
+        const float xx = x * x, yy = y * y, zz = z * z;
+        gx += 6 * a * x * y * h[9] + b1 * y * z * h[10] - 2 * c * x * y * h[11] -
+              6 * d * x * z * h[12] + c * (4 * zz - 3 * xx - yy) * h[13] + 2 * e * x * z * h[14] +
+              3 * a * (xx - yy) * h[15];
+        gy += 3 * a * (xx - yy) * h[9] + b1 * x * z * h[10] + c * (4 * zz - xx - 3 * yy) * h[11] -
+              6 * d * y * z * h[12] - 2 * c * x * y * h[13] - 2 * e * y * z * h[14] -
+              6 * a * x * y * h[15];
+        gz += b1 * x * y * h[10] + 8 * c * y * z * h[11] + d * (6 * zz - 3 * xx - 3 * yy) * h[12] +
+              8 * c * x * z * h[13] + e * (xx - yy) * h[14];
     }
+    gdir[0] += gx;
+    gdir[1] += gy;
+    gdir[2] += gz;
 }
 
 // Clamped colour raw = 0.5 + sum_k basis_k coef_k (spherical_harmonics.cu:62-64).
@@ -94,26 +98,32 @@ __device__ __forceinline__ void sh_direction_grad(const float* dir, const float*
 #pragma unroll
     for (int i = 0; i < 6; ++i) any = any || gcol[i] != 0.f;
     if (!any) return;
-    float basis[K], dx[K], dy[K], dz[K];
+    // Each clamped channel that passes weights its coefficients: h_k = sum over (set,
+    // channel) of g * coef_k, and d/ddir sum_k basis_k coef_k g = sum_k h_k grad(basis_k).
+    // One (set, channel) at a time, so only its K coefficients are live.
+    float basis[K], h[K];
     sh_basis<Degree>(dir[0], dir[1], dir[2], basis);
-    sh_basis_grad<Degree>(dir[0], dir[1], dir[2], dx, dy, dz);
 #pragma unroll
-    for (int set = 0; set < 2; ++set) {
-        const float* coeffs = set == 0 ? first : second;
+    for (int k = 0; k < K; ++k) h[k] = 0.f;
+#pragma unroll 1
+    for (int sc = 0; sc < 6; ++sc) {
+        float g = gcol[0];
 #pragma unroll
-        for (int ch = 0; ch < 3; ++ch) {
-            const float raw = sh_raw<Degree>(basis, coeffs, ch);
-            const float g = raw >= 0.f ? gcol[set * 3 + ch] : 0.f;
-            if (g == 0.f) continue;
+        for (int i = 1; i < 6; ++i) g = sc == i ? gcol[i] : g;
+        if (g == 0.f) continue;
+        const float* coeffs = (sc < 3 ? first : second) + (sc < 3 ? sc : sc - 3);
+        float coef[K];
+        float raw = 0.5f;
 #pragma unroll
-            for (int k = 0; k < K; ++k) {
-                const float cf = __ldg(coeffs + k * 3 + ch);
-                gdir[0] += g * cf * dx[k];
-                gdir[1] += g * cf * dy[k];
-                gdir[2] += g * cf * dz[k];
-            }
+        for (int k = 0; k < K; ++k) {
+            coef[k] = __ldg(coeffs + k * 3);
+            raw += basis[k] * coef[k];
         }
+        if (!(raw >= 0.f)) continue;   // clamped: adds nothing
+#pragma unroll
+        for (int k = 0; k < K; ++k) h[k] = fmaf(g, coef[k], h[k]);
     }
+    sh_basis_grad_dot<Degree>(dir[0], dir[1], dir[2], h, gdir);
 }
 
 }  // namespace gs
