@@ -213,6 +213,69 @@ __device__ __forceinline__ void load_batch(B& b, const Params& P, int first, int
     __syncthreads();
 }
 
+// Asynchronous staging for double-buffered batches: every element of a batch is a
+// 16-byte cp.async (LDGSTS) into shared memory, issued while the previous batch is
+// composited; `finish_batch` waits for this thread's own copies and applies the same
+// per-record fixups as load_batch to the elements this thread copied (the half weight
+// sum needs weights 0-1, so the thread copying weights 2-3 also copies them into a
+// scratch slot).  The caller's next barrier makes the batch visible to all threads.
+__device__ __forceinline__ void copy16_async(void* smem, const void* gmem) {
+    const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem) : "memory");
+}
+
+template <class B>
+__device__ __forceinline__ void issue_batch(B& b, float4* weights01, const Params& P, int first,
+                                            int count, int rank) {
+    constexpr int kRow = B::kRow;
+    constexpr int kPer = kRec / 4 + kRow / 4;
+    for (int i = rank; i < count * kPer; i += kBlock) {
+        const int e = i / kPer, part = i % kPer;
+        const int id = __ldg(P.point_list + first + e);
+        if (part < kRec / 4) {
+            if (part == 0) b.ids[e] = id;
+            copy16_async(&b.geo[e][part], P.records + int64_t(id) * (kRec / 4) + part);
+        } else {
+            const int q = part - kRec / 4;
+            const int64_t row = row_of(P, id);
+            if (q == 0) b.rows[e] = row;
+            copy16_async(&b.app[e][q], P.rows + row * (kRow / 4) + q);
+            if (!B::kNeural && q == 2) copy16_async(&weights01[e], P.rows + row * (kRow / 4) + 1);
+        }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+template <class B>
+__device__ __forceinline__ void finish_batch(B& b, const float4* weights01, int count, int rank) {
+    constexpr int kRow = B::kRow;
+    constexpr int kPer = kRec / 4 + kRow / 4;
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    for (int i = rank; i < count * kPer; i += kBlock) {
+        const int e = i / kPer, part = i % kPer;
+        if (part == 4) {   // slot 18 (pad in memory) <- rejection threshold of the opacity
+            float4& v = b.geo[e][4];
+            v.z = reject_threshold(v.y);
+        }
+        if constexpr (!B::kNeural) {
+            constexpr float kTwoPi = 2 * kPi;
+            const int q = part - kRec / 4;
+            if (q == 2) {   // weights 2-3, magnitudes 0-1
+                float4& v = b.app[e][2];
+                const float4 w01 = weights01[e];
+                b.half_weight[e] = 0.5f * ((w01.z + w01.w) + (v.x + v.y));
+                v.z = kTwoPi * v.z;
+                v.w = kTwoPi * v.w;
+            }
+            if (q == 3) {   // magnitudes 2-3
+                float4& v = b.app[e][3];
+                v.x = kTwoPi * v.x;
+                v.y = kTwoPi * v.y;
+            }
+        }
+    }
+}
+
 struct Sample {
     float k[3], l[3], p[3], s[2], depth, expo, alpha;
     bool surface;
@@ -347,9 +410,10 @@ __device__ __forceinline__ void appearance_forward(const float* a, const float* 
 }
 
 template <bool Neural, bool Count, bool Exact, bool Median>
-__global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params P) {
+__global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Params P) {
     unsigned tests = 0, accepts = 0;
-    __shared__ Batch<Neural> batch;
+    __shared__ Batch<Neural> batches[2];
+    __shared__ float4 weights01[2][Neural ? 1 : kBatch];
     const int rank = threadIdx.y * kTile + threadIdx.x;
     const PixelSlot slot = pixel_slot(P, rank);
     const int tile = slot.tile, image = slot.image, x = slot.x, y = slot.y;
@@ -363,10 +427,18 @@ __global__ __launch_bounds__(kBlock) void composite_forward_kernel(const Params 
     const Directions dirs;
     const float mscale = P.far_plane / (P.far_plane - P.near_plane);
     const float mscale_near = mscale * P.near_plane;
-    for (int start = range.x; start < range.y; start += kBatch) {
-        if (__syncthreads_count(done) == kBlock) break;
+    // Double-buffered batches: batch b+1's copies are in flight while batch b is
+    // composited; one barrier per batch (after this thread's copies of batch b landed and
+    // were fixed up) makes batch b visible and retires batch b-1's buffer.
+    if (range.x < range.y) issue_batch(batches[0], weights01[0], P, range.x, min(kBatch, range.y - range.x), rank);
+    for (int start = range.x, b = 0; start < range.y; start += kBatch, ++b) {
+        auto& batch = batches[b & 1];
         const int count = min(kBatch, range.y - start);
-        load_batch(batch, P, start, 1, count, rank);
+        finish_batch(batch, weights01[b & 1], count, rank);
+        if (__syncthreads_count(done) == kBlock) break;
+        if (start + kBatch < range.y)
+            issue_batch(batches[(b + 1) & 1], weights01[(b + 1) & 1], P, start + kBatch,
+                        min(kBatch, range.y - start - kBatch), rank);
         for (int j = 0; j < count && !done; ++j) {
             const float* g = reinterpret_cast<const float*>(batch.geo[j]);
             Sample v;
