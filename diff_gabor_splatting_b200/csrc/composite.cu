@@ -169,56 +169,18 @@ struct Batch {
     float half_weight[Neural ? 1 : kSize];   // classic: half the sum of the 4 wave weights
 };
 
-// Stage `count` records (list positions first + stride*e) and their rows.  Per record
-// it also stores the early-rejection threshold in record slot 18 (memory pad) and,
-// for classic rows, 2*pi*magnitude in place of each magnitude: the factor every wave
-// argument uses, computed once per record instead of once per sample (the same
-// float product the per-sample expression 2 * pi * magnitude rounds to).
-template <class B>
-__device__ __forceinline__ void load_batch(B& b, const Params& P, int first, int stride,
-                                           int count, int rank, unsigned* reset = nullptr) {
-    constexpr int kRow = B::kRow;
-    constexpr int kPer = kRec / 4 + kRow / 4;
-    __syncthreads();   // the previous batch is no longer read
-    // each loading thread reads its record id (L1-cached), so ids need no barrier of
-    // their own; the part-0 thread keeps it for the kernels' gradient writes
-    if (reset && rank < B::kCapacity) reset[rank] = 0u;   // reset[] has one entry per slot
-    for (int i = rank; i < count * kPer; i += kBlock) {
-        const int e = i / kPer, part = i % kPer;
-        const int id = __ldg(P.point_list + first + stride * e);
-        if (part < kRec / 4) {
-            if (part == 0) b.ids[e] = id;
-            float4 v = __ldg(P.records + int64_t(id) * (kRec / 4) + part);
-            // slot 18 (pad in memory) <- rejection threshold of this record's opacity
-            if (part == 4) v.z = reject_threshold(v.y);
-            b.geo[e][part] = v;
-        } else {
-            const int q = part - kRec / 4;
-            const int64_t row = row_of(P, id);
-            if (q == 0) b.rows[e] = row;
-            float4 v = __ldg(P.rows + row * (kRow / 4) + q);
-            if constexpr (!B::kNeural) {
-                constexpr float kTwoPi = 2 * kPi;
-                if (q == 2) {   // weights 2-3, magnitudes 0-1
-                    const float4 w01 = __ldg(P.rows + row * (kRow / 4) + 1);
-                    b.half_weight[e] = 0.5f * ((w01.z + w01.w) + (v.x + v.y));
-                    v.z = kTwoPi * v.z;
-                    v.w = kTwoPi * v.w;
-                }
-                if (q == 3) { v.x = kTwoPi * v.x; v.y = kTwoPi * v.y; }   // magnitudes 2-3
-            }
-            b.app[e][q] = v;
-        }
-    }
-    __syncthreads();
-}
-
-// Asynchronous staging for double-buffered batches: every element of a batch is a
-// 16-byte cp.async (LDGSTS) into shared memory, issued while the previous batch is
-// composited; `finish_batch` waits for this thread's own copies and applies the same
-// per-record fixups as load_batch to the elements this thread copied (the half weight
-// sum needs weights 0-1, so the thread copying weights 2-3 also copies them into a
-// scratch slot).  The caller's next barrier makes the batch visible to all threads.
+// Batch staging, double-buffered: `issue_batch` stages `count` records (list positions
+// first + stride*e) and their appearance rows with one 16-byte cp.async (LDGSTS) per
+// element, issued while the previous batch is composited; `finish_batch` waits for this
+// thread's own copies and fixes up the elements it copied: record slot 18 (pad in
+// memory) gets the early-rejection threshold of the record's opacity, and classic rows
+// get 2*pi*magnitude in place of each magnitude (the factor every wave argument uses,
+// computed once per record instead of once per sample: the same float product the
+// per-sample expression 2 * pi * magnitude rounds to) and the half sum of the four wave
+// weights (the thread copying weights 2-3 also copies weights 0-1 into a scratch slot).
+// The caller's next barrier makes the batch visible to all threads.  Each loading
+// thread reads its record id (L1-cached); the part-0 thread keeps it for the kernels'
+// gradient writes.
 __device__ __forceinline__ void copy16_async(void* smem, const void* gmem) {
     const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(smem));
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(gmem) : "memory");
@@ -226,12 +188,12 @@ __device__ __forceinline__ void copy16_async(void* smem, const void* gmem) {
 
 template <class B>
 __device__ __forceinline__ void issue_batch(B& b, float4* weights01, const Params& P, int first,
-                                            int count, int rank) {
+                                            int stride, int count, int rank) {
     constexpr int kRow = B::kRow;
     constexpr int kPer = kRec / 4 + kRow / 4;
     for (int i = rank; i < count * kPer; i += kBlock) {
         const int e = i / kPer, part = i % kPer;
-        const int id = __ldg(P.point_list + first + e);
+        const int id = __ldg(P.point_list + first + stride * e);
         if (part < kRec / 4) {
             if (part == 0) b.ids[e] = id;
             copy16_async(&b.geo[e][part], P.records + int64_t(id) * (kRec / 4) + part);
@@ -430,14 +392,15 @@ __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Para
     // Double-buffered batches: batch b+1's copies are in flight while batch b is
     // composited; one barrier per batch (after this thread's copies of batch b landed and
     // were fixed up) makes batch b visible and retires batch b-1's buffer.
-    if (range.x < range.y) issue_batch(batches[0], weights01[0], P, range.x, min(kBatch, range.y - range.x), rank);
+    if (range.x < range.y)
+        issue_batch(batches[0], weights01[0], P, range.x, 1, min(kBatch, range.y - range.x), rank);
     for (int start = range.x, b = 0; start < range.y; start += kBatch, ++b) {
         auto& batch = batches[b & 1];
         const int count = min(kBatch, range.y - start);
         finish_batch(batch, weights01[b & 1], count, rank);
         if (__syncthreads_count(done) == kBlock) break;
         if (start + kBatch < range.y)
-            issue_batch(batches[(b + 1) & 1], weights01[(b + 1) & 1], P, start + kBatch,
+            issue_batch(batches[(b + 1) & 1], weights01[(b + 1) & 1], P, start + kBatch, 1,
                         min(kBatch, range.y - start - kBatch), rank);
         for (int j = 0; j < count && !done; ++j) {
             const float* g = reinterpret_cast<const float*>(batch.geo[j]);
@@ -519,10 +482,11 @@ template <bool Neural>
 struct BackShared {
     using F = Fields<Neural>;
     static constexpr int kStride = (F::kCount + 3) / 4 * 4;   // 36 classic, 76 neural
-    Batch<Neural, kBackBatch> batch;
+    Batch<Neural, kBackBatch> batch[2];        // double-buffered: batch b+1 lands during b
+    float4 weights01[2][Neural ? 1 : kBackBatch];
     float rows[kWarps][kBackBatch][kStride];   // per (warp, record) field sums
     float lanes[kWarps][32][kLaneStride];      // per-warp transpose scratch, 32 fields a pass
-    unsigned mask[kBackBatch];                 // warps that stored a row for the record
+    unsigned mask[2][kBackBatch];              // warps that stored a row for the record
     int warp_max[kWarps];
     float bg[3];
 };
@@ -576,7 +540,6 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     constexpr int kRow = Batch<Neural>::kRow;
     extern __shared__ float4 dynamic_smem[];
     S& sh = *reinterpret_cast<S*>(dynamic_smem);
-    auto& batch = sh.batch;
     int* warp_max = sh.warp_max;
     float* bg_acc = sh.bg;
     const int lane = (threadIdx.y * kTile + threadIdx.x) & 31;
@@ -591,6 +554,7 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     const int median_at = inside && P.gin_median ? P.median_index[pixel] : 0;
     const float go_median = median_at ? P.gin_median[pixel * P.gin_median_px] : 0.f;
     if (rank < 3) bg_acc[rank] = 0.f;
+    if (rank < 2 * kBackBatch) sh.mask[rank / kBackBatch][rank % kBackBatch] = 0u;
     int wmax = last;
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
@@ -630,10 +594,25 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     const float mscale_near = mscale * P.near_plane;
     const float depth_term = go[8] * 2 * mscale_near;                // d distortion / d depth
     const float background_term = final_t * (go[3] - background_dot);  // galpha's T-independent part
-    for (int start = block_last; start > 0; start -= kBackBatch) {
+    // Double-buffered batches in reverse list order: batch b+1's copies are in flight
+    // while batch b is replayed and flushed.  The barrier after this thread's copies of
+    // batch b landed also orders batch b-1's flush (its ids, rows and masks) before batch
+    // b+1's copies and mask reset reuse that buffer.
+    if (block_last > 0)
+        issue_batch(sh.batch[0], sh.weights01[0], P, range.x + block_last - 1, -1,
+                    min(kBackBatch, block_last), rank);
+    for (int start = block_last, b = 0; start > 0; start -= kBackBatch, ++b) {
         const int count = min(kBackBatch, start);
-        // masks reset after the barrier that ends the previous batch's flush
-        load_batch(batch, P, range.x + start - 1, -1, count, rank, sh.mask);
+        auto& batch = sh.batch[b & 1];
+        unsigned* mask = sh.mask[b & 1];
+        finish_batch(batch, sh.weights01[b & 1], count, rank);
+        __syncthreads();
+        if (start > kBackBatch) {
+            issue_batch(sh.batch[(b + 1) & 1], sh.weights01[(b + 1) & 1], P,
+                        range.x + start - kBackBatch - 1, -1, min(kBackBatch, start - kBackBatch),
+                        rank);
+            if (rank < kBackBatch) sh.mask[(b + 1) & 1][rank] = 0u;
+        }
         for (int j = 0; j < count; ++j) {
             const float* g = reinterpret_cast<const float*>(batch.geo[j]);
             const float* a = reinterpret_cast<const float*>(batch.app[j]);
@@ -791,18 +770,18 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                     gg[6 + k] += x * gk[k] + y * gl[k];
                 }
             }
-            warp_store<Neural>(vals, sh.lanes[warp], sh.rows[warp][j], &sh.mask[j], warp, lane);
+            warp_store<Neural>(vals, sh.lanes[warp], sh.rows[warp][j], &mask[j], warp, lane);
         }
         // flush: sum the warps' rows of each record in warp order, one global atomic per
         // (tile, record, field)
         __syncthreads();
         for (int i = rank; i < count * F::kCount; i += kBlock) {
             const int e = i / F::kCount, field = i % F::kCount;
-            const unsigned mask = sh.mask[e];
+            const unsigned stored = mask[e];
             float val = 0.f;
 #pragma unroll
             for (int w = 0; w < kWarps; ++w)
-                if (mask & (1u << w)) val += sh.rows[w][e][field];
+                if (stored & (1u << w)) val += sh.rows[w][e][field];
             if (val == 0.f) continue;
             const int slot = F::slot(field);
             if (!Neural && slot >= kRec + 10 && slot < kRec + 14) val *= 2 * kPi;   // magnitudes
