@@ -473,7 +473,7 @@ struct Fields {
     }
 };
 
-constexpr int kBackBatch = 16;
+constexpr int kBackBatch = 24;
 constexpr int kWarps = kBlock / 32;
 
 constexpr int kLaneStride = 36;   // 32 fields + 4 pad: a lane's 16-byte stores hit 4 new banks
