@@ -467,10 +467,11 @@ struct Fields {
     static constexpr int kGeo = Neural ? 17 : 14;
     static constexpr int kRow = Neural ? 57 : 18;
     static constexpr int kCount = kGeo + 1 + kRow;            // 33 classic, 75 neural
-    // packed field -> accumulator slot (record slots 0-19, row slots 20+)
-    static __device__ __forceinline__ int slot(int i) {
-        return i < kGeo ? i : (i == kGeo ? 17 : kRec + (i - kGeo - 1));
+    // packed field of record slot s / appearance-row slot q (-1: no field)
+    static __device__ __forceinline__ int record_field(int s) {
+        return s < kGeo ? s : (s == 17 ? kGeo : -1);
     }
+    static __device__ __forceinline__ int row_field(int q) { return q < kRow ? kGeo + 1 + q : -1; }
 };
 
 constexpr int kBackBatch = 24;
@@ -594,6 +595,12 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
     const float mscale_near = mscale * P.near_plane;
     const float depth_term = go[8] * 2 * mscale_near;                // d distortion / d depth
     const float background_term = final_t * (go[3] - background_dot);  // galpha's T-independent part
+    constexpr int kRecQuads = kRec / 4, kQuads = kRecQuads + kRow / 4;
+    // 16-byte vector atomics need 16-byte aligned gradient rows (records and rows are
+    // 80/240-byte rows, so aligned bases suffice)
+    const bool vector_atomics =
+        ((reinterpret_cast<uintptr_t>(P.grad_records) | reinterpret_cast<uintptr_t>(P.grad_rows)) &
+         15u) == 0u;
     // Double-buffered batches in reverse list order: batch b+1's copies are in flight
     // while batch b is replayed and flushed.  The barrier after this thread's copies of
     // batch b landed also orders batch b-1's flush (its ids, rows and masks) before batch
@@ -772,27 +779,75 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
             }
             warp_store<Neural>(vals, sh.lanes[warp], sh.rows[warp][j], &mask[j], warp, lane);
         }
-        // flush: sum the warps' rows of each record in warp order, one global atomic per
-        // (tile, record, field)
+        // flush: sum the warps' rows of each record in warp order and add them to global
+        // memory.  Classic: one 16-byte vector atomic per (tile, record, 4-slot quad) of
+        // the record and its appearance row (slots without a field add zero).  Neural: one
+        // atomic per (tile, record, field) (its 57-field rows gain nothing from quads).
         __syncthreads();
-        for (int i = rank; i < count * F::kCount; i += kBlock) {
-            const int e = i / F::kCount, field = i % F::kCount;
-            const unsigned stored = mask[e];
-            float val = 0.f;
+        if constexpr (Neural) {
+            for (int i = rank; i < count * F::kCount; i += kBlock) {
+                const int e = i / F::kCount, field = i % F::kCount;
+                const unsigned stored = mask[e];
+                float val = 0.f;
 #pragma unroll
-            for (int w = 0; w < kWarps; ++w)
-                if (stored & (1u << w)) val += sh.rows[w][e][field];
-            if (val == 0.f) continue;
-            const int slot = F::slot(field);
-            if (!Neural && slot >= kRec + 10 && slot < kRec + 14) val *= 2 * kPi;   // magnitudes
-            if (slot < kRec) {
+                for (int w = 0; w < kWarps; ++w)
+                    if (stored & (1u << w)) val += sh.rows[w][e][field];
+                if (val == 0.f) continue;
+                if (field <= F::kGeo) {
+                    const int slot = field < F::kGeo ? field : 17;
+                    const int64_t r = batch.ids[e];
+                    if (P.grad_xy && (slot == 9 || slot == 10))
+                        atomicAdd(P.grad_xy + r * 2 + (slot - 9), val);
+                    else
+                        atomicAdd(P.grad_records + r * kRec + slot, val);
+                } else {
+                    atomicAdd(P.grad_rows + batch.rows[e] * kRow + (field - F::kGeo - 1), val);
+                }
+            }
+            continue;
+        }
+        for (int i = rank; i < count * kQuads; i += kBlock) {
+            const int e = i / kQuads, quad = i % kQuads;
+            const unsigned stored = mask[e];
+            float v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int field = quad < kRecQuads ? F::record_field(4 * quad + k)
+                                                   : F::row_field(4 * (quad - kRecQuads) + k);
+                float val = 0.f;
+                if (field >= 0) {
+#pragma unroll
+                    for (int w = 0; w < kWarps; ++w)
+                        if (stored & (1u << w)) val += sh.rows[w][e][field];
+                }
+                v[k] = val;
+            }
+            if (v[0] == 0.f && v[1] == 0.f && v[2] == 0.f && v[3] == 0.f) continue;
+            float* dst;
+            if (quad < kRecQuads) {
                 const int64_t r = batch.ids[e];
-                if (P.grad_xy && (slot == 9 || slot == 10))
-                    atomicAdd(P.grad_xy + r * 2 + (slot - 9), val);
-                else
-                    atomicAdd(P.grad_records + r * kRec + slot, val);
+                dst = P.grad_records + r * kRec + 4 * quad;
+                if (P.grad_xy && quad == 2) {   // slots 9-10 (xy) go to their own array
+                    if (v[0] != 0.f) atomicAdd(dst, v[0]);
+                    if (v[1] != 0.f) atomicAdd(P.grad_xy + r * 2, v[1]);
+                    if (v[2] != 0.f) atomicAdd(P.grad_xy + r * 2 + 1, v[2]);
+                    if (v[3] != 0.f) atomicAdd(dst + 3, v[3]);
+                    continue;
+                }
             } else {
-                atomicAdd(P.grad_rows + batch.rows[e] * kRow + (slot - kRec), val);
+                const int q = 4 * (quad - kRecQuads);
+                if constexpr (!Neural) {   // magnitudes (row slots 10-13) take their 2 pi
+                    if (q == 8) { v[2] *= 2 * kPi; v[3] *= 2 * kPi; }
+                    if (q == 12) { v[0] *= 2 * kPi; v[1] *= 2 * kPi; }
+                }
+                dst = P.grad_rows + batch.rows[e] * kRow + q;
+            }
+            if (vector_atomics) {
+                atomicAdd(reinterpret_cast<float4*>(dst), make_float4(v[0], v[1], v[2], v[3]));
+            } else {
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (v[k] != 0.f) atomicAdd(dst + k, v[k]);
             }
         }
     }
