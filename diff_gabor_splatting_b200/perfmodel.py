@@ -31,8 +31,8 @@ BACKWARD_ACCEPT_FLOP = {"classic": 400, "neural": 520}
 # accepted samples (the compositors' DRAM traffic is the record batches, gradient
 # atomics and pixel buffers, all of which grow with the accepted work).
 PROFILED_TRAFFIC = {
-    "gs_composite_forward": (12.000512e6 + 53.144832e6, 130426868),
-    "gs_composite_backward": (88.055040e6 + 4.032512e6, 130426868),
+    "gs_composite_forward": (16.224256e6 + 52.915456e6, 130426868),
+    "gs_composite_backward": (88.160768e6 + 4.975616e6, 130426868),
 }
 
 
