@@ -49,7 +49,7 @@ OWN_KERNELS = {"gs_project_forward": 1, "gs_project_backward": 1, "gs_bin_count"
                "gs_composite_forward_split": 1, "gs_composite_backward_split": 1,
                "gs_sh_forward": 1, "gs_sh_backward": 1, "gs_pack_geometry": 1,
                "gs_pack_rows": 1, "gs_unpack_geometry_grads": 1, "gs_unpack_rows": 1,
-               "gs_adam_step": 1, "gs_bin_arena": 6}
+               "gs_adam_step": 1, "gs_adam_step_capturable": 2, "gs_bin_arena": 6}
 
 
 def parse():
@@ -511,11 +511,20 @@ def graph_leg(args, job, fn, calls, device, world, pixels_all):
         return {"unavailable": "graph leg needs one render call per rank and no camera split"}
     w = job.workload
     static = calls[0]
+    # with --optimizer fused the graph records the whole training step: render, loss,
+    # backward and the Adam step (FusedAdam with device step counts)
+    optimizer = None
+    if args.optimizer == "torch":
+        return {"unavailable": "the graph leg records FusedAdam(capturable=True) only"}
+    if args.optimizer == "fused":
+        from diff_gabor_splatting_b200.optim import FusedAdam
+        optimizer = FusedAdam([t for t in static.values() if t.requires_grad], lr=1e-3,
+                              capturable=True)
     # packing counts visible pairs on the host; images and gradients are the same dense
     step_graph = GraphedStep(fn, static,
                              lambda rgb, alpha, meta: loss_of(rgb, alpha, meta,
                                                               w.depth_normal_loss),
-                             **dict(w.kwargs(), packed=False))
+                             optimizer=optimizer, **dict(w.kwargs(), packed=False))
     for _ in range(3):
         step_graph.replay()
     barrier(world)
@@ -531,7 +540,8 @@ def graph_leg(args, job, fn, calls, device, world, pixels_all):
     out = {"value": pixels_all * args.steps / (gms * 1e-3) / 1e6, "unit": "Mpix/s",
            "ms_per_step": gms / args.steps, "overflow": step_graph.arena.overflowed(),
            "arena": [step_graph.arena.max_intersections, step_graph.arena.max_spans],
-           "packed": False}
+           "packed": False,
+           "optimizer": "FusedAdam(capturable=True) in the graph" if optimizer else None}
     host = {k: v.detach().cpu().pin_memory() for k, v in static.items()}
     h2d = sum(v.numel() * v.element_size() for v in host.values())
 

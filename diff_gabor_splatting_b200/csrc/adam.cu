@@ -11,6 +11,11 @@
 // gradient, m = lerp(m, g, 1 - beta1), v = v * beta2 + (1 - beta2) g g, then
 // p += -(lr / bias_correction1) * m / (sqrt(v) / sqrt(bias_correction2) + eps)), with
 // the bias corrections computed in double on the host as torch does.
+//
+// The capturable form (gs_adam_step_capturable) keeps each tensor's step count on the
+// device, as torch.optim.Adam(capturable=True) does: one small launch increments the
+// counts, and the update computes the bias corrections from them (in double), so the
+// step can be recorded in a CUDA graph and replayed with the count advancing.
 #include "common.cuh"
 
 namespace gs {
@@ -30,6 +35,9 @@ struct AdamTable {
     int tensors;
     bool vector[kAdamTensors];                // all four arrays 16-byte aligned
     float beta1_weight, beta2, beta2_weight, eps, weight_decay, step_size, bias2_sqrt;
+    // capturable form: per-tensor step counts on the device (NULL: host scalars above)
+    const float* step[kAdamTensors];
+    double lr, beta1_d, beta2_d;
 };
 
 struct AdamScalars {
@@ -47,11 +55,16 @@ __device__ __forceinline__ void adam_element(float& p, float g, float& m, float&
 }
 
 __global__ __launch_bounds__(kAdamThreads) void adam_kernel(const AdamTable T) {
-    const AdamScalars s{T.beta1_weight, T.beta2, T.beta2_weight, T.eps, T.weight_decay,
-                        T.step_size, T.bias2_sqrt};
+    AdamScalars s{T.beta1_weight, T.beta2, T.beta2_weight, T.eps, T.weight_decay,
+                  T.step_size, T.bias2_sqrt};
     const int64_t block = blockIdx.x;
     int t = 0;
     while (t + 1 < T.tensors && T.first_block[t + 1] <= block) ++t;   // <= 48 tensors
+    if (T.step[t]) {   // bias corrections of this tensor's device step count, in double
+        const double step = double(*T.step[t]);
+        s.step_size = float(-(T.lr / (1.0 - pow(T.beta1_d, step))));
+        s.bias2_sqrt = float(sqrt(1.0 - pow(T.beta2_d, step)));
+    }
     const int64_t begin = (block - T.first_block[t]) * kAdamChunk;
     const int64_t end = min(begin + kAdamChunk, T.size[t]);
     float* __restrict__ param = T.param[t];
@@ -81,32 +94,31 @@ __global__ __launch_bounds__(kAdamThreads) void adam_kernel(const AdamTable T) {
     }
 }
 
+// Advance each tensor's device step count by one (before the update reads it).
+__global__ void adam_count_kernel(AdamTable T) {
+    const int t = threadIdx.x;
+    if (t < T.tensors) *const_cast<float*>(T.step[t]) += 1.f;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-}  // namespace
-}  // namespace gs
-
-using namespace gs;
-
-extern "C" int gs_adam_step(int tensors, float* const* params, const float* const* grads,
-                            float* const* exp_avgs, float* const* exp_avg_sqs,
-                            const int64_t* sizes, double lr, double beta1, double beta2,
-                            double eps, double weight_decay, int64_t step, void* stream) {
+// Shared by both entry points: tables of up to kAdamTensors non-empty tensors, one
+// update launch each (preceded, with device step counts, by the count launch).
+int adam_launches(const char* fn, int tensors, float* const* params, const float* const* grads,
+                  float* const* exp_avgs, float* const* exp_avg_sqs, const int64_t* sizes,
+                  float* const* steps, double lr, double beta1, double beta2, double eps,
+                  double weight_decay, double bias1, double bias2, cudaStream_t s) {
     if (tensors < 0 || (tensors > 0 && (!params || !grads || !exp_avgs || !exp_avg_sqs || !sizes)))
-        return fail(GS_ERR_ARGUMENT, "gs_adam_step: invalid tensor table");
-    if (step < 1) return fail(GS_ERR_ARGUMENT, "gs_adam_step: step counts from 1");
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": invalid tensor table");
     if (!(lr >= 0.0) || !(eps >= 0.0) || !(beta1 >= 0.0 && beta1 < 1.0) ||
         !(beta2 >= 0.0 && beta2 < 1.0) || !(weight_decay >= 0.0))
-        return fail(GS_ERR_ARGUMENT, "gs_adam_step: invalid hyper-parameters");
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": invalid hyper-parameters");
     for (int t = 0; t < tensors; ++t) {
-        if (sizes[t] < 0) return fail(GS_ERR_ARGUMENT, "gs_adam_step: negative tensor size");
-        if (sizes[t] > 0 && (!params[t] || !grads[t] || !exp_avgs[t] || !exp_avg_sqs[t]))
-            return fail(GS_ERR_ARGUMENT, "gs_adam_step: NULL tensor");
+        if (sizes[t] < 0) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": negative tensor size");
+        if (sizes[t] > 0 && (!params[t] || !grads[t] || !exp_avgs[t] || !exp_avg_sqs[t] ||
+                             (steps && !steps[t])))
+            return fail(GS_ERR_ARGUMENT, std::string(fn) + ": NULL tensor");
     }
-    // bias corrections in double, as torch.optim.Adam computes them in Python
-    const double bias1 = 1.0 - std::pow(beta1, double(step));
-    const double bias2 = 1.0 - std::pow(beta2, double(step));
-    auto s = as_stream(stream);
     for (int first = 0; first < tensors; first += kAdamTensors) {
         AdamTable T{};
         T.tensors = 0;
@@ -119,6 +131,7 @@ extern "C" int gs_adam_step(int tensors, float* const* params, const float* cons
             T.exp_avg[k] = exp_avgs[t];
             T.exp_avg_sq[k] = exp_avg_sqs[t];
             T.size[k] = sizes[t];
+            T.step[k] = steps ? steps[t] : nullptr;
             T.vector[k] = aligned16(params[t]) && aligned16(grads[t]) && aligned16(exp_avgs[t]) &&
                           aligned16(exp_avg_sqs[t]);
             T.first_block[k] = blocks;
@@ -126,7 +139,7 @@ extern "C" int gs_adam_step(int tensors, float* const* params, const float* cons
         }
         if (T.tensors == 0) continue;
         T.first_block[T.tensors] = blocks;
-        if (blocks > INT_MAX) return fail(GS_ERR_LIMIT, "gs_adam_step: tensors too large");
+        if (blocks > INT_MAX) return fail(GS_ERR_LIMIT, std::string(fn) + ": tensors too large");
         T.beta1_weight = float(1.0 - beta1);
         T.beta2 = float(beta2);
         T.beta2_weight = float(1.0 - beta2);
@@ -134,8 +147,46 @@ extern "C" int gs_adam_step(int tensors, float* const* params, const float* cons
         T.weight_decay = float(weight_decay);
         T.step_size = float(-(lr / bias1));
         T.bias2_sqrt = float(std::sqrt(bias2));
+        T.lr = lr;
+        T.beta1_d = beta1;
+        T.beta2_d = beta2;
+        if (steps) {
+            adam_count_kernel<<<1, kAdamTensors, 0, s>>>(T);
+            GS_CHECK_LAUNCH("adam_count_kernel");
+        }
         adam_kernel<<<unsigned(blocks), kAdamThreads, 0, s>>>(T);
         GS_CHECK_LAUNCH("adam_kernel");
     }
     return GS_OK;
+}
+
+}  // namespace
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" int gs_adam_step(int tensors, float* const* params, const float* const* grads,
+                            float* const* exp_avgs, float* const* exp_avg_sqs,
+                            const int64_t* sizes, double lr, double beta1, double beta2,
+                            double eps, double weight_decay, int64_t step, void* stream) {
+    if (step < 1) return fail(GS_ERR_ARGUMENT, "gs_adam_step: step counts from 1");
+    // bias corrections in double, as torch.optim.Adam computes them in Python
+    const double bias1 = 1.0 - std::pow(beta1, double(step));
+    const double bias2 = 1.0 - std::pow(beta2, double(step));
+    return adam_launches("gs_adam_step", tensors, params, grads, exp_avgs, exp_avg_sqs, sizes,
+                         nullptr, lr, beta1, beta2, eps, weight_decay, bias1, bias2,
+                         as_stream(stream));
+}
+
+extern "C" int gs_adam_step_capturable(int tensors, float* const* params,
+                                       const float* const* grads, float* const* exp_avgs,
+                                       float* const* exp_avg_sqs, const int64_t* sizes,
+                                       float* const* steps, double lr, double beta1,
+                                       double beta2, double eps, double weight_decay,
+                                       void* stream) {
+    if (tensors > 0 && !steps)
+        return fail(GS_ERR_ARGUMENT, "gs_adam_step_capturable: NULL step table");
+    return adam_launches("gs_adam_step_capturable", tensors, params, grads, exp_avgs,
+                         exp_avg_sqs, sizes, steps, lr, beta1, beta2, eps, weight_decay, 1.0,
+                         1.0, as_stream(stream));
 }

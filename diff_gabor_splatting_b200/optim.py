@@ -7,6 +7,11 @@ drop-in for that optimizer (same constructor arguments without ``amsgrad``,
 state keys ``step``, ``exp_avg``, ``exp_avg_sq``; same update), whose ``step()`` is one
 launch of ``gs_adam_step`` per parameter group (48 tensors per launch) instead of
 torch's ~10 element-wise passes over every parameter, gradient and moment.
+
+``capturable=True`` mirrors ``torch.optim.Adam(capturable=True)``: each parameter's step
+count is a float32 tensor on its device, advanced and read by the kernels
+(``gs_adam_step_capturable``), so ``step()`` makes no host round trip and can be recorded
+in a CUDA graph (``graphs.GraphedStep(optimizer=...)``).
 """
 
 from __future__ import annotations
@@ -26,7 +31,7 @@ class FusedAdam(torch.optim.Optimizer):
     """
 
     def __init__(self, params, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
-                 weight_decay: float = 0.0):
+                 weight_decay: float = 0.0, capturable: bool = False):
         if not lr >= 0.0:
             raise ValueError(f"Invalid learning rate: {lr}")
         if not eps >= 0.0:
@@ -37,7 +42,20 @@ class FusedAdam(torch.optim.Optimizer):
             raise ValueError(f"Invalid beta parameter at index 1: {betas[1]}")
         if not weight_decay >= 0.0:
             raise ValueError(f"Invalid weight_decay value: {weight_decay}")
-        super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
+        super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
+                                      capturable=capturable))
+
+    def init_state(self):
+        """Create every parameter's state (zero moments, step 0) without stepping, so a
+        CUDA graph can record ``step()`` with the state tensors already allocated."""
+        for group in self.param_groups:
+            for p in group["params"]:
+                state = self.state[p]
+                if len(state) == 0:
+                    state["step"] = (torch.zeros((), dtype=torch.float32, device=p.device)
+                                     if group["capturable"] else torch.tensor(0.0))
+                    state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                    state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -46,6 +64,9 @@ class FusedAdam(torch.optim.Optimizer):
             with torch.enable_grad():
                 loss = closure()
         for group in self.param_groups:
+            if group["capturable"]:
+                self._step_capturable(group)
+                continue
             by_step = {}
             for p in group["params"]:
                 if p.grad is None:
@@ -78,3 +99,38 @@ class FusedAdam(torch.optim.Optimizer):
                              float(group["eps"]), float(group["weight_decay"]), step,
                              nat.stream_of(device))
         return loss
+
+    def _step_capturable(self, group):
+        """One ``gs_adam_step_capturable`` call per device: step counts stay on the device."""
+        by_device = {}
+        for p in group["params"]:
+            if p.grad is None:
+                continue
+            if p.grad.is_sparse:
+                raise RuntimeError("FusedAdam does not support sparse gradients")
+            if not (p.is_cuda and p.dtype == torch.float32 and p.is_contiguous()):
+                raise RuntimeError("FusedAdam needs contiguous float32 CUDA parameters")
+            if not p.grad.is_contiguous():
+                raise RuntimeError("FusedAdam(capturable=True) needs contiguous gradients")
+            state = self.state[p]
+            if len(state) == 0:
+                state["step"] = torch.zeros((), dtype=torch.float32, device=p.device)
+                state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            if not (state["step"].is_cuda and state["step"].device == p.device):
+                raise RuntimeError("FusedAdam(capturable=True) needs step counts on the "
+                                   "parameters' device")
+            by_device.setdefault(p.device, []).append((p, state))
+        beta1, beta2 = group["betas"]
+        for device, items in by_device.items():
+            arrays = [nat.host_array(ctypes.c_void_p, ptrs) for ptrs in (
+                [p.data_ptr() for p, _ in items], [p.grad.data_ptr() for p, _ in items],
+                [s["exp_avg"].data_ptr() for _, s in items],
+                [s["exp_avg_sq"].data_ptr() for _, s in items],
+                [s["step"].data_ptr() for _, s in items])]
+            sizes = nat.host_array(ctypes.c_int64, [p.numel() for p, _ in items])
+            with torch.cuda.device(device):
+                nat.call("gs_adam_step_capturable", len(items), arrays[0][1], arrays[1][1],
+                         arrays[2][1], arrays[3][1], sizes[1], arrays[4][1], float(group["lr"]),
+                         float(beta1), float(beta2), float(group["eps"]),
+                         float(group["weight_decay"]), nat.stream_of(device))

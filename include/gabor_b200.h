@@ -292,6 +292,19 @@ int gs_adam_step(int tensors, float* const* params, const float* const* grads,
                  double lr, double beta1, double beta2, double eps, double weight_decay,
                  int64_t step, void* stream);
 
+/* Capturable form of gs_adam_step, the counterpart of torch.optim.Adam(capturable=True)
+ * (torch/optim/adam.py, _multi_tensor_adam with device step tensors): `steps` is a host
+ * array of device pointers, one float32 step count per tensor (its own, not shared),
+ * which this call increments by one on the device before the update computes its bias
+ * corrections from it (in double).  Nothing is read back to the host, so the call can
+ * be recorded in a CUDA graph and replayed.  No counterpart in the reference's native
+ * module.
+ */
+int gs_adam_step_capturable(int tensors, float* const* params, const float* const* grads,
+                            float* const* exp_avgs, float* const* exp_avg_sqs,
+                            const int64_t* sizes, float* const* steps, double lr, double beta1,
+                            double beta2, double eps, double weight_decay, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Layout converters for the reference-layout entry points (the `_C` mirror).
  * gs_pack_geometry: geometry[Q][17] + opacities[primitive_ids[q]] -> records[Q][20].

@@ -109,3 +109,44 @@ def test_graph_overflow_is_reported():
     assert needed[0] > 16
     with pytest.raises(ValueError, match="packed=False"):
         GraphedStep(rasterize_gabors, static, _loss, width=W, height=H, packed=True)
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_graphed_training_step_matches_eager_training(method):
+    """Render + loss + backward + FusedAdam(capturable) captured as one graph: three
+    replays leave the parameters where three eager training steps do, and building the
+    graph leaves the parameters and optimizer state untouched."""
+    from diff_gabor_splatting_b200.optim import FusedAdam
+
+    v = random_scene(method, scenes=1, cameras=2, n=300, width=W, height=H, conditioned=True)
+    fn = rasterize_gabors if method == "classic" else rasterize_neural_gabors
+    static = {k: t.clone().requires_grad_() for k, t in ordered(v, method).items()}
+    eager = {k: t.detach().clone().requires_grad_() for k, t in static.items()}
+    trained = [k for k in static if k not in ("view_matrices", "intrinsics", "backgrounds")]
+    opt = FusedAdam([static[k] for k in trained], lr=1e-3, capturable=True)
+    ref = FusedAdam([eager[k] for k in trained], lr=1e-3)
+    step = GraphedStep(fn, static, _loss, optimizer=opt, width=W, height=H)
+    for k in static:   # the warm-up steps were undone
+        torch.testing.assert_close(static[k].detach(), eager[k].detach(), rtol=0, atol=0)
+    assert int(opt.state[static[trained[0]]]["step"]) == 0
+    losses = []
+    for _ in range(3):
+        losses.append(step.replay().clone())
+        for t in eager.values():
+            t.grad = None
+        # trained quaternions and wave weights leave the reference's validation ranges
+        rgb, alpha, meta = fn(**eager, width=W, height=H, validate=False)
+        loss = _loss(rgb, alpha, meta)
+        loss.backward()
+        ref.step()
+        torch.testing.assert_close(losses[-1], loss.detach(), rtol=1e-5, atol=1e-7)
+    torch.cuda.synchronize()
+    assert not step.arena.overflowed()
+    assert int(opt.state[static[trained[0]]]["step"]) == 3
+    for k in trained:
+        scale = float(eager[k].detach().abs().max()) + 1e-12
+        err = float((static[k].detach() - eager[k].detach()).abs().max()) / scale
+        assert err < 1e-5, f"{k}: {err:.2e} of its scale after three training steps"
+    with pytest.raises(ValueError, match="capturable"):
+        GraphedStep(fn, static, _loss, optimizer=FusedAdam([static["means"]]), width=W,
+                    height=H)

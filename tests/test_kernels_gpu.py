@@ -403,3 +403,46 @@ def test_output_gradient_layouts_give_the_same_gradients(method):
     # a loss on depth and normals only: rgb, alpha and distortion gradients are absent
     only = grads(lambda rgb, alpha, meta: meta["accumulated_depth"].mean() + meta["normals"].sum())
     assert any(g.abs().max() > 0 for g in only.values())
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_backward_flush_with_unaligned_gradient_buffers(method):
+    """The backward adds classic gradients with 16-byte vector atomics when the gradient
+    buffers are 16-byte aligned and falls back to per-slot atomics otherwise: both give
+    the same gradients (to atomic-order rounding)."""
+    from diff_gabor_splatting_b200 import _native as nat
+
+    v = random_scene(method, scenes=1, cameras=2, n=300, width=W, height=H, conditioned=True)
+    cpu = {k: t.cpu() for k, t in v.items()}
+    T, xy, normals, dirs, radii = O.project_surfaces(
+        cpu["means"], cpu["quaternions"], cpu["scales"], cpu["view_matrices"],
+        cpu["intrinsics"], W, H, 0.2, 100.0)
+    rec = O.pack(T, xy, normals, dirs, radii, cpu["opacities"],
+                 [cpu[k] for k in appearance_names(method)], method == "neural", None, True)
+    args = [rec[k].cuda().contiguous() for k in ("geometry", "parameters", "opacities",
+                                                   "primitive_ids", "image_ids", "radii")]
+    bg = v["backgrounds"].reshape(-1, 3).contiguous()
+    neural = method == "neural"
+    maps, point_list, ranges, state, contrib = native_c.rasterize_forward(
+        *args, bg, W, H, neural, 0.2, 100.0)
+    records, rows = native_c._pack(args[0], args[1], args[2], args[3], neural)
+    grad_maps = torch.randn(maps.shape, generator=torch.Generator().manual_seed(5)).cuda()
+
+    def backward(offset):
+        buf_r = torch.zeros(records.numel() + 4, device="cuda")
+        buf_a = torch.zeros(rows.numel() + 4, device="cuda")
+        g_records = buf_r[offset:offset + records.numel()].view_as(records)
+        g_rows = buf_a[offset:offset + rows.numel()].view_as(rows)
+        g_bg = torch.zeros_like(bg)
+        nat.call("gs_composite_backward", nat.ptr(records), nat.ptr(rows), nat.ROWS_EXPLICIT,
+                 nat.ptr(args[3]), 1, 1, records.shape[0], rows.shape[0], nat.ptr(bg),
+                 nat.ptr(point_list), nat.ptr(ranges), nat.ptr(state), nat.ptr(contrib),
+                 nat.ptr(grad_maps), bg.shape[0], W, H, int(neural), 0.2, 100.0,
+                 nat.ptr(g_records), None, nat.ptr(g_rows), nat.ptr(g_bg), None,
+                 nat.stream_of(records.device))
+        return g_records.clone(), g_rows.clone(), g_bg
+    aligned, unaligned = backward(0), backward(1)
+    assert nat.ptr(torch.zeros(4, device="cuda")[1:]) % 16 != 0
+    for name, a, u in zip(("records", "rows", "backgrounds"), aligned, unaligned):
+        assert bool(a.abs().sum() > 0), name
+        torch.testing.assert_close(u, a, rtol=1e-5, atol=1e-6 * float(a.abs().max()), msg=name)

@@ -123,3 +123,63 @@ def test_fit_texture_loop_matches_torch_adam(method):
     assert ours[-1] < ours[0]
     for a, b in zip(ours, theirs):
         assert abs(a - b) <= 1e-5 * max(abs(b), 1e-6) + 1e-9, (a, b)
+
+
+@pytest.mark.parametrize("kw", [dict(lr=0.01), dict(lr=3e-3, betas=(0.8, 0.99), eps=1e-6,
+                                                    weight_decay=0.01)])
+def test_capturable_matches_torch_adam(kw):
+    """Device step counts (gs_adam_step_capturable) give torch.optim.Adam's update, with
+    the counts advanced on the device (a parameter without a gradient keeps its count)."""
+    shapes = [(1,), (5, 7), (4097,), (300_001,)]
+    ours, theirs, fused, reference, g = _pair(shapes, 1, **kw)
+    fused = FusedAdam(ours, capturable=True, **kw)
+    for step in range(6):
+        for a, b in zip(ours, theirs):
+            grad = torch.randn(a.shape, device="cuda", generator=g) * (10.0 ** (step - 3))
+            a.grad, b.grad = grad.clone(), grad.clone()
+        if step == 2:
+            ours[1].grad = theirs[1].grad = None
+        fused.step()
+        reference.step()
+    for a, b in zip(ours, theirs):
+        torch.testing.assert_close(a, b, rtol=2e-6, atol=1e-7)
+        sa, sb = fused.state[a], reference.state[b]
+        assert sa["step"].is_cuda and int(sa["step"]) == int(sb["step"])
+        torch.testing.assert_close(sa["exp_avg"], sb["exp_avg"], rtol=1e-6, atol=1e-9)
+
+
+def test_capturable_step_replays_in_a_cuda_graph():
+    """The capturable step recorded once in a CUDA graph and replayed on gradients written
+    in place equals eager steps (the step count advancing on every replay)."""
+    g = torch.Generator(device="cuda").manual_seed(2)
+    base = [torch.randn(s, device="cuda", generator=g) for s in [(33,), (1000, 3)]]
+    graphed = [t.clone() for t in base]
+    eager = [t.clone() for t in base]
+    grads = [torch.zeros_like(t) for t in base]
+    for p, gr in zip(graphed, grads):
+        p.grad = gr
+    opt = FusedAdam(graphed, lr=0.05, capturable=True)
+    opt.init_state()
+    ref = FusedAdam(eager, lr=0.05)
+    warm = torch.zeros(8, device="cuda")   # load the kernels before capturing
+    warm.grad = torch.ones_like(warm)
+    FusedAdam([warm], capturable=True).step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side), torch.cuda.graph(graph):
+        opt.step()
+    torch.cuda.current_stream().wait_stream(side)
+    for _ in range(5):
+        step_grads = [torch.randn(t.shape, device="cuda", generator=g) for t in base]
+        for gr, new in zip(grads, step_grads):
+            gr.copy_(new)
+        for p, new in zip(eager, step_grads):
+            p.grad = new.clone()
+        graph.replay()
+        ref.step()
+    torch.cuda.synchronize()
+    for a, b in zip(graphed, eager):
+        torch.testing.assert_close(a, b, rtol=2e-6, atol=1e-7)
+    assert int(opt.state[graphed[0]]["step"]) == 5
