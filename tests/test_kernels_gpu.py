@@ -7,6 +7,8 @@ lists and tile ranges bit-exact given the same records), forward compositing
 forward + backward against the oracle's float64 autograd.
 """
 
+import math
+
 import numpy as np
 import pytest
 import torch
@@ -446,3 +448,46 @@ def test_backward_flush_with_unaligned_gradient_buffers(method):
     for name, a, u in zip(("records", "rows", "backgrounds"), aligned, unaligned):
         assert bool(a.abs().sum() > 0), name
         torch.testing.assert_close(u, a, rtol=1e-5, atol=1e-6 * float(a.abs().max()), msg=name)
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_tight_bins_render_identically_on_adversarial_surfels(method, monkeypatch):
+    """Tight binning's rows are evaluated in single precision with a derived error margin:
+    on surfels chosen to stress it -- needle-thin (1000:1), within half a degree of
+    edge-on, large enough to cover much of the image, just past the near plane, and
+    with opacities just above 1/255 -- every map is bit-identical to the square bins'."""
+    g = torch.Generator().manual_seed(11)
+    Wa, Ha = 256, 192
+    v = random_scene(method, scenes=1, cameras=2, n=2000, width=Wa, height=Ha, focal=220.0,
+                     seed=11, device="cpu")
+    n = v["means"].shape[1]
+    kind = torch.randint(0, 6, (n,), generator=g)
+    scales, quats, means, opac = v["scales"][0], v["quaternions"][0], v["means"][0], v["opacities"][0]
+    thin = kind == 1
+    scales[thin, 1] = scales[thin, 0] * 1e-3
+    edge = kind == 2
+    angle = math.pi / 2 + (torch.rand(int(edge.sum()), generator=g) - 0.5) * (math.pi / 180)
+    quats[edge] = torch.stack([torch.cos(angle / 2), torch.sin(angle / 2),
+                               torch.zeros_like(angle), torch.zeros_like(angle)], -1)
+    huge = kind == 3
+    scales[huge] = torch.rand(int(huge.sum()), 2, generator=g) * 1.5 + 0.5
+    near = kind == 4
+    means[near, 2] = 0.2 + torch.rand(int(near.sum()), generator=g) * 0.1
+    faint = kind == 5
+    opac[faint] = 1 / 255 + torch.rand(int(faint.sum()), generator=g) * 0.01
+    fn = rasterize_gabors if method == "classic" else rasterize_neural_gabors
+    results = {}
+    for tight in (False, True):
+        monkeypatch.setattr(rendering, "TIGHT_BINNING", tight)
+        values = {k: t.cuda() for k, t in ordered(v, method).items()}
+        rendering.WORK = {}
+        try:
+            with torch.no_grad():
+                out = fn(**values, width=Wa, height=Ha)
+            torch.cuda.synchronize()
+            work = rendering.WORK
+        finally:
+            rendering.WORK = None
+        results[tight] = (maps_from_result(out), work["intersections"])
+    assert results[True][1] < results[False][1]
+    assert torch.equal(results[True][0], results[False][0])
