@@ -464,14 +464,26 @@ __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Para
 // [dir 14-16 neural]), opacity (record slot 17), then the appearance row.
 template <bool Neural>
 struct Fields {
-    static constexpr int kGeo = Neural ? 17 : 14;
-    static constexpr int kRow = Neural ? 57 : 18;
-    static constexpr int kCount = kGeo + 1 + kRow;            // 33 classic, 75 neural
-    // packed field of record slot s / appearance-row slot q (-1: no field)
+    // Packed per-record gradient fields summed over a warp's pixels: record slots 0-13
+    // (T, xy, normal), the opacity, then the appearance row.  Classic: the 18-float row.
+    // Neural: 39 of the 57 row floats -- per hidden unit the weights of the (u, v) inputs,
+    // then b1, W2, b2.  The weights of the three direction inputs and the direction
+    // gradient (record slots 14-16) are per-record constants (the direction, the input
+    // weights) times the b1 sums, so the flush forms them (21 values per record).
+    static constexpr int kGeo = 14;
+    static constexpr int kRow = Neural ? 39 : 18;
+    static constexpr int kCount = kGeo + 1 + kRow;            // 33 classic, 54 neural
+    static constexpr int kB1 = kGeo + 1 + 12;                  // neural: field of b1[0]
+    // classic: packed field of record slot s / appearance-row slot q (-1: no field)
     static __device__ __forceinline__ int record_field(int s) {
         return s < kGeo ? s : (s == 17 ? kGeo : -1);
     }
     static __device__ __forceinline__ int row_field(int q) { return q < kRow ? kGeo + 1 + q : -1; }
+    // neural: row slot of packed row field p (W1 (u, v) columns, b1, W2, b2)
+    static __device__ __forceinline__ int neural_row_slot(int p) {
+        return p < 12 ? (p >> 1) * 5 + (p & 1) : p < 18 ? 30 + (p - 12) : p < 36 ? 36 + (p - 18)
+                                                                          : 54 + (p - 36);
+    }
 };
 
 constexpr int kBackBatch = 24;
@@ -482,7 +494,7 @@ constexpr int kLaneStride = 36;   // 32 fields + 4 pad: a lane's 16-byte stores 
 template <bool Neural>
 struct BackShared {
     using F = Fields<Neural>;
-    static constexpr int kStride = (F::kCount + 3) / 4 * 4;   // 36 classic, 76 neural
+    static constexpr int kStride = (F::kCount + 3) / 4 * 4;   // 36 classic, 56 neural
     Batch<Neural, kBackBatch> batch[2];        // double-buffered: batch b+1 lands during b
     float4 weights01[2][Neural ? 1 : kBackBatch];
     float rows[kWarps][kBackBatch][kStride];   // per (warp, record) field sums
@@ -688,32 +700,33 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                 suffix += w * gw;
                 // appearance backward: rasterize.cu:146-197
                 if constexpr (Neural) {
-                    const float input[5] = {v.s[0] * kThird, v.s[1] * kThird, g[14], g[15], g[16]};
-                    float gh[6] = {}, gi[5] = {};
+                    // packed row fields: W1 (u, v) columns 0-11, b1 12-17, W2 18-35, b2 36-38;
+                    // the direction columns and the direction gradient come from the b1
+                    // sums at the flush
+                    const float input[2] = {v.s[0] * kThird, v.s[1] * kThird};
+                    float gh[6] = {}, gi[2] = {};
 #pragma unroll
                     for (int c = 0; c < 3; ++c) {
                         const float gz = gc[c] * color[c] * (1 - color[c]);
-                        ga[54 + c] += gz;
+                        ga[36 + c] += gz;
 #pragma unroll
                         for (int h = 0; h < 6; ++h) {
-                            ga[36 + c * 6 + h] += gz * hidden[h];
+                            ga[18 + c * 6 + h] += gz * hidden[h];
                             gh[h] += gz * a[36 + c * 6 + h];
                         }
                     }
 #pragma unroll
                     for (int h = 0; h < 6; ++h) {
                         const float gz = gh[h] * 30 * coss[h];
-                        ga[30 + h] += gz;
+                        ga[12 + h] += gz;
 #pragma unroll
-                        for (int k = 0; k < 5; ++k) {
-                            ga[h * 5 + k] += gz * input[k];
+                        for (int k = 0; k < 2; ++k) {
+                            ga[2 * h + k] += gz * input[k];
                             gi[k] += gz * a[h * 5 + k];
                         }
                     }
                     gs[0] += gi[0] * kThird;
                     gs[1] += gi[1] * kThird;
-#pragma unroll
-                    for (int k = 0; k < 3; ++k) gg[14 + k] += gi[k + 2];
                 } else {
                     // The reference's per-wave loop (rasterize.cu:173-195) factored: summed
                     // over waves, d colour / d c1 = h1 and d colour / d c2 = h2; every
@@ -785,23 +798,47 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
         // atomic per (tile, record, field) (its 57-field rows gain nothing from quads).
         __syncthreads();
         if constexpr (Neural) {
-            for (int i = rank; i < count * F::kCount; i += kBlock) {
-                const int e = i / F::kCount, field = i % F::kCount;
+            constexpr int kItems = F::kCount + 21;   // fields, then the formed values
+            for (int i = rank; i < count * kItems; i += kBlock) {
+                const int e = i / kItems, item = i % kItems;
                 const unsigned stored = mask[e];
-                float val = 0.f;
+                auto field_sum = [&](int field) {
+                    float sum = 0.f;
 #pragma unroll
-                for (int w = 0; w < kWarps; ++w)
-                    if (stored & (1u << w)) val += sh.rows[w][e][field];
-                if (val == 0.f) continue;
-                if (field <= F::kGeo) {
-                    const int slot = field < F::kGeo ? field : 17;
-                    const int64_t r = batch.ids[e];
-                    if (P.grad_xy && (slot == 9 || slot == 10))
-                        atomicAdd(P.grad_xy + r * 2 + (slot - 9), val);
-                    else
-                        atomicAdd(P.grad_records + r * kRec + slot, val);
-                } else {
-                    atomicAdd(P.grad_rows + batch.rows[e] * kRow + (field - F::kGeo - 1), val);
+                    for (int w = 0; w < kWarps; ++w)
+                        if (stored & (1u << w)) sum += sh.rows[w][e][field];
+                    return sum;
+                };
+                const int64_t r = batch.ids[e];
+                float* grad_row = P.grad_rows + batch.rows[e] * kRow;
+                if (item < F::kCount) {
+                    const float val = field_sum(item);
+                    if (val == 0.f) continue;
+                    if (item < F::kGeo) {
+                        if (P.grad_xy && (item == 9 || item == 10))
+                            atomicAdd(P.grad_xy + r * 2 + (item - 9), val);
+                        else
+                            atomicAdd(P.grad_records + r * kRec + item, val);
+                    } else if (item == F::kGeo) {
+                        atomicAdd(P.grad_records + r * kRec + 17, val);   // opacity
+                    } else {
+                        atomicAdd(grad_row + F::neural_row_slot(item - F::kGeo - 1), val);
+                    }
+                    continue;
+                }
+                const int d = item - F::kCount;
+                const float* geo = reinterpret_cast<const float*>(batch.geo[e]);
+                if (d < 18) {   // W1[h][2 + k] = dir_k * sum of b1[h]
+                    const int h = d / 3, k = d % 3;
+                    const float val = geo[14 + k] * field_sum(F::kB1 + h);
+                    if (val != 0.f) atomicAdd(grad_row + h * 5 + 2 + k, val);
+                } else {        // direction_k = sum_h W1[h][2 + k] * sum of b1[h]
+                    const int k = d - 18;
+                    const float* app = reinterpret_cast<const float*>(batch.app[e]);
+                    float val = 0.f;
+#pragma unroll
+                    for (int h = 0; h < 6; ++h) val = fmaf(app[h * 5 + 2 + k], field_sum(F::kB1 + h), val);
+                    if (val != 0.f) atomicAdd(P.grad_records + r * kRec + 14 + k, val);
                 }
             }
             continue;
