@@ -9,16 +9,19 @@
 // Per-pixel arithmetic follows the reference expression by expression (same
 // operation order, full-precision expf/sinf/cosf), so images agree to rounding.
 //
-// Differences, all in data movement:
-//   * records and appearance rows are 80/240-byte aligned rows staged with
-//     16-byte vector loads (the reference gathers scalars through two levels of
-//     indirection, :219-226);
+// Differences, all in data movement and in where sums are formed:
+//   * records and appearance rows are 80/240-byte aligned rows staged with 16-byte
+//     cp.async copies, double-buffered (the next batch lands while the current one is
+//     composited; the reference gathers scalars through two levels of indirection,
+//     :219-226, between two barriers per batch);
 //   * opacity travels inside the record, so no per-primitive opacity gather;
-//   * backward gradients of one record are reduced across the warp with a
-//     reduce-scatter (each lane ends up owning one field: ~36 shuffles for 33
-//     fields instead of 5 per field), summed across the CTA's 8 warps in shared
-//     memory, and added to global memory once per (tile, record) -- 8x fewer
-//     global atomics than one per warp.
+//   * backward gradients of one record are summed across the warp with a
+//     shared-memory transpose (every lane stores its fields as a row, every lane sums
+//     a column), across the CTA's 8 warps at the flush, and added to global memory
+//     once per (tile, record): 8x fewer global atomics than one per warp, and for
+//     classic rows one 16-byte vector atomic per four fields;
+//   * neural: the gradients of the direction inputs' weights and of the direction
+//     are per-record constants times the b1 sums, formed once per (tile, record).
 #include <mutex>
 #include <set>
 #include <utility>
