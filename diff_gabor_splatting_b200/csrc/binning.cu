@@ -11,13 +11,15 @@
 //   2. per record, in that order, its tiles as row spans (one span per tile row it
 //      reaches) and their counts; inclusive scans of slots and spans; one host read
 //      of the totals (the reference's one synchronisation, rasterize.cu:466-468);
-//   3. the spans written out with their first slot and first tile;
-//   4. expansion of every (record, tile) slot in depth order, writing a 32-bit tile
-//      id and the record index (8 bytes per slot, coalesced);
-//   5. stable radix sort of the slots by tile id over only ceil(log2(tiles)) bits
-//      (2 passes for up to 65536 tiles), which keeps the depth order inside each
-//      tile;
-//   6. tile ranges from the sorted tile ids.
+//   3. images up to kRowMaxColumns tiles wide (the row path): the spans written out as
+//      (tile row, packed span) pairs, stably sorted by tile row, and the tile lists
+//      assembled per chunk of a row's spans (counts per column, a scan over the row's
+//      chunks, ranked writes staged in shared memory) -- no per-slot sort at all;
+//   4. wider images and arena mode (the slot path): the spans written with their
+//      first slot and first tile, every (record, tile) slot expanded in depth order
+//      (32-bit tile id + record), stably sorted by tile id over only
+//      ceil(log2(tiles)) bits, which keeps the depth order inside each tile, and tile
+//      ranges from the sorted ids.
 // With the reference's rectangles (flags 0) point_list and ranges are identical to
 // the reference's.  GS_BIN_TIGHT keeps, per tile row, only the tiles a sample with
 // alpha >= 1/255 can reach (see record_region): same images, shorter lists.
