@@ -14,7 +14,7 @@
 //   3. images up to kRowMaxColumns tiles wide (the row path): the spans written out as
 //      (tile row, packed span) pairs, stably sorted by tile row, and the tile lists
 //      assembled per chunk of a row's spans (counts per column, a scan over the row's
-//      chunks, ranked writes staged in shared memory) -- no per-slot sort at all;
+//      chunks, ranked writes straight to the point list) -- no per-slot sort at all;
 //   4. wider images and arena mode (the slot path): the spans written with their
 //      first slot and first tile, every (record, tile) slot expanded in depth order
 //      (32-bit tile id + record), stably sorted by tile id over only
@@ -545,9 +545,7 @@ unsigned blocks_for(int64_t n) { return unsigned((n + kBinThreads - 1) / kBinThr
 // stable tile sort's lists exactly: within a tile, records in depth order.
 // ------------------------------------------------------------------------------
 constexpr int kRowChunk = 64;         // spans per chunk (one warp)
-constexpr int kRowStage = 1024;       // slots of a chunk staged in shared memory
-constexpr int kRowStageColumns = 256; // widest rows whose chunks are staged (8-bit columns)
-constexpr int kRowWarps = 8;          // warps (chunks) per block
+constexpr int kRowWarps = 4;          // warps (chunks) per block
 constexpr int kRowMaxColumns = 1024;  // tile columns this path handles (wider: slot sort)
 
 inline bool rows_path(int tw) { return tw <= kRowMaxColumns; }
@@ -691,10 +689,10 @@ __global__ void tile_ranges_kernel(int64_t n_tiles, const int* __restrict__ tile
 // Per chunk: write each span's record into every tile it covers.  Lanes take 32 spans
 // at a time in list (depth) order; a tile's rank among them is the number of lower
 // lanes covering it (a per-column lane mask built with shared atomics), so the order
-// within a tile follows the list whatever the lanes' timing.  Chunks of rows up to
-// kRowStageColumns tiles wide with at most kRowStage slots are assembled in shared
-// memory column by column and copied out in runs (each column's slots of a chunk are
-// adjacent in the point list); others write every slot directly.
+// within a tile follows the list whatever the lanes' timing.  Each slot is written
+// straight to the point list (a column's slots of one chunk are adjacent there); with
+// only two tile-wide arrays of shared memory per warp the kernel keeps most of an SM's
+// warps resident, which hides the latency of its scattered writes.
 __device__ __forceinline__ void rank_group(int x0, int x1, unsigned* lanes, int lane) {
     for (int x = x0; x < x1; ++x) atomicOr(lanes + x, 1u << lane);
     __syncwarp();
@@ -713,71 +711,18 @@ __device__ __forceinline__ void advance_group(int x0, int x1, unsigned* lanes, i
 __global__ __launch_bounds__(kRowWarps * 32) void row_write_kernel(
     int64_t rows, int tw, const int* __restrict__ chunk_base, const int* __restrict__ chunk_row,
     const int* __restrict__ row_first, const int* __restrict__ row_end,
-    const uint64_t* __restrict__ spans_by_row, const int* __restrict__ chunk_counts,
-    const int* __restrict__ chunk_prefix,
+    const uint64_t* __restrict__ spans_by_row, const int* __restrict__ chunk_prefix,
     const int* __restrict__ tile_start, int* __restrict__ point_list) {
     extern __shared__ int row_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const bool staged_rows = tw <= kRowStageColumns;
-    int* base = row_smem + warp * (staged_rows ? 3 * tw + kRowStage + kRowStage / 4 : 2 * tw);
-    unsigned* lanes = reinterpret_cast<unsigned*>(base + tw);
+    int* cursor = row_smem + warp * 2 * tw;   // next point-list position of each column
+    unsigned* lanes = reinterpret_cast<unsigned*>(cursor + tw);
     RowChunk c;
     const int64_t chunk = int64_t(blockIdx.x) * kRowWarps + warp;
     if (!row_chunk(chunk, rows, chunk_base, chunk_row, row_first, row_end, c)) return;
     const unsigned below = (1u << lane) - 1u;
-    // slots of this chunk: its per-column counts summed
-    int total = 0;
-    for (int x = lane; x < tw; x += 32) total += chunk_counts[chunk * tw + x];
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-    if (staged_rows && total <= kRowStage) {
-        int* cursor = base + 2 * tw;                  // local offset of each column's run
-        int* staged = base + 3 * tw;                  // records, column by column
-        auto* column = reinterpret_cast<uint8_t*>(staged + kRowStage);   // their columns
-        // exclusive scan of the chunk's column counts (columns in blocks of `per` a lane)
-        const int per = (tw + 31) / 32;
-        int run = 0;
-        for (int i = 0; i < per; ++i) {
-            const int x = lane * per + i;
-            if (x < tw) run += chunk_counts[chunk * tw + x];
-        }
-        int prefix = run;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, prefix, o);
-            if (lane >= o) prefix += v;
-        }
-        prefix -= run;
-        for (int i = 0; i < per; ++i) {
-            const int x = lane * per + i;
-            if (x < tw) {
-                cursor[x] = prefix;
-                // global position of local slot l of column x: base[x] + l
-                base[x] = tile_start[int64_t(c.row) * tw + x] + chunk_prefix[chunk * tw + x] -
-                          prefix;
-                lanes[x] = 0u;
-                prefix += chunk_counts[chunk * tw + x];
-            }
-        }
-        __syncwarp();
-        for (int g0 = c.begin; g0 < c.end; g0 += 32) {
-            const int g = g0 + lane;
-            int x0 = 0, x1 = 0, record = 0;
-            if (g < c.end) unpack_span(spans_by_row[g], x0, x1, record);
-            rank_group(x0, x1, lanes, lane);
-            for (int x = x0; x < x1; ++x) {
-                const int local = cursor[x] + __popc(lanes[x] & below);
-                staged[local] = record;
-                column[local] = uint8_t(x);
-            }
-            advance_group(x0, x1, lanes, cursor, below);
-        }
-        __syncwarp();
-        for (int e = lane; e < total; e += 32) point_list[base[column[e]] + e] = staged[e];
-        return;
-    }
     for (int x = lane; x < tw; x += 32) {
-        base[x] = tile_start[int64_t(c.row) * tw + x] + chunk_prefix[chunk * tw + x];
+        cursor[x] = tile_start[int64_t(c.row) * tw + x] + chunk_prefix[chunk * tw + x];
         lanes[x] = 0u;
     }
     __syncwarp();
@@ -786,8 +731,8 @@ __global__ __launch_bounds__(kRowWarps * 32) void row_write_kernel(
         int x0 = 0, x1 = 0, record = 0;
         if (g < c.end) unpack_span(spans_by_row[g], x0, x1, record);
         rank_group(x0, x1, lanes, lane);
-        for (int x = x0; x < x1; ++x) point_list[base[x] + __popc(lanes[x] & below)] = record;
-        advance_group(x0, x1, lanes, base, below);
+        for (int x = x0; x < x1; ++x) point_list[cursor[x] + __popc(lanes[x] & below)] = record;
+        advance_group(x0, x1, lanes, cursor, below);
     }
 }
 
@@ -965,15 +910,10 @@ int sort_phase_rows(const float* records, int record_stride, const int32_t* radi
     tile_ranges_kernel<<<blocks_for(n_tiles), kBinThreads, 0, s>>>(
         n_tiles, tile_count, tile_start, reinterpret_cast<int2*>(ranges));
     GS_CHECK_LAUNCH("tile_ranges_kernel");
-    const size_t write_smem =
-        sizeof(int) * kRowWarps *
-        (tw <= kRowStageColumns ? 3 * tw + kRowStage + kRowStage / 4 : 2 * tw);
-    if (write_smem > 48 * 1024)
-        GS_CUDA(cudaFuncSetAttribute(row_write_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     int(write_smem)));
+    const size_t write_smem = sizeof(int) * kRowWarps * 2 * tw;   // <= 32 KB (tw <= 1024)
     row_write_kernel<<<chunk_blocks, kRowWarps * 32, write_smem, s>>>(
-        L.rows, tw, chunk_base, chunk_row, row_first, row_end, idx_out, chunk_counts,
-        chunk_prefix, tile_start, point_list);
+        L.rows, tw, chunk_base, chunk_row, row_first, row_end, idx_out, chunk_prefix, tile_start,
+        point_list);
     GS_CHECK_LAUNCH("row_write_kernel");
     (void)I;
     return GS_OK;
