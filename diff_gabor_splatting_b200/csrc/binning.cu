@@ -671,7 +671,20 @@ __global__ void row_scan_kernel(int64_t rows, int tw, const int* __restrict__ ch
     if (t >= rows * tw) return;
     const int64_t row = t / tw, x = t % tw;
     int sum = 0;
-    for (int64_t c = chunk_base[row]; c < chunk_base[row + 1]; ++c) {
+    const int64_t end = chunk_base[row + 1];
+    int64_t c = chunk_base[row];
+    // eight chunks' counts loaded at once, so the walk waits on memory once per eight
+    for (; c + 8 <= end; c += 8) {
+        int n[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) n[k] = chunk_counts[(c + k) * tw + x];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            chunk_prefix[(c + k) * tw + x] = sum;
+            sum += n[k];
+        }
+    }
+    for (; c < end; ++c) {
         chunk_prefix[c * tw + x] = sum;
         sum += chunk_counts[c * tw + x];
     }
