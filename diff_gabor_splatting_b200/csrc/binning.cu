@@ -294,7 +294,7 @@ __device__ __forceinline__ int owner_lane(const int* first, int t) {
     return lo;
 }
 
-__global__ __launch_bounds__(kBinThreads, 2) void tile_counts_balanced_kernel(
+__global__ __launch_bounds__(kBinThreads, 4) void tile_counts_balanced_kernel(
     int64_t R, const float* __restrict__ records, int stride, const int* __restrict__ radii,
     const int* __restrict__ order, int tw, int th, bool tight, int64_t* __restrict__ slots,
     int64_t* __restrict__ spans) {
@@ -354,7 +354,7 @@ __global__ __launch_bounds__(kBinThreads, 2) void tile_counts_balanced_kernel(
 // Row-path spans (as spans_kernel<true>), balanced: a row's output index is its record's
 // first span plus the non-empty rows before it, counted across passes per record and
 // within a pass with a ballot over the lanes holding rows of the same record.
-__global__ __launch_bounds__(kBinThreads, 2) void spans_rows_balanced_kernel(
+__global__ __launch_bounds__(kBinThreads, 4) void spans_rows_balanced_kernel(
     int64_t R, const float* __restrict__ records, int stride, const int* __restrict__ radii,
     const int* __restrict__ order, const int64_t* __restrict__ span_end,
     const int64_t* __restrict__ image_ids, int64_t per_image, int tw, int th, bool tight,
