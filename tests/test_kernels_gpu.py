@@ -491,3 +491,41 @@ def test_tight_bins_render_identically_on_adversarial_surfels(method, monkeypatc
         results[tight] = (maps_from_result(out), work["intersections"])
     assert results[True][1] < results[False][1]
     assert torch.equal(results[True][0], results[False][0])
+
+
+@pytest.mark.parametrize("width", [16384, 16400])
+def test_binning_of_very_wide_images(width):
+    """Images of up to 1024 tile columns take the row-span list builder, wider ones the
+    slot expansion and tile sort: both give the reference's square lists bit-exactly,
+    and tight lists that are ordered subsets of them, at the boundary (1024 columns)
+    and just past it (1025)."""
+    from diff_gabor_splatting_b200 import _native as nat
+
+    height = 40
+    v = random_scene(scenes=1, cameras=2, n=500, width=width, height=height, focal=6000.0,
+                     spread=1.4)
+    records, xy, rows, radii = project(v, width=width, height=height)
+    N = v["means"].shape[1]
+    images, P = 2, records.shape[0]
+    point_list, ranges = rendering.bin_records(records, 20, radii, None, N, images, width,
+                                               height, 0)
+    image_ids = torch.arange(P) // N
+    expect = O.bin_tiles(records[:, :17].cpu(), radii.cpu(), image_ids, images, width, height)
+    assert expect["point_list"].shape[0] > 1000
+    np.testing.assert_array_equal(point_list.cpu().numpy(), expect["point_list"])
+    np.testing.assert_array_equal(ranges.cpu().numpy(), expect["ranges"])
+
+    def keys(flags):
+        pl, rg = rendering.bin_records(records, 20, radii, None, N, images, width, height, flags)
+        lengths = (rg[:, 1] - rg[:, 0]).long()
+        assert int(lengths.sum()) == pl.shape[0]
+        tiles = torch.repeat_interleave(torch.arange(rg.shape[0], device="cuda"), lengths)
+        return tiles * P + pl.long()
+
+    square, tight = keys(0), keys(nat.BIN_TIGHT)
+    assert 0 < tight.shape[0] < square.shape[0]
+    ordered_keys, perm = torch.sort(square)
+    at = torch.searchsorted(ordered_keys, tight).clamp_(max=square.shape[0] - 1)
+    assert torch.equal(ordered_keys[at], tight), "tight entries missing from the square list"
+    position = perm[at]
+    assert bool((position[1:] > position[:-1]).all()), "tight list out of the square list's order"
