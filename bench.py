@@ -158,26 +158,32 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
+    def __init__(self, index, interval_ms=50):
         self.index = index
+        self.interval_ms = interval_ms
         self.proc = None
         self.lines = []
+        self.first = 0   # samples before this index precede the timed region
+        self.live = threading.Event()
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            self.live.wait(timeout=5)   # sampling has started before the timer does
         except (OSError, ValueError):
             self.proc = None
+        self.first = len(self.lines)
         return self
 
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+            self.live.set()
 
     def __exit__(self, *exc):
         if self.proc:
@@ -189,7 +195,7 @@ class ClockSampler:
 
     def summary(self):
         rows = []
-        for line in self.lines:
+        for line in self.lines[self.first:] or self.lines[-1:]:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 9:
                 try:
