@@ -1,0 +1,74 @@
+"""CPU: host-side logic of the optimiser, the graph-captured step and the work model
+(no GPU needed: every check here runs before any kernel would)."""
+
+import pytest
+import torch
+
+from diff_gabor_splatting_b200 import perfmodel
+from diff_gabor_splatting_b200.graphs import GraphedStep
+from diff_gabor_splatting_b200.optim import FusedAdam
+from diff_gabor_splatting_b200.workloads import Workload
+
+
+@pytest.mark.parametrize("kw,message", [
+    (dict(lr=-1.0), "Invalid learning rate"),
+    (dict(eps=-1e-8), "Invalid epsilon value"),
+    (dict(betas=(1.0, 0.999)), "Invalid beta parameter at index 0"),
+    (dict(betas=(0.9, -0.1)), "Invalid beta parameter at index 1"),
+    (dict(weight_decay=-0.1), "Invalid weight_decay value"),
+])
+def test_fused_adam_rejects_what_torch_adam_rejects(kw, message):
+    p = [torch.zeros(3, requires_grad=True)]
+    with pytest.raises(ValueError, match=message):
+        torch.optim.Adam(p, **kw)
+    with pytest.raises(ValueError, match=message):
+        FusedAdam(p, **kw)
+
+
+@pytest.mark.parametrize("capturable", [False, True])
+def test_init_state_allocates_zero_state_without_stepping(capturable):
+    a, b = torch.ones(5, requires_grad=True), torch.ones(2, 3, requires_grad=True)
+    opt = FusedAdam([a, b], capturable=capturable)
+    opt.init_state()
+    for p in (a, b):
+        state = opt.state[p]
+        assert set(state) == {"step", "exp_avg", "exp_avg_sq"}
+        assert float(state["step"]) == 0.0 and state["step"].dtype == torch.float32
+        assert state["exp_avg"].shape == p.shape and not state["exp_avg"].any()
+        assert not state["exp_avg_sq"].any()
+        assert torch.equal(p.detach(), torch.ones_like(p))
+    assert opt.param_groups[0]["capturable"] is capturable
+    first = opt.state[a]["exp_avg"]
+    opt.init_state()   # idempotent: existing state is kept
+    assert opt.state[a]["exp_avg"] is first
+
+
+def test_graphed_step_validates_before_any_gpu_work():
+    inputs = {"means": torch.zeros(1, 4, 3, requires_grad=True)}
+    loss = lambda rgb, alpha, meta: rgb.sum()   # noqa: E731
+    with pytest.raises(ValueError, match="packed=False"):
+        GraphedStep(None, inputs, loss, packed=True)
+    with pytest.raises(ValueError, match="capturable"):
+        GraphedStep(None, inputs, loss, optimizer=torch.optim.SGD(inputs.values(), lr=0.1))
+    with pytest.raises(ValueError, match="capturable"):
+        GraphedStep(None, inputs, loss, optimizer=FusedAdam(inputs.values(), capturable=False))
+
+
+def test_work_model_is_positive_and_scales_with_the_counts():
+    w = Workload(config=1, method="classic", scenes=1, cameras=4, surfels=500_000,
+                 width=1920, height=1080, sh_degree=3, packed=False, depth_normal_loss=False)
+    counts = dict(records=2_000_000, intersections=69_386_971, spans=12_307_690,
+                  forward_tests=916_009_984, forward_accepts=647_833_643,
+                  backward_tests=905_160_015, backward_accepts=647_833_643)
+    names = ["gs_project_forward", "gs_bin_count", "gs_bin_sort", "gs_composite_forward_split",
+             "gs_composite_backward_split", "gs_project_backward"]
+    for name in names:
+        m = perfmodel.stage_model(name, counts, w)
+        assert m["work"] > 0 and m["bound"] in ("hbm", "fp32"), name
+        doubled = perfmodel.stage_model(name, {k: 2 * v for k, v in counts.items()}, w)
+        if name.startswith(("gs_bin", "gs_composite")):
+            assert doubled["work"] == 2 * m["work"], name
+    backward = perfmodel.stage_model("gs_composite_backward_split", counts, w)
+    assert backward["unit"] == "TFLOP/s"
+    assert perfmodel.traffic("gs_composite_backward_split", counts) > 0
+    assert perfmodel.traffic("gs_bin_sort", counts) is None
