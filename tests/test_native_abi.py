@@ -39,6 +39,25 @@ def test_library_exports_every_declared_symbol():
     assert set(nat.SIGNATURES) <= set(names)
 
 
+def test_bindings_match_header_prototypes():
+    """Every ctypes binding has as many arguments as the header's prototype, and pointer
+    / integer / floating kinds line up argument by argument."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    kinds = {ctypes.c_void_p: "pointer", ctypes.c_char_p: "pointer", ctypes.c_int: "int",
+             ctypes.c_int64: "int", ctypes.c_uint64: "int", ctypes.c_size_t: "int",
+             ctypes.c_float: "float", ctypes.c_double: "float"}
+    for name, argtypes in nat.SIGNATURES.items():
+        match = re.search(r"\b" + name + r"\s*\(([^;]*?)\)\s*;", text, re.S)
+        assert match, name
+        params = [p.strip() for p in match.group(1).split(",") if p.strip() not in ("", "void")]
+        assert len(params) == len(argtypes), f"{name}: header {len(params)}, binding {len(argtypes)}"
+        for param, argtype in zip(params, argtypes):
+            declared = "pointer" if "*" in param else (
+                "float" if re.match(r"(const\s+)?(float|double)\b", param) else "int")
+            kind = "pointer" if issubclass(argtype, ctypes._Pointer) else kinds[argtype]
+            assert kind == declared, f"{name}: '{param}' bound as {argtype.__name__}"
+
+
 def test_invalid_arguments_fail_before_any_gpu_work():
     lib = nat.lib
     size = ctypes.c_size_t()
