@@ -72,3 +72,30 @@ def test_work_model_is_positive_and_scales_with_the_counts():
     assert backward["unit"] == "TFLOP/s"
     assert perfmodel.traffic("gs_composite_backward_split", counts) > 0
     assert perfmodel.traffic("gs_bin_sort", counts) is None
+
+
+def test_product_package_never_imports_the_oracle():
+    """The oracle is test infrastructure: only tests/, __graft_entry__.smoke() and
+    bench.py's CPU baseline may use it.  No module of the package imports it, and
+    importing the package does not load it."""
+    import ast
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    package = Path(__file__).resolve().parents[1] / "diff_gabor_splatting_b200"
+    for path in sorted(package.glob("*.py")):
+        tree = ast.parse(path.read_text())
+        for node in ast.walk(tree):
+            names = []
+            if isinstance(node, ast.Import):
+                names = [a.name for a in node.names]
+            elif isinstance(node, ast.ImportFrom):
+                names = [node.module or ""]
+            assert not any(n == "oracle" or n.startswith("oracle.") for n in names), path.name
+    code = ("import sys, diff_gabor_splatting_b200 as g; g.rasterize_gabors; "
+            "print(any(m == 'oracle' or m.startswith('oracle.') for m in sys.modules))")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         cwd=package.parent, timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == "False"
