@@ -99,3 +99,28 @@ def test_product_package_never_imports_the_oracle():
                          cwd=package.parent, timeout=300)
     assert out.returncode == 0, out.stderr
     assert out.stdout.strip() == "False"
+
+
+def test_missing_library_fails_loudly():
+    """Without the built library the package raises ImportError with build instructions
+    (no CPU or alternative-backend fallback)."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    code = (
+        "import pathlib\n"
+        "exists = pathlib.Path.exists\n"
+        "pathlib.Path.exists = lambda self: False if self.name == 'libgabor_b200.so' "
+        "else exists(self)\n"
+        "try:\n"
+        "    import diff_gabor_splatting_b200 as g\n"
+        "    g.rasterize_gabors\n"
+        "    print('loaded')\n"
+        "except ImportError as error:\n"
+        "    print('ImportError:', error)\n")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
+                         cwd=Path(__file__).resolve().parents[1], timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.startswith("ImportError:"), out.stdout
+    assert "no CPU or alternative-backend fallback" in out.stdout
