@@ -124,3 +124,39 @@ def test_missing_library_fails_loudly():
     assert out.returncode == 0, out.stderr
     assert out.stdout.startswith("ImportError:"), out.stdout
     assert "no CPU or alternative-backend fallback" in out.stdout
+
+
+def test_selection_groups_pixels_by_tile():
+    """Selected-pixel grouping (host side of the compositor's selected-pixel mode): every
+    pixel lands in exactly one group of at most 256 pixels of its own tile, in the stable
+    tile order, and per-chunk views rebase tiles and output indices."""
+    from diff_gabor_splatting_b200.rendering import Selection
+
+    g = torch.Generator().manual_seed(3)
+    W, H, images, P = 70, 45, 3, 900
+    x = torch.randint(0, W, (images, P), generator=g)
+    y = torch.randint(0, H, (images, P), generator=g)
+    x[1, :400], y[1, :400] = 5, 7   # one tile with more than 256 pixels (duplicates too)
+    pixels = torch.stack((x, y), -1)
+    sel = Selection(pixels, W, H)
+    tw, th = (W + 15) // 16, (H + 15) // 16
+    image = torch.arange(images).repeat_interleave(P)
+    tile = image * tw * th + (y.reshape(-1) // 16) * tw + x.reshape(-1) // 16
+    expected_order = torch.argsort(tile, stable=True)
+    assert torch.equal(sel.sel_index, expected_order)
+    seen = torch.zeros(images * P, dtype=torch.long)
+    for t, first, count in zip(sel.group_tile.tolist(), sel.group_first.tolist(),
+                               sel.group_count.tolist()):
+        assert 1 <= count <= 256
+        members = sel.sel_index[first:first + count]
+        assert bool((tile[members] == t).all())
+        seen[members] += 1
+    assert bool((seen == 1).all())
+    assert int(sel.group_count.sum()) == images * P
+    selected, groups = sel.for_images(1, 2)   # images 1-2 as one chunk
+    assert bool((groups[:, 0] >= 0).all()) and bool((groups[:, 0] < 2 * tw * th).all())
+    assert int(groups[:, 2].sum()) == 2 * P
+    for local_tile, first, count, _ in groups.tolist():
+        out = selected[first:first + count, 2].long()
+        assert bool((out >= 0).all()) and bool((out < 2 * P).all())
+        assert bool((tile[out + P] == local_tile + tw * th).all())
