@@ -10,8 +10,10 @@ Events (per pixel and record):
   accept  classic forward blend incl. 4-frequency appearance               100 flop
           neural forward blend incl. the 5->6->3 SIREN                     156 flop
   backward per tested sample                                                40 flop
-  backward per accepted sample: classic 400 flop, neural 520 flop
-          (forward replay + appearance and geometry adjoints)
+  backward per accepted sample: classic 400 flop, neural 448 flop
+          (forward replay + appearance and geometry adjoints; the neural weights of
+          the direction inputs and the direction gradient are formed once per (tile,
+          record) from the b1 sums, not per sample: 36 fused multiply-adds fewer)
 """
 
 from __future__ import annotations
@@ -22,7 +24,7 @@ FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # 74.4, nominal (no measu
 
 TEST_FLOP = 40
 ACCEPT_FLOP = {"classic": 100, "neural": 156}
-BACKWARD_ACCEPT_FLOP = {"classic": 400, "neural": 520}
+BACKWARD_ACCEPT_FLOP = {"classic": 400, "neural": 448}
 
 
 # DRAM bytes (read + write) of one launch measured with ncu on the config-1 small case
