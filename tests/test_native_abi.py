@@ -69,6 +69,13 @@ def test_invalid_arguments_fail_before_any_gpu_work():
     assert lib.gs_project_forward(*([None] * 11), 4, 1, 1, 1, 8, 8, 0.2, 100.0,
                                   None, None, None, None, None) == 1
     assert b"SH degree" in lib.gs_last_error()
+    # ragged projection: the per-scene surfel offsets are required
+    assert lib.gs_project_forward_ragged(*([None] * 11), 0, 1, 1, None, 1, 8, 8, 0.2, 100.0,
+                                         None, None, None, None, None) == 1
+    assert b"NULL offsets" in lib.gs_last_error()
+    assert lib.gs_project_backward_ragged(*([None] * 7), 0, 1, 1, None, 1, 1,
+                                          *([None] * 14), None) == 1
+    assert b"invalid offsets" in lib.gs_last_error()
     assert lib.gs_pack_rows(None, 4, 17, None, None) == 1
     assert lib.gs_sh_forward(None, None, None, 4, 1, 1, 1, None, None) == 1
     assert lib.gs_composite_forward(None, None, 0, None, 1, 1, 0, 0, None, None, None, 0, 8, 8, 0,
