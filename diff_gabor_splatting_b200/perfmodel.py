@@ -28,7 +28,7 @@ BACKWARD_ACCEPT_FLOP = {"classic": 400, "neural": 448}
 
 
 # DRAM bytes (read + write) of one launch measured with ncu on the config-1 small case
-# (N=100k, 1 camera; profiles/composite_kernels_config1_small.md) and the accepted
+# (N=100k surfels, 1 camera, ncu --set full) and the accepted
 # samples of that launch.  A full-size launch is estimated by scaling with its own
 # accepted samples (the compositors' DRAM traffic is the record batches, gradient
 # atomics and pixel buffers, all of which grow with the accepted work).

@@ -21,9 +21,10 @@ import torch
 
 ROOT = Path(__file__).resolve().parents[1]
 sys.path.insert(0, str(ROOT))
-sys.path.insert(0, str(ROOT / "oracle" / "_ref"))
 
-import gabor_splatting as ref  # noqa: E402
+from oracle import reference  # noqa: E402
+
+ref = reference.load()   # the compiled reference package, as module gs_reference
 
 from diff_gabor_splatting_b200.workloads import loss_of, make_workload  # noqa: E402
 
@@ -65,7 +66,10 @@ def main():
                       "value": w.pixels / (ms * 1e-3) / 1e6, "ms_per_step": ms,
                       "pixels_per_step": w.pixels, "steps": args.steps,
                       "calls_per_step": len(chunks), "surfels": w.surfels, "scenes": w.scenes,
-                      "cameras": w.cameras}), flush=True)
+                      "cameras": w.cameras, "validate": False,
+                      "chunking": ("one scene per call: the batch exceeds the reference's "
+                                   "int32 tile-intersection limit (rasterize.cu:469)"
+                                   if len(chunks) > 1 else "one call per step")}), flush=True)
 
 
 if __name__ == "__main__":

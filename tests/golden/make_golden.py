@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import importlib
 import inspect
+import os
 import sys
 import types
 from pathlib import Path
@@ -149,7 +150,11 @@ def projection_inputs(seed=0, n=96, cameras=3):
 
 
 def main():
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    # the reference checkout: argument, else $GS_REFERENCE_DIR, else a checkout named
+    # `reference` beside this repository
+    default = os.environ.get("GS_REFERENCE_DIR",
+                             Path(__file__).resolve().parents[3] / "reference")
+    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path(default)
     rendering, reference_render, evaluate_sh_reference = import_reference(root)
     torch.set_grad_enabled(True)
     out = {}

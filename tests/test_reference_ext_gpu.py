@@ -11,24 +11,17 @@ compiled unmodified for sm_100a into oracle/_ref/ (oracle/build_ref.sh).
 * SH colours: `SHColors` of both.
 """
 
-import sys
-from pathlib import Path
-
 import numpy as np
 import pytest
 import torch
 
 from helpers import appearance_names, assert_images_close, maps_from_result, ordered, random_scene
 
-ROOT = Path(__file__).resolve().parents[1]
-REF_DIR = ROOT / "oracle" / "_ref"
+from oracle import reference as reference_loader  # noqa: E402
+
 try:
-    if not (REF_DIR / "gabor_splatting").exists():
-        raise ImportError("oracle/_ref not built")
-    sys.path.insert(0, str(REF_DIR))
-    import gabor_splatting as ref
-    from gabor_splatting import _C as ref_C
-    from gabor_splatting import rendering as ref_rendering
+    ref = reference_loader.load()   # the reference package, as module gs_reference
+    ref_C, ref_rendering = ref._C, ref.rendering
 except ImportError:   # pragma: no cover - depends on the build container
     ref = None
 
