@@ -1133,18 +1133,28 @@ extern "C" int gs_bin_arena(const float* records, int record_stride, const int32
 //
 // Some callers cannot allocate device memory at the moment they need binning: a
 // renderer embedded in a host application whose allocator owns every device byte
-// (game-engine or DCC plugins with a fixed memory budget), code that runs while a
-// CUDA stream is being captured into a graph (cudaMalloc is not permitted during
-// capture), or real-time loops that forbid allocation after start-up.  For them the
-// two workspaces of gs_bin_count/gs_bin_sort live in one file-scope device array,
-// which every GPU that loads this library holds (32 MiB) until the process exits.
+// (game-engine or DCC plugins with a fixed memory budget), or a real-time loop that
+// forbids allocation after start-up.  For them the two workspaces of
+// gs_bin_count/gs_bin_sort live in one file-scope device array, which every GPU that
+// loads this library holds (80 MiB) until the process exits.
+//
+// Limits.  The workspaces grow with the records (count phase), the row spans, the
+// tile columns and the tiles (sort phase).  Within kStaticMaxRecords records,
+// kStaticMaxIntersections intersections (spans never exceed intersections),
+// kStaticMaxColumns tile columns and kStaticMaxTiles tiles over all images, the two
+// together stay below kStaticScratchBytes (the sort phase's largest case, 2^20 spans
+// over 128 columns, needs about 61 MiB with CUB's temporary storage; the count phase
+// 3.5 MiB).  The entry point checks each limit before any work and checks the
+// computed workspace sizes again before using the array.
 // ------------------------------------------------------------------------------
 namespace gs {
 namespace {
 
 constexpr int64_t kStaticMaxRecords = 65536;
 constexpr int64_t kStaticMaxIntersections = int64_t(1) << 20;
-constexpr size_t kStaticScratchBytes = size_t(32) << 20;
+constexpr int64_t kStaticMaxColumns = 128;                 // images up to 2048 px wide
+constexpr int64_t kStaticMaxTiles = int64_t(1) << 18;      // 16x16 tiles, all images
+constexpr size_t kStaticScratchBytes = size_t(80) << 20;
 
 static __device__ __align__(256) unsigned char g_bin_scratch[kStaticScratchBytes];
 
@@ -1152,7 +1162,11 @@ constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
 void* g_scratch_address[kMaxDevices] = {};
 
-// Device address of g_bin_scratch on the current device, looked up once per device.
+// Device address of g_bin_scratch on the current device.  Host code only knows the
+// array's host-side stand-in; the device address is looked up once per device (the
+// first gs_bin_static call made with that device current) and kept for the process.
+// A device reset (cudaDeviceReset) would invalidate the kept address: processes that
+// reset a device after using this entry point are not supported.
 int static_scratch(void** out) {
     int device = 0;
     GS_CUDA(cudaGetDevice(&device));
@@ -1185,6 +1199,14 @@ extern "C" int gs_bin_static(const float* records, int record_stride, const int3
     int st = check_common("gs_bin_static", records, record_stride, radii, records_count,
                           records_per_image, images, width, height);
     if (st) return st;
+    const int64_t tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
+    if (tw > kStaticMaxColumns)
+        return fail(GS_ERR_LIMIT, "gs_bin_static: image wider than 2048 pixels (128 tile "
+                                  "columns, the static scratch limit)");
+    if (images > kStaticMaxTiles / (tw * th) ||
+        images * tw * th > kStaticMaxTiles)
+        return fail(GS_ERR_LIMIT, "gs_bin_static: more than 262144 tiles over all images "
+                                  "(the static scratch limit)");
     void* scratch = nullptr;
     st = static_scratch(&scratch);
     if (st) return st;
