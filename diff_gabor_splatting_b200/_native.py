@@ -51,7 +51,7 @@ SIGNATURES = {
     "gs_adam_step": [_i, _p, _p, _p, _p, _p, ctypes.c_double, ctypes.c_double, ctypes.c_double,
                      ctypes.c_double, ctypes.c_double, _l, _p],
     "gs_adam_step_capturable": [_i, _p, _p, _p, _p, _p, _p, ctypes.c_double, ctypes.c_double,
-                                ctypes.c_double, ctypes.c_double, ctypes.c_double, _p],
+                                ctypes.c_double, ctypes.c_double, ctypes.c_double, _p, _p],
     "gs_pack_geometry": [_p, _p, _p, _l, _l, _p, _p],
     "gs_pack_rows": [_p, _l, _i, _p, _p],
     "gs_unpack_geometry_grads": [_p, _p, _l, _l, _p, _p, _p],

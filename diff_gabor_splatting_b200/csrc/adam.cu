@@ -15,7 +15,10 @@
 // The capturable form (gs_adam_step_capturable) keeps each tensor's step count on the
 // device, as torch.optim.Adam(capturable=True) does: one small launch increments the
 // counts, and the update computes the bias corrections from them (in double), so the
-// step can be recorded in a CUDA graph and replayed with the count advancing.
+// step can be recorded in a CUDA graph and replayed with the count advancing.  An
+// optional device flag lets a recorded step skip itself (counts and update) when the
+// step that produced the gradients went wrong -- for a graphed training step, when the
+// render's binning overflowed its arena and rendered background only.
 #include "common.cuh"
 
 namespace gs {
@@ -38,6 +41,8 @@ struct AdamTable {
     // capturable form: per-tensor step counts on the device (NULL: host scalars above)
     const float* step[kAdamTensors];
     double lr, beta1_d, beta2_d;
+    // capturable form: device flag (NULL: none); nonzero skips the whole step
+    const int32_t* skip;
 };
 
 struct AdamScalars {
@@ -57,6 +62,7 @@ __device__ __forceinline__ void adam_element(float& p, float g, float& m, float&
 __global__ __launch_bounds__(kAdamThreads) void adam_kernel(const AdamTable T) {
     AdamScalars s{T.beta1_weight, T.beta2, T.beta2_weight, T.eps, T.weight_decay,
                   T.step_size, T.bias2_sqrt};
+    if (T.skip && *T.skip) return;   // e.g. the render's binning overflowed its arena
     const int64_t block = blockIdx.x;
     int t = 0;
     while (t + 1 < T.tensors && T.first_block[t + 1] <= block) ++t;   // <= 48 tensors
@@ -96,6 +102,7 @@ __global__ __launch_bounds__(kAdamThreads) void adam_kernel(const AdamTable T) {
 
 // Advance each tensor's device step count by one (before the update reads it).
 __global__ void adam_count_kernel(AdamTable T) {
+    if (T.skip && *T.skip) return;
     const int t = threadIdx.x;
     if (t < T.tensors) *const_cast<float*>(T.step[t]) += 1.f;
 }
@@ -106,8 +113,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 // update launch each (preceded, with device step counts, by the count launch).
 int adam_launches(const char* fn, int tensors, float* const* params, const float* const* grads,
                   float* const* exp_avgs, float* const* exp_avg_sqs, const int64_t* sizes,
-                  float* const* steps, double lr, double beta1, double beta2, double eps,
-                  double weight_decay, double bias1, double bias2, cudaStream_t s) {
+                  float* const* steps, const int32_t* skip, double lr, double beta1,
+                  double beta2, double eps, double weight_decay, double bias1, double bias2,
+                  cudaStream_t s) {
     if (tensors < 0 || (tensors > 0 && (!params || !grads || !exp_avgs || !exp_avg_sqs || !sizes)))
         return fail(GS_ERR_ARGUMENT, std::string(fn) + ": invalid tensor table");
     if (!(lr >= 0.0) || !(eps >= 0.0) || !(beta1 >= 0.0 && beta1 < 1.0) ||
@@ -150,6 +158,7 @@ int adam_launches(const char* fn, int tensors, float* const* params, const float
         T.lr = lr;
         T.beta1_d = beta1;
         T.beta2_d = beta2;
+        T.skip = skip;
         if (steps) {
             adam_count_kernel<<<1, kAdamTensors, 0, s>>>(T);
             GS_CHECK_LAUNCH("adam_count_kernel");
@@ -174,7 +183,7 @@ extern "C" int gs_adam_step(int tensors, float* const* params, const float* cons
     const double bias1 = 1.0 - std::pow(beta1, double(step));
     const double bias2 = 1.0 - std::pow(beta2, double(step));
     return adam_launches("gs_adam_step", tensors, params, grads, exp_avgs, exp_avg_sqs, sizes,
-                         nullptr, lr, beta1, beta2, eps, weight_decay, bias1, bias2,
+                         nullptr, nullptr, lr, beta1, beta2, eps, weight_decay, bias1, bias2,
                          as_stream(stream));
 }
 
@@ -183,10 +192,10 @@ extern "C" int gs_adam_step_capturable(int tensors, float* const* params,
                                        float* const* exp_avg_sqs, const int64_t* sizes,
                                        float* const* steps, double lr, double beta1,
                                        double beta2, double eps, double weight_decay,
-                                       void* stream) {
+                                       const int32_t* skip, void* stream) {
     if (tensors > 0 && !steps)
         return fail(GS_ERR_ARGUMENT, "gs_adam_step_capturable: NULL step table");
     return adam_launches("gs_adam_step_capturable", tensors, params, grads, exp_avgs,
-                         exp_avg_sqs, sizes, steps, lr, beta1, beta2, eps, weight_decay, 1.0,
-                         1.0, as_stream(stream));
+                         exp_avg_sqs, sizes, steps, skip, lr, beta1, beta2, eps, weight_decay,
+                         1.0, 1.0, as_stream(stream));
 }

@@ -33,7 +33,8 @@ class GraphedStep:
 
     ``optimizer`` (a ``FusedAdam`` with ``capturable=True``) is stepped after the
     backward inside the graph: every replay updates its parameters and advances its
-    device step counts.  The warm-up steps that precede the capture leave the
+    device step counts, except a replay whose binning overflowed the arena, which
+    leaves them as they were.  The warm-up steps that precede the capture leave the
     parameters and the optimizer's state as they were.
     """
 
@@ -84,7 +85,14 @@ class GraphedStep:
         loss = self.loss_fn(rgb, alpha, meta)
         loss.backward()
         if self.optimizer is not None:
-            self.optimizer.step()
+            # a replay whose binning overflowed the arena rendered background only: its
+            # gradients are not the step's, so the recorded Adam step skips itself on
+            # the device (parameters, moments and step counts stay as they were)
+            self.optimizer.skip_flag = self.arena.overflow_flag()
+            try:
+                self.optimizer.step()
+            finally:
+                self.optimizer.skip_flag = None
         return loss.detach()
 
     def _save_training_state(self):

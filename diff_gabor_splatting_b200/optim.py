@@ -44,6 +44,10 @@ class FusedAdam(torch.optim.Optimizer):
             raise ValueError(f"Invalid weight_decay value: {weight_decay}")
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
                                       capturable=capturable))
+        # capturable steps only: a device int32 flag read when the step runs; nonzero
+        # leaves parameters, moments and step counts unchanged (set by GraphedStep to
+        # its arena's overflow flag)
+        self.skip_flag = None
 
     def init_state(self):
         """Create every parameter's state (zero moments, step 0) without stepping, so a
@@ -122,7 +126,12 @@ class FusedAdam(torch.optim.Optimizer):
                                    "parameters' device")
             by_device.setdefault(p.device, []).append((p, state))
         beta1, beta2 = group["betas"]
+        flag = self.skip_flag
+        if flag is not None and not (flag.is_cuda and flag.dtype == torch.int32
+                                     and flag.numel() == 1):
+            raise RuntimeError("FusedAdam.skip_flag must be a one-element int32 CUDA tensor")
         for device, items in by_device.items():
+            skip = nat.ptr(flag) if flag is not None and flag.device == device else None
             arrays = [nat.host_array(ctypes.c_void_p, ptrs) for ptrs in (
                 [p.data_ptr() for p, _ in items], [p.grad.data_ptr() for p, _ in items],
                 [s["exp_avg"].data_ptr() for _, s in items],
@@ -133,4 +142,4 @@ class FusedAdam(torch.optim.Optimizer):
                 nat.call("gs_adam_step_capturable", len(items), arrays[0][1], arrays[1][1],
                          arrays[2][1], arrays[3][1], sizes[1], arrays[4][1], float(group["lr"]),
                          float(beta1), float(beta2), float(group["eps"]),
-                         float(group["weight_decay"]), nat.stream_of(device))
+                         float(group["weight_decay"]), skip, nat.stream_of(device))

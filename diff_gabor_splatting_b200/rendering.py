@@ -453,6 +453,12 @@ class Arena:
         live = self.totals.tolist()
         return live[0] > self.max_intersections or live[1] > self.max_spans
 
+    def overflow_flag(self) -> torch.Tensor:
+        """Device int32 scalar, 1 when the latest binning exceeded the capacities
+        (computed on the device: no host read, so it can be recorded in a graph)."""
+        over = (self.totals[0] > self.max_intersections) | (self.totals[1] > self.max_spans)
+        return over.to(torch.int32).reshape(1)
+
     def needed(self) -> tuple[int, int]:
         """Live (intersections, spans) of the latest binning (one host read)."""
         return tuple(self.totals.tolist())

@@ -176,16 +176,21 @@ int gs_bin_arena(const float* records, int record_stride, const int32_t* radii,
                  int32_t* point_list, int32_t* ranges, int64_t* totals, void* stream);
 
 /* No-allocation binning: gs_bin_count followed by gs_bin_sort with both workspaces
- * taken from a 32 MiB array compiled into the library (one per GPU, held until
- * exit), for callers that cannot allocate device memory (a host application that
- * owns all device memory, code running during CUDA graph capture, allocation-free
- * real-time loops).  No counterpart in the reference.  Limits: at most 65536 records
- * and 1048576 tile intersections (GS_ERR_LIMIT beyond; *intersections still reports
- * the count when that is the cause).  point_list must hold point_list_capacity
- * entries.  The first call on a device looks the array up on the current device
- * (make that call before any stream capture).  All calls share the array: calls that
- * overlap on the GPU race, so serialise them (one stream, or events).  Waits on the
- * stream once, like gs_bin_count. */
+ * taken from an 80 MiB array compiled into the library (one per GPU that loads it,
+ * held until the process exits), for callers that cannot allocate device memory when
+ * they bin: a host application whose own allocator owns every device byte, or a
+ * real-time loop that forbids allocation after start-up.  No counterpart in the
+ * reference.  Square (reference) bins, flags 0.  Limits, each checked before any
+ * work (GS_ERR_LIMIT beyond; *intersections still reports the count when that is
+ * the cause): at most 65536 records, 1048576 tile intersections, images up to 2048
+ * pixels wide (128 tile columns) and 262144 16x16 tiles over all images; within them
+ * the workspaces always fit the array.  point_list must hold point_list_capacity
+ * entries.  The first call on a device looks the array's device address up with that
+ * device current (cudaGetSymbolAddress) and keeps it for the process: make that
+ * first call before any stream capture, and do not reset the device afterwards.
+ * Every call uses the same array: calls that overlap on the GPU race and corrupt each
+ * other's lists, so serialise them (one stream, or events).  Waits on the stream
+ * once, like gs_bin_count. */
 int gs_bin_static(const float* records, int record_stride, const int32_t* radii,
                   const int64_t* image_ids, int64_t records_count, int64_t records_per_image,
                   int64_t images, int width, int height, int32_t* point_list,
@@ -297,13 +302,16 @@ int gs_adam_step(int tensors, float* const* params, const float* const* grads,
  * array of device pointers, one float32 step count per tensor (its own, not shared),
  * which this call increments by one on the device before the update computes its bias
  * corrections from it (in double).  Nothing is read back to the host, so the call can
- * be recorded in a CUDA graph and replayed.  No counterpart in the reference's native
- * module.
+ * be recorded in a CUDA graph and replayed.  `skip` (nullable) is a device int32 flag
+ * read when the kernels run: nonzero leaves every parameter, moment and step count as
+ * it was (a recorded training step whose render overflowed its binning arena must not
+ * move the parameters).  No counterpart in the reference's native module.
  */
 int gs_adam_step_capturable(int tensors, float* const* params, const float* const* grads,
                             float* const* exp_avgs, float* const* exp_avg_sqs,
                             const int64_t* sizes, float* const* steps, double lr, double beta1,
-                            double beta2, double eps, double weight_decay, void* stream);
+                            double beta2, double eps, double weight_decay, const int32_t* skip,
+                            void* stream);
 
 /* ---------------------------------------------------------------------------
  * Layout converters for the reference-layout entry points (the `_C` mirror).

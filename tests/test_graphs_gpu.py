@@ -111,6 +111,36 @@ def test_graph_overflow_is_reported():
         GraphedStep(rasterize_gabors, static, _loss, width=W, height=H, packed=True)
 
 
+def test_graphed_training_step_skips_adam_when_the_arena_overflows():
+    """A replay whose binning overflowed renders background only; the recorded Adam step
+    then leaves parameters, moments and device step counts unchanged."""
+    from diff_gabor_splatting_b200.optim import FusedAdam
+
+    v = random_scene("classic", scenes=1, cameras=2, n=300, width=W, height=H)
+    static = {k: t.clone().requires_grad_() for k, t in ordered(v, "classic").items()}
+    trained = [k for k in static if k not in ("view_matrices", "intrinsics", "backgrounds")]
+    opt = FusedAdam([static[k] for k in trained], lr=1e-2, capturable=True)
+    step = GraphedStep(rasterize_gabors, static, _loss, optimizer=opt, width=W, height=H,
+                       max_intersections=16, max_spans=16)
+    before = {k: static[k].detach().clone() for k in trained}
+    for _ in range(2):
+        step.replay()
+    torch.cuda.synchronize()
+    assert step.arena.overflowed()
+    for k in trained:
+        assert torch.equal(static[k].detach(), before[k]), k
+        state = opt.state[static[k]]
+        assert float(state["step"]) == 0.0, k
+        assert state["exp_avg"].count_nonzero() == 0 and state["exp_avg_sq"].count_nonzero() == 0
+    # the same graph machinery with room in the arena does train
+    roomy = GraphedStep(rasterize_gabors, static, _loss, optimizer=opt, width=W, height=H)
+    roomy.replay()
+    torch.cuda.synchronize()
+    assert not roomy.arena.overflowed()
+    assert float(opt.state[static["means"]]["step"]) == 1.0
+    assert not torch.equal(static["means"].detach(), before["means"])
+
+
 @pytest.mark.parametrize("method", ["classic", "neural"])
 def test_graphed_training_step_matches_eager_training(method):
     """Render + loss + backward + FusedAdam(capturable) captured as one graph: three

@@ -131,13 +131,13 @@ def test_invalid_arguments_fail_before_any_gpu_work():
     one, one_ptr = nat.host_array(ctypes.c_int64, [1])
     ptrs, ptrs_ptr = nat.host_array(ctypes.c_void_p, [16])
     assert lib.gs_adam_step_capturable(1, ptrs_ptr, ptrs_ptr, ptrs_ptr, ptrs_ptr, one_ptr, None,
-                                       0.1, 0.9, 0.999, 1e-8, 0.0, None) == 1
+                                       0.1, 0.9, 0.999, 1e-8, 0.0, None, None) == 1
     assert b"NULL step table" in lib.gs_last_error()
     assert lib.gs_adam_step_capturable(0, None, None, None, None, None, None, 0.1, 0.9, 1.5,
-                                       1e-8, 0.0, None) == 1
+                                       1e-8, 0.0, None, None) == 1
     assert b"hyper-parameters" in lib.gs_last_error()
     assert lib.gs_adam_step_capturable(0, None, None, None, None, None, None, 0.1, 0.9, 0.999,
-                                       1e-8, 0.0, None) == 0   # nothing to do
+                                       1e-8, 0.0, None, None) == 0   # nothing to do
     # tiles beyond int32
     assert lib.gs_bin_sort_workspace(10, 10**10, 10, 1, 8, 8, ctypes.byref(size)) == 2
     assert lib.gs_bin_sort_workspace(10, 5, 6, 1, 8, 8, ctypes.byref(size)) == 1   # spans > slots
