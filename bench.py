@@ -10,14 +10,26 @@ the same metric with every step's inputs copied from pinned host memory (on a si
 stream, overlapping the previous step, as a prefetching loader does) and the loss read
 back.
 
-Default workload: config 1 (classic Gabor, SH degree 3, N=500k surfels, 4 cameras at
-1920x1080).  With N GPUs each rank renders its own independent scene of that size
-(scene sharding, weak scaling, no collective in the step).  Config 3 (32 scenes x 8
-cameras) shards its scenes across ranks (strong scaling).
+Default workload: config 3 (classic Gabor, SH degree 1, a fused batch of 32 independent
+scenes x 8 cameras at 256x256, N=50k surfels per scene, packed=True), the batched
+configuration the scaling target names.  It is strong-scaled: the 32 scenes are split
+into contiguous blocks over the N ranks (N=1 renders all 32), with no collective in the
+step; each rank renders its block in one call.  Config 4 shards the same way (cameras of
+a scene split over ranks, with an NCCL all-reduce of its parameter gradients, when there
+are more ranks than scenes); configs 0-2 (one scene) run one independent replica per
+rank (weak scaling), and --split-cameras splits config 1's cameras instead.
+
+Besides `value` (tight bins, the library's default) the line carries `square_bins`, the
+same step with the reference's square tile rectangles (point lists identical to the
+reference's), and, at N=1, `reference_cuda`: the reference's own CUDA extension
+(compiled unmodified into oracle/_ref) timed on the same workload, steps and loss in a
+child process after the timed region (oracle/ref_gpu_bench.py), with `vs_reference_cuda`
+= value / its value.  Renders run with validate=False on both sides (the reference's
+numerical checks cost one host synchronisation per call).
 
 --impl reference times the reference algorithm's CPU restatement (the oracle; the
-reference has no CPU renderer of its own) on a bounded pixel window of the same
-workload, on the host cores, rank 0 only.
+reference has no CPU renderer of its own) on a bounded pixel window of one camera of one
+scene of the same workload, on the host cores, rank 0 only.
 """
 
 from __future__ import annotations
@@ -57,10 +69,14 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    p.add_argument("--config", type=int, default=3, choices=[0, 1, 2, 3, 4])
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-square", action="store_true",
+                   help="skip the square-bins leg (the reference's tile rectangles)")
+    p.add_argument("--no-reference-cuda", action="store_true",
+                   help="skip timing the reference CUDA extension (N=1 only)")
     p.add_argument("--cpu-window", type=int, default=64, help="CPU sample window (pixels)")
     p.add_argument("--surfels", type=int, default=None, help="override N (profiling cases)")
     p.add_argument("--cameras", type=int, default=None, help="override C (profiling cases)")
@@ -332,7 +348,8 @@ def cpu_baseline(w, window, cores=None):
         torch.set_num_threads(cores)
     x0 = ((w.width - window) // 2) // 16 * 16
     y0 = ((w.height - window) // 2) // 16 * 16
-    sample = crop(w, x0, y0, min(window, w.width), min(window, w.height), camera_ids=[0])
+    sample = crop(w, x0, y0, min(window, w.width), min(window, w.height), camera_ids=[0],
+                  scene_ids=[0])
     names = (["input_weights", "input_biases", "output_weights", "output_biases"]
              if w.method == "neural" else
              ["colors", "secondary_colors", "frequency_weights", "frequency_magnitudes", "phases"])
@@ -346,8 +363,9 @@ def cpu_baseline(w, window, cores=None):
                                 sh_degree=sample.sh_degree)
     loss_of(rgb, alpha, meta, w.depth_normal_loss).backward()
     seconds = time.perf_counter() - t0
-    desc = (f"config {w.config}, camera 0, {sample.width}x{sample.height} window at "
-            f"({x0},{y0}), all {w.surfels} surfels projected; fwd+bwd with autograd")
+    desc = (f"config {w.config}, scene 0, camera 0, {sample.width}x{sample.height} window at "
+            f"({x0},{y0}), all {w.surfels} surfels of the scene projected (the projection is "
+            f"part of the per-window cost); fwd+bwd with autograd")
     return sample.pixels / seconds / 1e6, seconds, desc
 
 
@@ -385,6 +403,10 @@ def config_desc(w, parallelism):
               f"N={w.surfels} surfels/scene" + (", packed" if w.packed else ""),
             "global_batch": w.scenes * w.cameras, "pixels_per_step": w.pixels,
             "parallelism": parallelism,
+            "validate": False,
+            "validate_note": "renders called with validate=False (both this build and the "
+                             "reference CUDA arm); the reference's default validate=True adds "
+                             "its numerical checks and one host synchronisation per call",
             "l2": "working set larger than L2 (records, sort buffers and maps exceed 126 MB)"}
 
 
@@ -474,8 +496,16 @@ def main():
         e2e = {"value": pixels_all * args.steps / (ems * 1e-3) / 1e6, "unit": "Mpix/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                "ms_per_step": ems / args.steps,
-               "copies": "pinned host -> device on a side stream, overlapping the previous step"}
+               "copies": "pinned host -> device on a side stream, overlapping the previous step",
+               "read_back": "the step's loss (4 bytes); images and gradients stay on the "
+                            "device, as in an on-device training loop"}
+    square = None
+    if not args.no_square and opt is None:
+        square = square_leg(args, job, fn, calls, device, world, pixels_all)
     graph = graph_leg(args, job, fn, calls, device, world, pixels_all) if args.graph else None
+    ref_cuda = None
+    if rank == 0 and world == 1 and not args.no_reference_cuda and not args.pixels:
+        ref_cuda = reference_cuda(args)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cores = os.cpu_count() or 1
@@ -497,6 +527,14 @@ def main():
             line["config"]["selected_pixels_per_camera"] = args.pixels
             line["config"]["pixels_per_step"] = pixels_all
             line["roofline"]["note"] = "kernel work counted on a full render of the workload"
+        if square is not None:
+            line["square_bins"] = square
+        if ref_cuda is not None:
+            line["reference_cuda"] = ref_cuda
+            if ref_cuda.get("value"):
+                line["vs_reference_cuda"] = value / ref_cuda["value"]
+                if e2e is not None:
+                    line["e2e_vs_reference_cuda"] = e2e["value"] / ref_cuda["value"]
         if graph is not None:
             line["graph"] = graph
         if opt is not None:
@@ -505,6 +543,70 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def square_leg(args, job, fn, calls, device, world, pixels_all):
+    """The same step with the reference's square tile rectangles (``TIGHT_BINNING =
+    False``): point lists identical to the reference's, so the gain of tight binning is
+    separable from the kernels'.  Timed like the main loop (device events, max over
+    ranks)."""
+    from diff_gabor_splatting_b200 import rendering
+
+    previous = rendering.TIGHT_BINNING
+    rendering.TIGHT_BINNING = False
+    try:
+        for _ in range(2):
+            step(fn, job, calls)
+        rendering.WORK = {}
+        try:
+            step(fn, job, calls)
+            torch.cuda.synchronize()
+            intersections = rendering.WORK.get("intersections", 0)
+        finally:
+            rendering.WORK = None
+        barrier(world)
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            step(fn, job, calls)
+        s1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        sms = max_over_ranks(s0.elapsed_time(s1), world, device)
+    finally:
+        rendering.TIGHT_BINNING = previous
+    return {"value": pixels_all * args.steps / (sms * 1e-3) / 1e6, "unit": "Mpix/s",
+            "ms_per_step": sms / args.steps, "intersections_rank0": intersections,
+            "binning": "square tile rectangles (the reference's bins; point lists identical "
+                       "to the reference's)"}
+
+
+def reference_cuda(args):
+    """The reference's CUDA extension (oracle/_ref, compiled unmodified for sm_100a) on
+    the same workload, steps, warm-up and loss, timed in a child process after this
+    process's timed region (oracle/ref_gpu_bench.py).  Measurement only: nothing of the
+    reference runs in this build's step."""
+    script = ROOT / "oracle" / "ref_gpu_bench.py"
+    ref_pkg = ROOT / "oracle" / "_ref" / "gabor_splatting"
+    if not ref_pkg.exists():
+        return {"unavailable": "the compiled reference is not in oracle/_ref"}
+    cmd = [sys.executable, str(script), "--config", str(args.config), "--steps",
+           str(args.steps), "--warmup", str(max(args.warmup, 3))]
+    for flag, value in (("--surfels", args.surfels), ("--cameras", args.cameras),
+                        ("--scenes", args.scenes)):
+        if value:
+            cmd += [flag, str(value)]
+    torch.cuda.empty_cache()   # leave the device memory to the child
+    try:
+        out = subprocess.run(cmd, capture_output=True, text=True, timeout=1500)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "reference timing exceeded 1500 s"}
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    if out.returncode != 0 or not lines:
+        return {"unavailable": f"reference timing failed (rc {out.returncode}): "
+                               + (out.stderr.strip().splitlines() or [""])[-1][:300]}
+    return json.loads(lines[-1])
 
 
 def graph_leg(args, job, fn, calls, device, world, pixels_all):

@@ -162,21 +162,22 @@ def loss_of(rgb, alpha, meta, depth_normal: bool):
 
 
 def crop(w: Workload, x0: int, y0: int, width: int, height: int,
-         camera_ids=None) -> Workload:
-    """The same scene seen through a pixel window of some cameras.
+         camera_ids=None, scene_ids=None) -> Workload:
+    """The same scenes seen through a pixel window of some cameras.
 
     Shifting the principal point by (-x0, -y0) makes pixel (x, y) of the crop
     the pixel (x0 + x, y0 + y) of the full image: the same rays, so the same values.
     Used to time the CPU oracle on a bounded sample of a large workload.
     """
     cams = list(range(w.cameras)) if camera_ids is None else list(camera_ids)
-    inputs = dict(w.inputs)
-    views = w.inputs["view_matrices"][:, cams].clone()
-    K = w.inputs["intrinsics"][:, cams].clone()
+    scenes = list(range(w.scenes)) if scene_ids is None else list(scene_ids)
+    inputs = {k: v[scenes].contiguous() for k, v in w.inputs.items()}
+    views = inputs["view_matrices"][:, cams].clone()
+    K = inputs["intrinsics"][:, cams].clone()
     K[..., 0, 2] -= x0
     K[..., 1, 2] -= y0
     inputs["view_matrices"], inputs["intrinsics"] = views.contiguous(), K.contiguous()
-    inputs["backgrounds"] = w.inputs["backgrounds"][:, cams].contiguous()
-    return Workload(config=w.config, method=w.method, scenes=w.scenes, cameras=len(cams),
+    inputs["backgrounds"] = inputs["backgrounds"][:, cams].contiguous()
+    return Workload(config=w.config, method=w.method, scenes=len(scenes), cameras=len(cams),
                     surfels=w.surfels, width=width, height=height, sh_degree=w.sh_degree,
                     packed=w.packed, depth_normal_loss=w.depth_normal_loss, inputs=inputs)
