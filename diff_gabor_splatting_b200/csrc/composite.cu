@@ -78,9 +78,16 @@ struct Params {
     unsigned long long* counters;
 };
 
-// The pixel a thread composites: in tile mode pixel (rank % 16, rank / 16) of tile
-// blockIdx.x, output index (image H + y) W + x; in selected-pixel mode the rank-th pixel
-// of group blockIdx.x (threads past the group's count are outside).
+// Each warp of a tile CTA composites an 8x4 block of the 16x16 tile (warps 0-1 the top
+// two blocks, and so on).  A splat covers a compact patch of a tile, which touches fewer
+// 8x4 blocks than 16x2 rows: fewer warps run a record's accept path with most lanes
+// idle (measured: config 3 compositors 61.6 -> 56.8 ms, config 1 19.0 -> 18.3 ms).
+constexpr int kWarpW = 8, kWarpH = 4, kWarpBlocksX = kTile / kWarpW;
+
+// The pixel a thread composites: in tile mode pixel (x, y) of tile blockIdx.x from the
+// warp's block and the lane's place in it, output index (image H + y) W + x; in
+// selected-pixel mode the rank-th pixel of group blockIdx.x (threads past the group's
+// count are outside).
 struct PixelSlot {
     int tile, image, x, y;
     int64_t pixel;
@@ -103,8 +110,9 @@ __device__ __forceinline__ PixelSlot pixel_slot(const Params& P, int rank) {
         q.tile = blockIdx.x;
         q.image = q.tile / tiles_per_image;
         const int local = q.tile % tiles_per_image;
-        q.x = (local % P.tw) * kTile + rank % kTile;
-        q.y = (local / P.tw) * kTile + rank / kTile;
+        const int lane = rank & 31, warp = rank >> 5;
+        q.x = (local % P.tw) * kTile + (warp % kWarpBlocksX) * kWarpW + lane % kWarpW;
+        q.y = (local / P.tw) * kTile + (warp / kWarpBlocksX) * kWarpH + lane / kWarpW;
         q.inside = q.x < P.width && q.y < P.height;
         q.pixel = (int64_t(q.image) * P.height + q.y) * P.width + q.x;
     }
