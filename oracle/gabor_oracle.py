@@ -338,6 +338,10 @@ def composite(geometry, appearance, opacities, primitive_ids, backgrounds, point
     # median depth: the depth of the last contribution made while the transmittance
     # before it exceeds 0.5 (the 2DGS convention; an addition beyond the reference)
     median = torch.zeros_like(T)
+    # test support: per pixel, the smallest |T - 0.5| over accepted contributions (the
+    # transmittance before each); a median that differs between two roundings of the
+    # same pixel needs a contribution this close to the 0.5 threshold
+    median_margin = torch.full_like(T, float("inf"))
     max_len = int(lens.max()) if n else 0
     one = torch.ones((), dtype=dtype)
     for j in range(max_len):
@@ -389,6 +393,8 @@ def composite(geometry, appearance, opacities, primitive_ids, backgrounds, point
         m1 = m1 + w * m
         m2 = m2 + w * m * m
         median = torch.where(accept & (T > 0.5), dsafe, median)
+        median_margin = torch.where(accept, torch.minimum(median_margin, (T - 0.5).abs()),
+                                    median_margin)
         T = torch.where(accept, nxt, T)
         last = torch.where(accept, torch.full_like(last, j + 1), last)
     bg = backgrounds[image][:, None, :]
@@ -402,7 +408,7 @@ def composite(geometry, appearance, opacities, primitive_ids, backgrounds, point
     contributors = torch.where(inside, last, torch.zeros_like(last)).to(torch.int32)
     median = torch.where(inside, median, zero)
     return dict(maps=maps, state=state, contributors=contributors, inside=inside, tiles=tiles,
-                median_depth=median)
+                median_depth=median, median_margin=median_margin.detach())
 
 
 def tiles_to_images(tile_values, images, width, height):
@@ -471,4 +477,5 @@ def render(means, quaternions, scales, opacities, appearance, view_matrices, int
         meta["_binning"] = binned
         meta["_state"] = tiles_to_images(comp["state"], images, width, height)
         meta["_contributors"] = tiles_to_images(comp["contributors"], images, width, height)
+        meta["_median_margin"] = tiles_to_images(comp["median_margin"], images, width, height)
     return maps[..., :3], maps[..., 3:4], meta

@@ -266,7 +266,12 @@ def test_projected_means_receive_screen_gradient():
 def test_median_depth_matches_oracle(method):
     """meta["median_depth"] (an addition: the depth of the last contribution made while
     the transmittance before it exceeds 0.5, the 2DGS convention) against the float64
-    oracle's restatement, values and the gradient of a loss on it."""
+    oracle's restatement.  The reference has no median depth, so the oracle is the
+    anchor.  A pixel may differ only where the float32 kernels and the float64 oracle
+    legitimately decide differently: a contribution whose transmittance before it lies
+    within 1e-4 of the 0.5 threshold, or an acceptance flip upstream (visible as a
+    different alpha); such pixels are counted and bounded, every other pixel agrees to
+    1e-5, and the gradient of a loss on the agreeing pixels matches the oracle's."""
     from oracle import gabor_oracle as O
     from helpers import random_scene
 
@@ -282,12 +287,18 @@ def test_median_depth_matches_oracle(method):
     _, o_alpha, o_meta = O.render(cpu["means"], cpu["quaternions"], cpu["scales"],
                                   cpu["opacities"], app, cpu["view_matrices"], cpu["intrinsics"],
                                   40, 30, backgrounds=cpu["backgrounds"], neural=method == "neural",
-                                  dtype=torch.float64)
+                                  dtype=torch.float64, return_internals=True)
     expected = o_meta["median_depth"]
-    close = torch.isclose(median.detach().cpu().double(), expected, rtol=1e-5, atol=1e-5)
-    assert close.double().mean().item() >= 0.99   # rare float32 threshold flips
-    # gradient of a weighted median-depth loss through the median contribution's depth
-    w = torch.linspace(0.5, 1.5, median.numel()).reshape(median.shape)
+    got = median.detach().cpu().double()
+    agree = torch.isclose(got, expected, rtol=1e-5, atol=1e-5)
+    threshold_case = o_meta["_median_margin"].reshape(agree.shape) < 1e-4
+    flipped_upstream = ~torch.isclose(alpha.detach().cpu().double(), o_alpha.detach(),
+                                      rtol=1e-5, atol=1e-6)
+    unexplained = ~agree & ~threshold_case & ~flipped_upstream
+    assert int(unexplained.sum()) == 0, f"{int(unexplained.sum())} pixels differ unexplained"
+    assert int((~agree).sum()) <= max(2, agree.numel() // 500), int((~agree).sum())
+    # gradient of a weighted median-depth loss on the agreeing pixels
+    w = torch.linspace(0.5, 1.5, median.numel()).reshape(median.shape) * agree.float()
     (median * w.cuda()).sum().backward()
     (expected * w.double()).sum().backward()
     reference_norm = cpu["means"].grad.norm().item()
@@ -297,7 +308,7 @@ def test_median_depth_matches_oracle(method):
         # means gradient's norm
         a, e = mine[name].grad.cpu().double(), cpu[name].grad
         rel = (a - e).norm().item() / max(e.norm().item(), reference_norm)
-        assert rel <= 2e-2, f"{name}: relative L2 {rel:.2e}"
+        assert rel <= 1e-4, f"{name}: relative L2 {rel:.2e}"
     # without the flag the key is absent and nothing changes
     _, _, plain = fn(**{k: t.detach() for k, t in mine.items()}, width=40, height=30)
     assert "median_depth" not in plain
