@@ -505,7 +505,10 @@ constexpr int kLaneStride = 36;   // 32 fields + 4 pad: a lane's 16-byte stores 
 template <bool Neural>
 struct BackShared {
     using F = Fields<Neural>;
-    static constexpr int kStride = (F::kCount + 3) / 4 * 4;   // 36 classic, 56 neural
+    // per (warp, record) row of field sums.  Classic: 33 floats, an odd stride, so the
+    // flush's reads (thread i: record i / 10, fields 4 (i % 10) + k) spread over the
+    // banks instead of four-way conflicts with a stride of 36.  Neural: 56.
+    static constexpr int kStride = Neural ? (F::kCount + 3) / 4 * 4 : F::kCount;
     Batch<Neural, kBackBatch> batch[2];        // double-buffered: batch b+1 lands during b
     float4 weights01[2][Neural ? 1 : kBackBatch];
     float rows[kWarps][kBackBatch][kStride];   // per (warp, record) field sums
