@@ -189,12 +189,16 @@ __device__ __forceinline__ int pair_radius(const Pair& p, int tw, int th, float 
     visible = visible && isfinite(radius) && radius < 1073741824.f && isfinite(p.xy[0]) &&
               isfinite(p.xy[1]);
     if (!visible) return 0;
-    const float tile = float(kTile), lim[2] = {float(tw), float(th)};
+    // x / 16 is exact in binary floating point: the product with 1/16 rounds to the same
+    // value as the division, without a division sequence
+    constexpr float kInvTile = 1.f / kTile;
+    const float lim[2] = {float(tw), float(th)};
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-        float lower = fmaxf(truncf(__fdiv_rn(__fsub_rn(p.xy[i], radius), tile)), 0.f);
+        float lower = fmaxf(truncf(__fmul_rn(__fsub_rn(p.xy[i], radius), kInvTile)), 0.f);
         float upper =
-            fmaxf(truncf(__fdiv_rn(__fadd_rn(__fadd_rn(p.xy[i], radius), float(kTile - 1)), tile)), 0.f);
+            fmaxf(truncf(__fmul_rn(__fadd_rn(__fadd_rn(p.xy[i], radius), float(kTile - 1)), kInvTile)),
+                  0.f);
         if (!(fminf(upper, lim[i]) > fminf(lower, lim[i]))) return 0;
     }
     return int(radius);
@@ -398,8 +402,9 @@ __global__ __launch_bounds__(kProjThreads, 2) void project_backward_kernel(
                     }
                     if (p.valid) {
                         float gden = 0.f;
+                        const float inv_denom = 1.f / p.denom;
 #pragma unroll
-                        for (int j = 0; j < 3; ++j) gden -= gf[j] * p.f[j] / p.denom;
+                        for (int j = 0; j < 3; ++j) gden -= gf[j] * p.f[j] * inv_denom;
 #pragma unroll
                         for (int j = 0; j < 3; ++j) gT[2][j] += gden * 2.f * t[j] * p.T[2][j];
                     }

@@ -120,6 +120,28 @@ class Projection(torch.autograd.Function):
                 g_p, None, None, None, None, None)
 
 
+class PackedRows(torch.autograd.Function):
+    """``values[selected]`` for the packed metadata, whose backward scatters into zeros.
+
+    ``selected`` holds distinct, increasing pair indices, so the adjoint is a plain
+    scatter (``index_copy_``); autograd's generic indexing backward would sort the
+    indices and accumulate (about 2.5 ms per call for a 10M-pair batch).
+    """
+
+    @staticmethod
+    def forward(ctx, values, selected):
+        ctx.save_for_backward(selected)
+        ctx.rows = values.shape[0]
+        return values.index_select(0, selected)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad):
+        (selected,) = ctx.saved_tensors
+        out = grad.new_zeros((ctx.rows,) + tuple(grad.shape[1:]))
+        return out.index_copy_(0, selected, grad.contiguous()), None
+
+
 # channels of the five map planes the compositor writes: rgb, alpha, accumulated depth,
 # normals, distortion (together the reference's [..][9] maps, in that order)
 PLANES = (3, 1, 1, 3, 1)
@@ -279,7 +301,7 @@ class Composite(torch.autograd.Function):
                      _at(g_records, ch.record0 * nat.RECORD_FLOATS), _at(g_xy, ch.record0 * 2),
                      _at(g_rows, a["row0"] * rows.shape[1]), _at(g_bg, ch.image0 * 3),
                      nat.ptr(_counters("backward", device)), stream)
-        g_pm = g_xy if selected is None else g_xy[selected]
+        g_pm = g_xy if selected is None else g_xy.index_select(0, selected)
         return (g_records, g_pm, g_rows, g_bg) + (None,) * 14
 
 
@@ -778,12 +800,24 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
                          + [means.new_zeros((S * N, pad))], -1)
         row_mode = nat.ROWS_PER_SURFEL
     images = S * C
+    visible_count = None
+    if packed:
+        # The packed metadata needs the number of visible pairs on the host.  Count them
+        # on the device and copy the count to pinned memory ahead of binning: binning
+        # reads its own totals back with one stream synchronisation per call (as the
+        # reference's does, rasterize.cu:466-468), after which the count is readable, so
+        # packing adds no second synchronisation (torch.nonzero would).
+        visible = radii > 0
+        visible_count = torch.empty((), dtype=torch.int64, pin_memory=True)
+        visible_count.copy_(visible.sum(), non_blocking=True)
     chunks = bin_chunks(records, radii, S, C, max(N, 1), width, height)
     selected = None
     projected_means = xy
     if packed:
-        selected = torch.nonzero(radii > 0).reshape(-1)
-        projected_means = xy[selected]
+        if ARENA is not None or P == 0:   # binning made no host synchronisation
+            torch.cuda.current_stream(device).synchronize()
+        selected = torch.nonzero_static(visible, size=int(visible_count)).reshape(-1)
+        projected_means = PackedRows.apply(xy, selected)
     selection = None
     pixel_shape = (height, width)
     if pixels is not None:
@@ -797,7 +831,7 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
         plane.reshape(batch + (C,) + pixel_shape + (plane.shape[-1],)) for plane in outputs[:5])
     ids = selected if packed else torch.arange(P, device=device)
     meta = {
-        "radii": radii[selected] if packed else radii.reshape(batch + (C, N)),
+        "radii": radii.index_select(0, selected) if packed else radii.reshape(batch + (C, N)),
         "projected_means": projected_means,
         "scene_ids": ids // (C * max(N, 1)),
         "camera_ids": ids // max(N, 1) % C,
