@@ -61,7 +61,8 @@ OWN_KERNELS = {"gs_project_forward": 1, "gs_project_backward": 1, "gs_bin_count"
                "gs_composite_forward_split": 1, "gs_composite_backward_split": 1,
                "gs_sh_forward": 1, "gs_sh_backward": 1, "gs_pack_geometry": 1,
                "gs_pack_rows": 1, "gs_unpack_geometry_grads": 1, "gs_unpack_rows": 1,
-               "gs_adam_step": 1, "gs_adam_step_capturable": 2, "gs_bin_arena": 6}
+               "gs_adam_step": 1, "gs_adam_step_capturable": 2, "gs_bin_arena": 6,
+               "gs_pair_ids": 1}
 
 
 def parse():
@@ -104,8 +105,12 @@ def dist_setup(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
-        torch.distributed.init_process_group(
-            "nccl" if args.impl == "ours" else "gloo", timeout=timedelta(seconds=300))
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+            torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                                 device_id=torch.device("cuda", local))
+        else:
+            torch.distributed.init_process_group("gloo", timeout=timedelta(seconds=300))
     return world, rank, local
 
 

@@ -54,6 +54,30 @@ __global__ void unpack_geometry_kernel(int64_t Q, const float* __restrict__ grad
     if (k < 17) grad_geometry[q * 17 + k] = v;
     else if (v != 0.f) atomicAdd(grad_opacities + prim_ids[q], v);
 }
+// Scene, camera and surfel of each reported pair p = (s C + c) N + n.  Unsigned 32-bit
+// division when the pair index and the divisors fit (the usual case), 64-bit otherwise.
+__global__ void pair_ids_kernel(int64_t count, const int64_t* __restrict__ pairs, int64_t C,
+                                int64_t N, bool narrow, int64_t* __restrict__ scene_ids,
+                                int64_t* __restrict__ camera_ids,
+                                int64_t* __restrict__ primitive_ids) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const int64_t p = pairs ? pairs[i] : i;
+    int64_t image, n;
+    narrow = narrow && p >= 0 && p <= 0xffffffffLL;
+    if (narrow) {
+        const unsigned q = unsigned(p) / unsigned(N);
+        image = q;
+        n = int64_t(unsigned(p) - q * unsigned(N));
+    } else {
+        image = p / N;
+        n = p - image * N;
+    }
+    const int64_t s = narrow ? int64_t(unsigned(image) / unsigned(C)) : image / C;
+    if (scene_ids) scene_ids[i] = s;
+    if (camera_ids) camera_ids[i] = image - s * C;
+    if (primitive_ids) primitive_ids[i] = n;
+}
 }  // namespace
 
 void set_error(const std::string& message) { g_last_error = message; }
@@ -116,5 +140,18 @@ extern "C" int gs_unpack_rows(const float* rows, int64_t A, int width, float* ap
     unpack_rows_kernel<<<blocks_for(A * width), kPackThreads, 0, as_stream(stream)>>>(
         A, width, padded, rows, appearance);
     GS_CHECK_LAUNCH("unpack_rows_kernel");
+    return GS_OK;
+}
+
+extern "C" int gs_pair_ids(const int64_t* pairs, int64_t count, int64_t cameras, int64_t surfels,
+                           int64_t* scene_ids, int64_t* camera_ids, int64_t* primitive_ids,
+                           void* stream) {
+    if (count < 0 || cameras < 1 || surfels < 1)
+        return fail(GS_ERR_ARGUMENT, "gs_pair_ids: invalid sizes");
+    if (count == 0) return GS_OK;
+    const bool narrow = cameras <= 0xffffffffLL && surfels <= 0xffffffffLL;
+    pair_ids_kernel<<<blocks_for(count), kPackThreads, 0, as_stream(stream)>>>(
+        count, pairs, cameras, surfels, narrow, scene_ids, camera_ids, primitive_ids);
+    GS_CHECK_LAUNCH("pair_ids_kernel");
     return GS_OK;
 }

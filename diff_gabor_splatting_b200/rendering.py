@@ -829,13 +829,18 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
                               selection)
     rgb, alpha, depth, normals, distortion = (
         plane.reshape(batch + (C,) + pixel_shape + (plane.shape[-1],)) for plane in outputs[:5])
-    ids = selected if packed else torch.arange(P, device=device)
+    count = selected.shape[0] if packed else P
+    scene_ids, camera_ids, primitive_ids = (torch.empty((count,), device=device, dtype=torch.int64)
+                                            for _ in range(3))
+    nat.call("gs_pair_ids", nat.ptr(selected) if packed else None, count, C, max(N, 1),
+             nat.ptr(scene_ids), nat.ptr(camera_ids), nat.ptr(primitive_ids),
+             nat.stream_of(device))
     meta = {
         "radii": radii.index_select(0, selected) if packed else radii.reshape(batch + (C, N)),
         "projected_means": projected_means,
-        "scene_ids": ids // (C * max(N, 1)),
-        "camera_ids": ids // max(N, 1) % C,
-        "primitive_ids": ids % max(N, 1),
+        "scene_ids": scene_ids,
+        "camera_ids": camera_ids,
+        "primitive_ids": primitive_ids,
         "packed": packed,
         "accumulated_depth": depth,
         "normals": normals,

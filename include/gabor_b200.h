@@ -332,6 +332,14 @@ int gs_unpack_geometry_grads(const float* grad_records, const int64_t* primitive
 int gs_unpack_rows(const float* rows, int64_t rows_count, int width, float* appearance,
                    void* stream);
 
+/* Metadata ids of reported pairs (rendering.py:389-399: scene_ids, camera_ids,
+ * primitive_ids = pair // (C N), pair // N % C, pair % N) in one pass: for i < count the
+ * pair p = pairs[i] (pairs NULL: p = i) of the dense (scene, camera, surfel) layout
+ * p = (s C + c) N + n gives scene_ids[i] = s, camera_ids[i] = c, primitive_ids[i] = n
+ * (int64 outputs, each nullable). */
+int gs_pair_ids(const int64_t* pairs, int64_t count, int64_t cameras, int64_t surfels,
+                int64_t* scene_ids, int64_t* camera_ids, int64_t* primitive_ids, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Spherical-harmonic colours (spherical_harmonics.cu:45-150) for the
  * SHColors entry points.  first/second [B][N][K][3], directions [B][C][N][3],
