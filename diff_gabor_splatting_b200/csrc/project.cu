@@ -538,37 +538,67 @@ __global__ __launch_bounds__(kProjThreads, 2) void project_backward_kernel(
         }
         if constexpr (Degree >= 0) {
             if (live) {
-                // SH coefficient gradients: for each (colour set, channel) sum over the
-                // scene's cameras of g * basis(dir) where the clamp passes; recomputing
-                // the basis per (set, channel) keeps 3K accumulators live, not 6K.
+                // SH coefficient gradients: sum over the scene's cameras of g * basis(dir)
+                // where the clamp passes, per (colour set, channel).  The camera loop is
+                // outermost, so each camera's direction and basis are evaluated once per
+                // pass and its six colour gradients read with two vector loads; degrees
+                // 0-1 take both sets in one pass (6K accumulators), degrees 2-3 one set
+                // per pass (3K).  Per accumulator the cameras add in order, as before.
+                constexpr int kSets = Degree <= 1 ? 2 : 1;
 #pragma unroll 1
-                for (int sc = 0; sc < 6; ++sc) {
-                    const int set = sc / 3, ch = sc % 3;
-                    const float* cf = (set == 0 ? sh_first : sh_second) + sn * K * 3;
-                    float coef[K], acc[K];
+                for (int pass = 0; pass < 2 / kSets; ++pass) {
+                    float acc[kSets][3][K];
 #pragma unroll
-                    for (int k = 0; k < K; ++k) { coef[k] = __ldg(cf + k * 3 + ch); acc[k] = 0.f; }
+                    for (int t = 0; t < kSets; ++t)
+#pragma unroll
+                        for (int ch = 0; ch < 3; ++ch)
+#pragma unroll
+                            for (int k = 0; k < K; ++k) acc[t][ch][k] = 0.f;
                     for (int64_t c = 0; c < C; ++c) {
                         const int64_t pid = C * base + c * N + n;
-                        const float g = grad_rows[pid * GS_CLASSIC_ROW_FLOATS + set * 3 + ch];
-                        if (g == 0.f) continue;
+                        const float4* grow =
+                            reinterpret_cast<const float4*>(grad_rows) + pid * (GS_CLASSIC_ROW_FLOATS / 4);
+                        const float4 q0 = grow[0], q1 = grow[1];
+                        const float gall[6] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y};
+                        bool any = false;
+#pragma unroll
+                        for (int t = 0; t < kSets; ++t)
+#pragma unroll
+                            for (int ch = 0; ch < 3; ++ch)
+                                any = any || gall[(pass * kSets + t) * 3 + ch] != 0.f;
+                        if (!any) continue;
                         Camera cam;
                         load_camera(cam, views, intr, s * C + c);
-                        float dir[3];
+                        float dir[3], basis[K];
                         view_direction(v, cam, dir);
-                        float basis[K];
                         sh_basis<Degree>(dir[0], dir[1], dir[2], basis);
-                        float raw = 0.5f;
 #pragma unroll
-                        for (int k = 0; k < K; ++k) raw += basis[k] * coef[k];
-                        if (raw >= 0.f) {
+                        for (int t = 0; t < kSets; ++t) {
+                            const int set = pass * kSets + t;
+                            const float* cf = (set == 0 ? sh_first : sh_second) + sn * K * 3;
 #pragma unroll
-                            for (int k = 0; k < K; ++k) acc[k] += g * basis[k];
+                            for (int ch = 0; ch < 3; ++ch) {
+                                const float g = gall[set * 3 + ch];
+                                if (g == 0.f) continue;
+                                float raw = 0.5f;
+#pragma unroll
+                                for (int k = 0; k < K; ++k) raw += basis[k] * __ldg(cf + k * 3 + ch);
+                                if (raw >= 0.f) {
+#pragma unroll
+                                    for (int k = 0; k < K; ++k) acc[t][ch][k] += g * basis[k];
+                                }
+                            }
                         }
                     }
-                    float* gco = (set == 0 ? g_sh1 : g_sh2) + sn * K * 3;
 #pragma unroll
-                    for (int k = 0; k < K; ++k) gco[k * 3 + ch] = acc[k];
+                    for (int t = 0; t < kSets; ++t) {
+                        const int set = pass * kSets + t;
+                        float* gco = (set == 0 ? g_sh1 : g_sh2) + sn * K * 3;
+#pragma unroll
+                        for (int ch = 0; ch < 3; ++ch)
+#pragma unroll
+                            for (int k = 0; k < K; ++k) gco[k * 3 + ch] = acc[t][ch][k];
+                    }
                 }
             }
         }
