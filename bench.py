@@ -148,6 +148,8 @@ class Job:
                                 for c in self.calls) * full.width * full.height
         self.pixel_count = args.pixels
         self.pixels = None
+        self.timing = False          # collect the camera-split all-reduce's CUDA events
+        self.allreduce_events = []
         if args.pixels:   # selected-pixel mode: the metric counts selected pixels
             scale = args.pixels / (full.width * full.height)
             self.total_pixels = round(self.total_pixels * scale)
@@ -282,9 +284,14 @@ def step(fn, job, calls, optimizer=None):
         loss.backward()
         total = loss.detach() if total is None else total + loss.detach()
     if job.shard is not None and job.shard.split:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
         for values in calls:
             params = [t for k, t in values.items() if k not in job.sharding.PER_CAMERA]
             job.sharding.allreduce_gradients(params, job.groups[job.shard.group_ranks])
+        t1.record()
+        if job.timing:
+            job.allreduce_events.append((t0, t1))
     if optimizer is not None:
         optimizer()
     return total
@@ -310,7 +317,33 @@ def peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def roofline(stage_ms, counts, w, steps, calls_per_step):
+def fp32_peak(device):
+    """FP32 multiply-add throughput of this GPU (TFLOP/s), measured with gs_fp32_probe:
+    148 x 8 blocks of 256 threads, eight independent FFMA chains each, best of three
+    launches of ~6 ms (CUDA events); also the paired FFMA2 form."""
+    from diff_gabor_splatting_b200 import _native as nat
+
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    blocks, iterations = sms * 8, 100_000
+    out = torch.zeros(blocks, device=device)
+    result = {}
+    for paired in (0, 1):
+        flops = blocks * 256 * iterations * 8 * (4 if paired else 2)
+        best = 0.0
+        for i in range(4):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            nat.call("gs_fp32_probe", blocks, iterations, paired, nat.ptr(out),
+                     nat.stream_of(device))
+            b.record()
+            torch.cuda.synchronize()
+            if i:   # the first launch warms up
+                best = max(best, flops / (a.elapsed_time(b) * 1e-3) / 1e12)
+        result["ffma2_tflops" if paired else "ffma_tflops"] = best
+    return result
+
+
+def roofline(stage_ms, counts, w, steps, calls_per_step, fp32=None):
     """Roofline of the dominant stage (largest total device time in the timed region).
 
     achieved = algorithmic work of every launch of that stage in the timed region
@@ -323,22 +356,28 @@ def roofline(stage_ms, counts, w, steps, calls_per_step):
     model = perfmodel.stage_model(name, counts, w)
     work = model["work"] * calls_per_step * steps
     data, source = peaks()
-    dram = perfmodel.traffic(name, counts)
+    dram = perfmodel.traffic(name, counts, w.config)
     out = {"kernel": name, "launches": launches, "ms_per_launch": total_ms / max(launches, 1),
            "bound": model["bound"], "unit": model["unit"],
            "traffic": dram * calls_per_step * steps / max(launches, 1) if dram else None}
     if dram:
-        out["traffic_basis"] = ("DRAM read+write bytes of one ncu-profiled small-case launch, "
-                                "scaled by accepted samples")
+        out["traffic_basis"] = ("DRAM read+write bytes of one ncu-profiled small-case launch of "
+                                "the same config (config 1 otherwise), scaled by accepted samples")
     if model["bound"] == "hbm":
         achieved = work / (total_ms * 1e-3) / 1e9
         peak = data["hbm_gbs"]
         out["peak_source"] = f"hbm_gbs of {source}"
     else:
         achieved = work / (total_ms * 1e-3) / 1e12
-        peak = perfmodel.FP32_NOMINAL_TFLOPS
-        out["peak_source"] = ("nominal FP32 (148 SM x 128 lanes x 2 flop x 1.965 GHz); "
-                              "no measured FP32 peak exists for this pool")
+        if fp32:
+            peak = fp32["ffma_tflops"]
+            out["peak_source"] = ("measured on this GPU by gs_fp32_probe (FFMA chains, "
+                                  f"{fp32['ffma_tflops']:.1f} TFLOP/s; paired FFMA2 "
+                                  f"{fp32['ffma2_tflops']:.1f}); nominal "
+                                  f"{perfmodel.FP32_NOMINAL_TFLOPS:.1f}")
+        else:
+            peak = perfmodel.FP32_NOMINAL_TFLOPS
+            out["peak_source"] = "nominal FP32 (148 SM x 128 lanes x 2 flop x 1.965 GHz)"
     out.update(achieved=achieved, peak=peak, frac=achieved / peak,
                work_per_launch=model["work"] * calls_per_step * steps / max(launches, 1),
                work_basis=model["basis"])
@@ -445,14 +484,27 @@ def main():
     with ClockSampler(local) as clocks, nat.StageTimer() as timer:
         if opt is not None:
             opt.timing = True
+        job.timing = True
         start.record()
         for _ in range(args.steps):
             step(fn, job, calls, opt)
         end.record()
         torch.cuda.synchronize()
+        job.timing = False
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end), world, device)
     stage = timer.totals()
+    allreduce = None
+    if job.allreduce_events:
+        ar_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in job.allreduce_events)
+                               / len(job.allreduce_events), world, device)
+        bucket = sum(t.numel() * 4 for c in calls for k, t in c.items()
+                     if k not in job.sharding.PER_CAMERA)
+        group = len(job.shard.group_ranks)
+        allreduce = {"ms_per_step": ar_ms, "bucket_bytes": bucket, "group_ranks": group,
+                     "bus_gbs": bucket * 2 * (group - 1) / group / (ar_ms * 1e-3) / 1e9,
+                     "timing": "CUDA events around the NCCL all-reduce of each step, mean over "
+                               "the timed steps, max over ranks"}
     launches = sum(OWN_KERNELS.get(name, 1) * n for name, (n, _) in stage.items()
                    if name in OWN_KERNELS)
     pixels_all = job.total_pixels
@@ -508,6 +560,7 @@ def main():
     if not args.no_square and opt is None:
         square = square_leg(args, job, fn, calls, device, world, pixels_all)
     graph = graph_leg(args, job, fn, calls, device, world, pixels_all) if args.graph else None
+    fp32 = fp32_peak(device) if rank == 0 else None
     ref_cuda = None
     if rank == 0 and world == 1 and not args.no_reference_cuda and not args.pixels:
         ref_cuda = reference_cuda(args)
@@ -525,13 +578,15 @@ def main():
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config shapes)",
                 "config": config_desc(w, parallelism(job, world)),
                 "gpu_launches": launches,
-                "roofline": roofline(stage, counts, w, args.steps, len(job.calls)),
+                "roofline": roofline(stage, counts, w, args.steps, len(job.calls), fp32),
                 "stages_ms_per_step": {k: v[1] / args.steps for k, v in stage.items()},
                 "work": counts, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks.summary()}
         if args.pixels:
             line["config"]["selected_pixels_per_camera"] = args.pixels
             line["config"]["pixels_per_step"] = pixels_all
             line["roofline"]["note"] = "kernel work counted on a full render of the workload"
+        if allreduce is not None:
+            line["allreduce"] = allreduce
         if square is not None:
             line["square_bins"] = square
         if ref_cuda is not None:

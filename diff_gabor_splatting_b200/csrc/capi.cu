@@ -78,6 +78,38 @@ __global__ void pair_ids_kernel(int64_t count, const int64_t* __restrict__ pairs
     if (camera_ids) camera_ids[i] = image - s * C;
     if (primitive_ids) primitive_ids[i] = n;
 }
+// FP32 throughput probe: every thread runs eight independent multiply-add chains (or
+// eight float2 chains issued as paired FFMA2), so the FMA pipes, not latency, bound it.
+template <bool Paired>
+__global__ __launch_bounds__(256) void fp32_probe_kernel(int iterations, float seed,
+                                                         float* __restrict__ out) {
+    constexpr int kChains = 8;
+    const float b = 0.999f, c = 1e-3f * seed;
+    float result = 0.f;
+    if constexpr (Paired) {
+        float2 acc[kChains];
+#pragma unroll
+        for (int k = 0; k < kChains; ++k) acc[k] = make_float2(threadIdx.x + k, blockIdx.x - k);
+        const float2 b2 = make_float2(b, b), c2 = make_float2(c, c);
+        for (int i = 0; i < iterations; ++i) {
+#pragma unroll
+            for (int k = 0; k < kChains; ++k) acc[k] = __ffma2_rn(acc[k], b2, c2);
+        }
+#pragma unroll
+        for (int k = 0; k < kChains; ++k) result += acc[k].x + acc[k].y;
+    } else {
+        float acc[kChains];
+#pragma unroll
+        for (int k = 0; k < kChains; ++k) acc[k] = float(threadIdx.x + k);
+        for (int i = 0; i < iterations; ++i) {
+#pragma unroll
+            for (int k = 0; k < kChains; ++k) acc[k] = fmaf(acc[k], b, c);
+        }
+#pragma unroll
+        for (int k = 0; k < kChains; ++k) result += acc[k];
+    }
+    if (result == 12345.f) out[blockIdx.x] = result;   // keeps the chains live
+}
 }  // namespace
 
 void set_error(const std::string& message) { g_last_error = message; }
@@ -153,5 +185,17 @@ extern "C" int gs_pair_ids(const int64_t* pairs, int64_t count, int64_t cameras,
     pair_ids_kernel<<<blocks_for(count), kPackThreads, 0, as_stream(stream)>>>(
         count, pairs, cameras, surfels, narrow, scene_ids, camera_ids, primitive_ids);
     GS_CHECK_LAUNCH("pair_ids_kernel");
+    return GS_OK;
+}
+
+extern "C" int gs_fp32_probe(int blocks, int iterations, int paired, float* out, void* stream) {
+    if (blocks < 1 || iterations < 1 || !out)
+        return fail(GS_ERR_ARGUMENT, "gs_fp32_probe: invalid arguments");
+    auto s = as_stream(stream);
+    if (paired)
+        fp32_probe_kernel<true><<<unsigned(blocks), 256, 0, s>>>(iterations, 1.f, out);
+    else
+        fp32_probe_kernel<false><<<unsigned(blocks), 256, 0, s>>>(iterations, 1.f, out);
+    GS_CHECK_LAUNCH("fp32_probe_kernel");
     return GS_OK;
 }

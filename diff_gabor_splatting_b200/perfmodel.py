@@ -1,51 +1,56 @@
 """Algorithmic work per stage, for roofline fractions.
 
 Memory-bound stages are charged the bytes they must move (HBM roofline).  The
-compositor is charged floating-point work (FP32 roofline): per event constants
-counted from the kernel source (an FMA counts 2; expf/sinf/cosf and a divide count
-1 each), times event counts measured by the kernels' own counters.
+compositors are charged floating-point work (FP32 roofline): per-event constants times
+event counts measured by the kernels' own counters (tests: (pixel, record) samples
+tested; accepts: samples blended forward / differentiated backward).
 
-Events (per pixel and record):
-  test    ray/splat intersection + filtered opacity (sample_surface)        40 flop
-  accept  classic forward blend incl. 4-frequency appearance               100 flop
-          neural forward blend incl. the 5->6->3 SIREN                     156 flop
-  backward per tested sample                                                40 flop
-  backward per accepted sample: classic 400 flop, neural 448 flop
-          (forward replay + appearance and geometry adjoints; the neural weights of
-          the direction inputs and the direction gradient are formed once per (tile,
-          record) from the b1 sums, not per sample: 36 fused multiply-adds fewer)
+The constants are executed FP32 flops per event (2 x FFMA + FADD + FMUL thread
+instructions with the predicate on, ncu), fitted over two classic workloads whose
+test/accept ratios differ (config 1 with 100k surfels and one camera: 1.45 tests per
+accept; config 3 with two scenes: 2.84), which both fit exactly; the neural accept cost
+follows from a neural workload (config 2, 50k surfels) given the classic test cost.
+They include the backward's reduction adds (the per-warp transpose sums its lanes'
+fields), which an accept pays in proportion to its warp's accepting lanes.
+
+  forward:  33 flop per test + 141 (classic) / 220 (neural) per accept
+  backward: 45 flop per test + 325 (classic) / 523 (neural) per accept
 """
 
 from __future__ import annotations
 
 import torch
 
-FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # 74.4, nominal (no measured figure)
+FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # 74.4 nominal; bench.py measures it
 
-TEST_FLOP = 40
-ACCEPT_FLOP = {"classic": 100, "neural": 156}
-BACKWARD_ACCEPT_FLOP = {"classic": 400, "neural": 448}
+TEST_FLOP = {"forward": 33, "backward": 45}
+ACCEPT_FLOP = {"classic": 141, "neural": 220}
+BACKWARD_ACCEPT_FLOP = {"classic": 325, "neural": 523}
 
 
-# DRAM bytes (read + write) of one launch measured with ncu on the config-1 small case
-# (N=100k surfels, 1 camera, ncu --set full) and the accepted
-# samples of that launch.  A full-size launch is estimated by scaling with its own
-# accepted samples (the compositors' DRAM traffic is the record batches, gradient
-# atomics and pixel buffers, all of which grow with the accepted work).
+# DRAM bytes (read + write) of one launch measured with ncu on small cases of two
+# workloads -- config 1 (N=100k surfels, 1 camera) and config 3 (2 of its 32 scenes) --
+# with the accepted samples of that launch.  A full-size launch is estimated by scaling
+# the matching workload's bytes with its own accepted samples (the compositors' DRAM
+# traffic is the record batches, gradient atomics and pixel buffers, all of which grow
+# with the accepted work); other workloads use the config-1 figures.
 PROFILED_TRAFFIC = {
-    "gs_composite_forward": (16.224256e6 + 52.915456e6, 130426868),
-    "gs_composite_backward": (88.160768e6 + 4.975616e6, 130426868),
+    1: {"gs_composite_forward": (16.224256e6 + 52.915456e6, 130426868),
+        "gs_composite_backward": (88.160768e6 + 4.975616e6, 130426868)},
+    3: {"gs_composite_forward": (87.757056e6 + 26.615808e6, 74378371),
+        "gs_composite_backward": (148.364288e6 + 18.006272e6, 74378371)},
 }
 
 
-def traffic(name: str, counts: dict):
+def traffic(name: str, counts: dict, config: int = 1):
     """Estimated DRAM bytes per launch of ``name`` (None when not profiled)."""
     name = name.removesuffix("_split")
-    if name not in PROFILED_TRAFFIC:
+    table = PROFILED_TRAFFIC.get(config, PROFILED_TRAFFIC[1])
+    if name not in table:
         return None
     stage = "forward" if name.endswith("forward") else "backward"
     accepts = counts.get(f"{stage}_accepts", 0)
-    bytes_small, accepts_small = PROFILED_TRAFFIC[name]
+    bytes_small, accepts_small = table[name]
     return bytes_small * accepts / accepts_small
 
 
@@ -83,17 +88,19 @@ def stage_model(name: str, counts: dict, w) -> dict:
     K = 0 if w.sh_degree is None else (w.sh_degree + 1) ** 2
     pixels = w.pixels
     if name == "gs_composite_forward":
-        flop = TEST_FLOP * counts.get("forward_tests", 0) + \
+        flop = TEST_FLOP["forward"] * counts.get("forward_tests", 0) + \
             ACCEPT_FLOP[w.method] * counts.get("forward_accepts", 0)
         return dict(bound="fp32", unit="TFLOP/s", work=flop,
-                    basis=f"{TEST_FLOP} flop/test x tests + {ACCEPT_FLOP[w.method]} flop/accept"
-                          " x accepts (kernel counters)")
+                    basis=f"{TEST_FLOP['forward']} flop/test x tests + {ACCEPT_FLOP[w.method]} "
+                          "flop/accept x accepts (kernel counters; constants = executed FP32 "
+                          "flops per event, ncu-fitted)")
     if name == "gs_composite_backward":
-        flop = TEST_FLOP * counts.get("backward_tests", 0) + \
+        flop = TEST_FLOP["backward"] * counts.get("backward_tests", 0) + \
             BACKWARD_ACCEPT_FLOP[w.method] * counts.get("backward_accepts", 0)
         return dict(bound="fp32", unit="TFLOP/s", work=flop,
-                    basis=f"{TEST_FLOP} flop/test x tests + {BACKWARD_ACCEPT_FLOP[w.method]} "
-                          "flop/accept x accepts (kernel counters)")
+                    basis=f"{TEST_FLOP['backward']} flop/test x tests + "
+                          f"{BACKWARD_ACCEPT_FLOP[w.method]} flop/accept x accepts (kernel "
+                          "counters; constants = executed FP32 flops per event, ncu-fitted)")
     if name == "gs_bin_sort":
         # per record: the span writer reads the fields its region uses (T, xy, opacity:
         # 48 B), radius, depth order and span offset (16 B); per row span: 12 B written

@@ -340,6 +340,14 @@ int gs_unpack_rows(const float* rows, int64_t rows_count, int width, float* appe
 int gs_pair_ids(const int64_t* pairs, int64_t count, int64_t cameras, int64_t surfels,
                 int64_t* scene_ids, int64_t* camera_ids, int64_t* primitive_ids, void* stream);
 
+/* Measurement: FP32 multiply-add throughput of this GPU, the denominator of the
+ * compositors' FP32 roofline (no counterpart in the reference).  blocks x 256 threads
+ * each run `iterations` steps of eight independent fused multiply-add chains (2 flops
+ * each; paired != 0: eight float2 chains as FFMA2, 4 flops each).  `out` (device, one
+ * float per block) is written only on an impossible value; time the launch with
+ * events on `stream`. */
+int gs_fp32_probe(int blocks, int iterations, int paired, float* out, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Spherical-harmonic colours (spherical_harmonics.cu:45-150) for the
  * SHColors entry points.  first/second [B][N][K][3], directions [B][C][N][3],
