@@ -450,14 +450,11 @@ def test_backward_flush_with_unaligned_gradient_buffers(method):
         torch.testing.assert_close(u, a, rtol=1e-5, atol=1e-6 * float(a.abs().max()), msg=name)
 
 
-@pytest.mark.parametrize("method", ["classic", "neural"])
-def test_tight_bins_render_identically_on_adversarial_surfels(method, monkeypatch):
-    """Tight binning's rows are evaluated in single precision with a derived error margin:
-    on surfels chosen to stress it -- needle-thin (1000:1), within half a degree of
-    edge-on, large enough to cover much of the image, just past the near plane, and
-    with opacities just above 1/255 -- every map is bit-identical to the square bins'."""
+def adversarial_scene(method, Wa=256, Ha=192):
+    """Surfels chosen to stress the conservative regions: needle-thin (1000:1), within
+    half a degree of edge-on, large enough to cover much of the image, just past the near
+    plane, and with opacities just above 1/255 (host tensors)."""
     g = torch.Generator().manual_seed(11)
-    Wa, Ha = 256, 192
     v = random_scene(method, scenes=1, cameras=2, n=2000, width=Wa, height=Ha, focal=220.0,
                      seed=11, device="cpu")
     n = v["means"].shape[1]
@@ -475,6 +472,15 @@ def test_tight_bins_render_identically_on_adversarial_surfels(method, monkeypatc
     means[near, 2] = 0.2 + torch.rand(int(near.sum()), generator=g) * 0.1
     faint = kind == 5
     opac[faint] = 1 / 255 + torch.rand(int(faint.sum()), generator=g) * 0.01
+    return v
+
+
+@pytest.mark.parametrize("method", ["classic", "neural"])
+def test_tight_bins_render_identically_on_adversarial_surfels(method, monkeypatch):
+    """Tight binning's rows are evaluated in single precision with a derived error margin:
+    on the adversarial surfels every map is bit-identical to the square bins'."""
+    Wa, Ha = 256, 192
+    v = adversarial_scene(method, Wa, Ha)
     fn = rasterize_gabors if method == "classic" else rasterize_neural_gabors
     results = {}
     for tight in (False, True):
