@@ -113,6 +113,14 @@ def test_invalid_arguments_fail_before_any_gpu_work():
                                            None, 0, 1, 8, 8, 0, 0.2, 100.0, None, None, None, fake,
                                            None, None) == 1
     assert b"negative stride" in lib.gs_last_error()
+    # metadata ids and the FP32 probe: sizes checked before any GPU work
+    assert lib.gs_pair_ids(None, -1, 2, 3, None, None, None, None) == 1
+    assert lib.gs_pair_ids(None, 4, 0, 3, None, None, None, None) == 1
+    assert b"gs_pair_ids" in lib.gs_last_error()
+    assert lib.gs_pair_ids(None, 0, 2, 3, None, None, None, None) == 0   # nothing to do
+    assert lib.gs_fp32_probe(0, 10, 0, fake, None) == 1
+    assert lib.gs_fp32_probe(1, 10, 0, None, None) == 1
+    assert b"gs_fp32_probe" in lib.gs_last_error()
     # arena binning: capacities checked before any GPU work
     assert lib.gs_bin_arena_workspace(10, 0, 0, 1, 8, 8, ctypes.byref(size)) == 1
     assert lib.gs_bin_arena_workspace(10, 5, 6, 1, 8, 8, ctypes.byref(size)) == 1   # spans > slots
