@@ -62,7 +62,7 @@ OWN_KERNELS = {"gs_project_forward": 1, "gs_project_backward": 1, "gs_bin_count"
                "gs_sh_forward": 1, "gs_sh_backward": 1, "gs_pack_geometry": 1,
                "gs_pack_rows": 1, "gs_unpack_geometry_grads": 1, "gs_unpack_rows": 1,
                "gs_adam_step": 1, "gs_adam_step_capturable": 2, "gs_bin_arena": 6,
-               "gs_pair_ids": 1}
+               "gs_pair_ids": 1, "gs_pack_surfel_rows": 1, "gs_unpack_surfel_rows": 1}
 
 
 def parse():

@@ -57,6 +57,8 @@ SIGNATURES = {
     "gs_unpack_geometry_grads": [_p, _p, _l, _l, _p, _p, _p],
     "gs_unpack_rows": [_p, _l, _i, _p, _p],
     "gs_pair_ids": [_p, _l, _l, _l, _p, _p, _p, _p],
+    "gs_pack_surfel_rows": [_i, _p, _l, _p, _p],
+    "gs_unpack_surfel_rows": [_i, _p, _l, _p, _p],
     "gs_fp32_probe": [_i, _i, _i, _p, _p],
     "gs_sh_forward": [_p, _p, _p, _i, _l, _l, _l, _p, _p],
     "gs_sh_backward": [_p, _p, _p, _p, _i, _l, _l, _l, _p, _p, _p, _p],

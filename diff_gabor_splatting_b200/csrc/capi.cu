@@ -78,6 +78,56 @@ __global__ void pair_ids_kernel(int64_t count, const int64_t* __restrict__ pairs
     if (camera_ids) camera_ids[i] = image - s * C;
     if (primitive_ids) primitive_ids[i] = n;
 }
+// Per-surfel appearance rows from the separate appearance tensors (classic: colour 3,
+// secondary colour 3, weights 4, magnitudes 4, phases 4 -> 20-float rows; neural: W1 30,
+// b1 6, W2 18, b2 3 -> 60-float rows), and the reverse for their gradients.  One thread
+// per row slot; the pad slots are written zero.
+struct SurfelRowTable {
+    const float* in[5];
+    float* out[5];
+    int width[5], first[6], parts, padded;
+};
+
+__global__ void pack_surfel_rows_kernel(int64_t A, SurfelRowTable t, float* __restrict__ rows) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= A * t.padded) return;
+    const int64_t a = i / t.padded;
+    const int k = int(i % t.padded);
+    float v = 0.f;
+#pragma unroll
+    for (int p = 0; p < 5; ++p)
+        if (p < t.parts && k >= t.first[p] && k < t.first[p + 1])
+            v = t.in[p][a * t.width[p] + (k - t.first[p])];
+    rows[i] = v;
+}
+
+__global__ void unpack_surfel_rows_kernel(int64_t A, SurfelRowTable t,
+                                          const float* __restrict__ rows) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int used = t.first[t.parts];
+    if (i >= A * used) return;
+    const int64_t a = i / used;
+    const int k = int(i % used);
+    const float v = rows[a * t.padded + k];
+#pragma unroll
+    for (int p = 0; p < 5; ++p)
+        if (p < t.parts && k >= t.first[p] && k < t.first[p + 1])
+            t.out[p][a * t.width[p] + (k - t.first[p])] = v;
+}
+
+SurfelRowTable surfel_row_table(int neural) {
+    SurfelRowTable t{};
+    static const int classic[5] = {3, 3, 4, 4, 4}, siren[4] = {30, 6, 18, 3};
+    t.parts = neural ? 4 : 5;
+    t.padded = neural ? GS_NEURAL_ROW_FLOATS : GS_CLASSIC_ROW_FLOATS;
+    t.first[0] = 0;
+    for (int p = 0; p < t.parts; ++p) {
+        t.width[p] = neural ? siren[p] : classic[p];
+        t.first[p + 1] = t.first[p] + t.width[p];
+    }
+    return t;
+}
+
 // FP32 throughput probe: every thread runs eight independent multiply-add chains (or
 // eight float2 chains issued as paired FFMA2), so the FMA pipes, not latency, bound it.
 template <bool Paired>
@@ -197,5 +247,37 @@ extern "C" int gs_fp32_probe(int blocks, int iterations, int paired, float* out,
     else
         fp32_probe_kernel<false><<<unsigned(blocks), 256, 0, s>>>(iterations, 1.f, out);
     GS_CHECK_LAUNCH("fp32_probe_kernel");
+    return GS_OK;
+}
+
+extern "C" int gs_pack_surfel_rows(int neural, const float* const* appearance, int64_t count,
+                                   float* rows, void* stream) {
+    if (count < 0 || !appearance || (count > 0 && !rows))
+        return fail(GS_ERR_ARGUMENT, "gs_pack_surfel_rows: invalid arguments");
+    if (count == 0) return GS_OK;
+    SurfelRowTable t = surfel_row_table(neural);
+    for (int p = 0; p < t.parts; ++p) {
+        if (!appearance[p]) return fail(GS_ERR_ARGUMENT, "gs_pack_surfel_rows: NULL input");
+        t.in[p] = appearance[p];
+    }
+    pack_surfel_rows_kernel<<<blocks_for(count * t.padded), kPackThreads, 0, as_stream(stream)>>>(
+        count, t, rows);
+    GS_CHECK_LAUNCH("pack_surfel_rows_kernel");
+    return GS_OK;
+}
+
+extern "C" int gs_unpack_surfel_rows(int neural, const float* rows, int64_t count,
+                                     float* const* grad_appearance, void* stream) {
+    if (count < 0 || !grad_appearance || (count > 0 && !rows))
+        return fail(GS_ERR_ARGUMENT, "gs_unpack_surfel_rows: invalid arguments");
+    if (count == 0) return GS_OK;
+    SurfelRowTable t = surfel_row_table(neural);
+    for (int p = 0; p < t.parts; ++p) {
+        if (!grad_appearance[p]) return fail(GS_ERR_ARGUMENT, "gs_unpack_surfel_rows: NULL output");
+        t.out[p] = grad_appearance[p];
+    }
+    unpack_surfel_rows_kernel<<<blocks_for(count * t.first[t.parts]), kPackThreads, 0,
+                                as_stream(stream)>>>(count, t, rows);
+    GS_CHECK_LAUNCH("unpack_surfel_rows_kernel");
     return GS_OK;
 }

@@ -23,7 +23,7 @@ from torch.autograd.function import once_differentiable
 
 from . import _native as nat
 from . import rendering
-from .rendering import Chunk, Composite, bin_records, check_tensor, check_values
+from .rendering import Chunk, Composite, SurfelRows, bin_records, check_tensor, check_values
 
 
 class RaggedProjection(torch.autograd.Function):
@@ -168,10 +168,8 @@ def _render_ragged(means, quaternions, scales, opacities, appearance, view_matri
         if sh:
             rows, row_mode, row_ids = sh_rows, nat.ROWS_PER_RECORD, None
         else:
-            widths = [30, 6, 18, 3] if neural else [3, 3, 4, 4, 4]
-            pad = (nat.NEURAL_ROW_FLOATS if neural else nat.CLASSIC_ROW_FLOATS) - sum(widths)
-            rows = torch.cat([t.reshape(total, k) for t, k in zip(appearance, widths)]
-                             + [means.new_zeros((total, pad))], -1)
+            rows = SurfelRows.apply(neural, *(t.reshape(total, k) for t, k in
+                                              zip(appearance, SurfelRows.widths(neural))))
             row_mode, row_ids = nat.ROWS_EXPLICIT, (offsets[scene] + primitive).contiguous()
         chunk = Chunk(0, images, 0, True)
         chunk.record0, chunk.record_count = 0, P

@@ -142,6 +142,43 @@ class PackedRows(torch.autograd.Function):
         return out.index_copy_(0, selected, grad.contiguous()), None
 
 
+class SurfelRows(torch.autograd.Function):
+    """Per-surfel appearance rows of the renderers without SH: the reference concatenates
+    the appearance tensors (rendering.py:347-356); here one kernel packs them into the
+    library's padded 20- / 60-float rows (``gs_pack_surfel_rows``) and one kernel writes
+    the rows' gradients back as contiguous per-tensor gradients
+    (``gs_unpack_surfel_rows``).  Inputs are contiguous [A, k] views.
+    """
+
+    @staticmethod
+    def widths(neural):
+        """Floats per surfel of each appearance tensor, in row order."""
+        return (30, 6, 18, 3) if neural else (3, 3, 4, 4, 4)
+
+    @staticmethod
+    def forward(ctx, neural, *appearance):
+        device = appearance[0].device
+        count = appearance[0].shape[0]
+        width = nat.NEURAL_ROW_FLOATS if neural else nat.CLASSIC_ROW_FLOATS
+        rows = torch.empty((count, width), device=device, dtype=torch.float32)
+        inputs, inputs_ptr = nat.host_array(ctypes.c_void_p, [t.data_ptr() for t in appearance])
+        nat.call("gs_pack_surfel_rows", int(neural), inputs_ptr, count, nat.ptr(rows),
+                 nat.stream_of(device))
+        ctx.neural = neural
+        ctx.shapes = [t.shape for t in appearance]
+        return rows
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, grad_rows):
+        grad_rows = grad_rows.contiguous()
+        grads = [grad_rows.new_empty(shape) for shape in ctx.shapes]
+        outs, outs_ptr = nat.host_array(ctypes.c_void_p, [g.data_ptr() for g in grads])
+        nat.call("gs_unpack_surfel_rows", int(ctx.neural), nat.ptr(grad_rows), grad_rows.shape[0],
+                 outs_ptr, nat.stream_of(grad_rows.device))
+        return (None, *grads)
+
+
 # channels of the five map planes the compositor writes: rgb, alpha, accumulated depth,
 # normals, distortion (together the reference's [..][9] maps, in that order)
 PLANES = (3, 1, 1, 3, 1)
@@ -794,10 +831,8 @@ def _render(means, quaternions, scales, opacities, appearance, view_matrices, in
     if sh:
         rows, row_mode = sh_rows, nat.ROWS_PER_RECORD
     else:
-        widths = [30, 6, 18, 3] if neural else [3, 3, 4, 4, 4]
-        pad = (nat.NEURAL_ROW_FLOATS if neural else nat.CLASSIC_ROW_FLOATS) - sum(widths)
-        rows = torch.cat([t.reshape(S * N, k) for t, k in zip(appearance, widths)]
-                         + [means.new_zeros((S * N, pad))], -1)
+        rows = SurfelRows.apply(neural, *(t.reshape(S * N, k) for t, k in
+                                          zip(appearance, SurfelRows.widths(neural))))
         row_mode = nat.ROWS_PER_SURFEL
     images = S * C
     visible_count = None

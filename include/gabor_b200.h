@@ -332,6 +332,18 @@ int gs_unpack_geometry_grads(const float* grad_records, const int64_t* primitive
 int gs_unpack_rows(const float* rows, int64_t rows_count, int width, float* appearance,
                    void* stream);
 
+/* Per-surfel appearance rows of the renderers without SH (the reference concatenates the
+ * appearance tensors, rendering.py:347-356): `appearance` is a host array of device
+ * pointers -- classic (neural == 0): colors [A][3], secondary_colors [A][3],
+ * frequency_weights, frequency_magnitudes, phases [A][4]; neural: input_weights [A][30],
+ * input_biases [A][6], output_weights [A][18], output_biases [A][3] -- packed into
+ * rows[A][20] (classic) or rows[A][60] (neural), pad slots zero.  The unpack form
+ * writes each row's fields back to the separate tensors (their gradients). */
+int gs_pack_surfel_rows(int neural, const float* const* appearance, int64_t count, float* rows,
+                        void* stream);
+int gs_unpack_surfel_rows(int neural, const float* rows, int64_t count,
+                          float* const* grad_appearance, void* stream);
+
 /* Metadata ids of reported pairs (rendering.py:389-399: scene_ids, camera_ids,
  * primitive_ids = pair // (C N), pair // N % C, pair % N) in one pass: for i < count the
  * pair p = pairs[i] (pairs NULL: p = i) of the dense (scene, camera, surfel) layout
