@@ -232,12 +232,12 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
         mv = reinterpret_cast<const float4*>(fmags)[sn];
         pv = reinterpret_cast<const float4*>(fphases)[sn];
     }
-    // Appearance rows with SH colours: for degrees 0-1 (at most 24 coefficients) both
-    // colours are evaluated inside the camera loop and each 80-byte row is written at
-    // once (five 16-byte stores, no partially written sectors); for degrees 2-3 the
-    // coefficient sets are too large to re-read per camera, so the camera loop writes
-    // the wave parameters and a second pass per coefficient set adds the colours.
-    constexpr bool kWholeRows = Degree >= 0 && Degree <= 1;
+    // Appearance rows with SH colours: both colours are evaluated inside the camera loop
+    // and each 80-byte row is written at once (five 16-byte stores, no partially written
+    // sectors).  The coefficient sets are re-read per camera from L1/L2; writing a row's
+    // colours in later passes instead left its first sector partly written, which with
+    // many cameras per surfel (16 on config 4: 2.5 GB of rows) reached DRAM as partial
+    // writes (projection forward 4.0 -> 2.7 ms there, config 1 unchanged).
     for (int64_t c = 0; c < C; ++c) {
         Camera cam;
         load_camera(cam, views, intr, s * C + c);
@@ -254,9 +254,9 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
         radii[pid] = pair_radius(p, tw, th, near_plane, far_plane);
         if constexpr (Degree >= 0) {
             float4* row = app_rows + pid * (GS_CLASSIC_ROW_FLOATS / 4);
-            if constexpr (kWholeRows) {
+            {
                 // both clamped SH colours of the pair's view direction (the direction
-                // spherical_harmonics.cu evaluates), coefficients re-read from L1
+                // spherical_harmonics.cu evaluates)
                 float basis[K], col[6];
                 sh_basis<Degree>(p.dir[0], p.dir[1], p.dir[2], basis);
 #pragma unroll
@@ -264,15 +264,18 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
                     const float4* src = reinterpret_cast<const float4*>(
                         (set == 0 ? sh_first : sh_second) + sn * K * 3);
                     float coef[K * 3];
+                    if constexpr ((K * 3) % 4 == 0) {
+                        // 12 or 48 floats per set: every set starts 16-byte aligned
 #pragma unroll
-                    for (int i = 0; i < K * 3 / 4; ++i) {   // K * 3 = 3 or 12 floats
-                        const float4 q = __ldg(src + i);
-                        coef[4 * i] = q.x; coef[4 * i + 1] = q.y;
-                        coef[4 * i + 2] = q.z; coef[4 * i + 3] = q.w;
-                    }
-                    if constexpr ((K * 3) % 4 != 0) {
+                        for (int i = 0; i < K * 3 / 4; ++i) {
+                            const float4 q = __ldg(src + i);
+                            coef[4 * i] = q.x; coef[4 * i + 1] = q.y;
+                            coef[4 * i + 2] = q.z; coef[4 * i + 3] = q.w;
+                        }
+                    } else {
+                        // 3 or 27 floats per set: sets start 4-byte aligned only
 #pragma unroll
-                        for (int i = (K * 3 / 4) * 4; i < K * 3; ++i)
+                        for (int i = 0; i < K * 3; ++i)
                             coef[i] = __ldg(reinterpret_cast<const float*>(src) + i);
                     }
 #pragma unroll
@@ -285,50 +288,10 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
                 }
                 row[0] = make_float4(col[0], col[1], col[2], col[3]);
                 row[1] = make_float4(col[4], col[5], wv.x, wv.y);
-            } else {
-                reinterpret_cast<float2*>(row + 1)[1] = make_float2(wv.x, wv.y);
             }
             row[2] = make_float4(wv.z, wv.w, mv.x, mv.y);
             row[3] = make_float4(mv.z, mv.w, pv.x, pv.y);
             row[4] = make_float4(pv.z, pv.w, 0.f, 0.f);
-        }
-    }
-    if constexpr (Degree >= 2) {
-        // Both clamped SH colours, one coefficient set at a time: the set's 3K
-        // coefficients are read once into registers (16-byte loads when the layout
-        // allows), then evaluated for every camera; the direction is recomputed with
-        // the same rounded operations as setup_pair.
-#pragma unroll 1
-        for (int set = 0; set < 2; ++set) {
-            const float* src = (set == 0 ? sh_first : sh_second) + sn * K * 3;
-            float coef[K * 3];
-            if constexpr ((K * 3) % 4 == 0) {
-#pragma unroll
-                for (int i = 0; i < K * 3 / 4; ++i) {
-                    const float4 q = __ldg(reinterpret_cast<const float4*>(src) + i);
-                    coef[4 * i] = q.x; coef[4 * i + 1] = q.y;
-                    coef[4 * i + 2] = q.z; coef[4 * i + 3] = q.w;
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < K * 3; ++i) coef[i] = __ldg(src + i);
-            }
-            for (int64_t c = 0; c < C; ++c) {
-                Camera cam;
-                load_camera(cam, views, intr, s * C + c);
-                float dir[3], basis[K];
-                view_direction(v, cam, dir);
-                sh_basis<Degree>(dir[0], dir[1], dir[2], basis);
-                float* row = reinterpret_cast<float*>(app_rows) +
-                             (C * base + c * N + n) * GS_CLASSIC_ROW_FLOATS + set * 3;
-#pragma unroll
-                for (int ch = 0; ch < 3; ++ch) {
-                    float raw = 0.5f;
-#pragma unroll
-                    for (int k = 0; k < K; ++k) raw += basis[k] * coef[k * 3 + ch];
-                    row[ch] = fmaxf(raw, 0.f);
-                }
-            }
         }
     }
 }
