@@ -505,8 +505,10 @@ def main():
                      "bus_gbs": bucket * 2 * (group - 1) / group / (ar_ms * 1e-3) / 1e9,
                      "timing": "CUDA events around the NCCL all-reduce of each step, mean over "
                                "the timed steps, max over ranks"}
-    launches = sum(OWN_KERNELS.get(name, 1) * n for name, (n, _) in stage.items()
-                   if name in OWN_KERNELS)
+    own = dict(OWN_KERNELS)
+    if w.sh_degree is not None and w.sh_degree >= 2:   # plus its SH coefficient kernel
+        own["gs_project_backward"] = 2
+    launches = sum(own.get(name, 1) * n for name, (n, _) in stage.items() if name in own)
     pixels_all = job.total_pixels
     value = pixels_all * args.steps / (ms * 1e-3) / 1e6
     # end to end: every step's inputs copied from pinned host memory and its loss read

@@ -499,15 +499,15 @@ __global__ __launch_bounds__(kProjThreads, 2) void project_backward_kernel(
                 }
             }
         }
-        if constexpr (Degree >= 0) {
+        if constexpr (Degree >= 0 && Degree <= 1) {
             if (live) {
-                // SH coefficient gradients: sum over the scene's cameras of g * basis(dir)
-                // where the clamp passes, per (colour set, channel).  The camera loop is
-                // outermost, so each camera's direction and basis are evaluated once per
-                // pass and its six colour gradients read with two vector loads; degrees
-                // 0-1 take both sets in one pass (6K accumulators), degrees 2-3 one set
-                // per pass (3K).  Per accumulator the cameras add in order, as before.
-                constexpr int kSets = Degree <= 1 ? 2 : 1;
+                // SH coefficient gradients, degrees 0-1 (degrees 2-3:
+                // sh_coefficient_grad_kernel): the sum over the scene's cameras of
+                // g * basis(dir) where the clamp passes, per (colour set, channel), both
+                // sets in one pass after the camera loop (6K accumulators), each camera's
+                // direction and basis evaluated once and its six colour gradients read with
+                // two vector loads.  Per accumulator the cameras add in order.
+                constexpr int kSets = 2;
 #pragma unroll 1
                 for (int pass = 0; pass < 2 / kSets; ++pass) {
                     float acc[kSets][3][K];
@@ -612,6 +612,66 @@ __global__ __launch_bounds__(kProjThreads, 2) void project_backward_kernel(
     }
 }
 
+// SH coefficient gradients of degrees 2-3 (spherical_harmonics.cu:128-150 under the
+// clamp of its forward, :80-85): per (surfel, colour set, channel), the sum over the
+// scene's cameras, in camera order, of g * basis(dir) for the cameras whose unclamped
+// colour is >= 0.  Eight lanes per surfel, six of them busy: each holds its channel's K
+// coefficients and K accumulators, reads its one colour gradient per camera (a surfel's
+// six lanes read the first 24 bytes of the pair's gradient row together) and recomputes
+// the pair's direction and basis.  Inside project_backward_kernel the 6K accumulators
+// of these degrees did not fit, and one pass per colour set after the camera loop
+// re-read every pair's gradient row from DRAM (config 4: 3.19 -> 2.71 ms, config 1
+// 0.46 -> 0.33 ms).  Every coefficient gradient of the launch is written.
+constexpr int kShLanes = 8;
+
+template <int Degree>
+__global__ __launch_bounds__(kProjThreads) void sh_coefficient_grad_kernel(
+    const float* __restrict__ means, const float* __restrict__ views,
+    const float* __restrict__ intr, const float* __restrict__ sh_first,
+    const float* __restrict__ sh_second, int64_t C, int64_t N,
+    const int64_t* __restrict__ offsets, const float* __restrict__ grad_rows,
+    float* __restrict__ g_sh1, float* __restrict__ g_sh2) {
+    constexpr int K = (Degree + 1) * (Degree + 1);
+    const int64_t s = blockIdx.y;
+    const int64_t base = offsets ? offsets[s] : s * N;   // ragged batches as in the forward
+    if (offsets) N = offsets[s + 1] - base;
+    const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t n = t / kShLanes;
+    const int sub = int(t % kShLanes);   // colour set sub / 3, channel sub % 3
+    if (n >= N || sub >= 6) return;
+    const int64_t sn = base + n;
+    Surfel v;   // view_direction reads the mean only
+#pragma unroll
+    for (int i = 0; i < 3; ++i) v.mean[i] = means[sn * 3 + i];
+    const int64_t at = sn * K * 3 + sub % 3;
+    const float* cf = (sub < 3 ? sh_first : sh_second) + at;
+    float coef[K], acc[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        coef[k] = __ldg(cf + k * 3);
+        acc[k] = 0.f;
+    }
+    for (int64_t c = 0; c < C; ++c) {
+        const float g = grad_rows[(C * base + c * N + n) * GS_CLASSIC_ROW_FLOATS + sub];
+        if (g == 0.f) continue;
+        Camera cam;
+        load_camera(cam, views, intr, s * C + c);
+        float dir[3], basis[K];
+        view_direction(v, cam, dir);
+        sh_basis<Degree>(dir[0], dir[1], dir[2], basis);
+        float raw = 0.5f;
+#pragma unroll
+        for (int k = 0; k < K; ++k) raw += basis[k] * coef[k];
+        if (raw >= 0.f) {
+#pragma unroll
+            for (int k = 0; k < K; ++k) acc[k] += g * basis[k];
+        }
+    }
+    float* out = (sub < 3 ? g_sh1 : g_sh2) + at;
+#pragma unroll
+    for (int k = 0; k < K; ++k) out[k * 3] = acc[k];
+}
+
 }  // namespace
 }  // namespace gs
 
@@ -713,8 +773,8 @@ static int project_backward_impl(const char* fn, const int64_t* offsets, int64_t
     auto s = as_stream(stream);
     GS_CUDA(cudaMemsetAsync(grad_view_matrices, 0, sizeof(float) * 16 * scenes * cameras, s));
     GS_CUDA(cudaMemsetAsync(grad_intrinsics, 0, sizeof(float) * 9 * scenes * cameras, s));
-    const int64_t sn = offsets ? total_surfels : scenes * surfels;
-    if (sh_degree >= 0) {
+    if (sh_degree >= 0 && sh_degree <= 1) {   // degrees 2-3: every one written below
+        const int64_t sn = offsets ? total_surfels : scenes * surfels;
         const int64_t K = int64_t(sh_degree + 1) * (sh_degree + 1);
         GS_CUDA(cudaMemsetAsync(grad_sh_first, 0, sizeof(float) * sn * K * 3, s));
         GS_CUDA(cudaMemsetAsync(grad_sh_second, 0, sizeof(float) * sn * K * 3, s));
@@ -745,6 +805,18 @@ static int project_backward_impl(const char* fn, const int64_t* offsets, int64_t
     }
 #undef GS_PROJ_BWD
     GS_CHECK_LAUNCH("project_backward_kernel");
+    if (sh_degree >= 2) {
+        const dim3 sh_grid{unsigned((surfels * kShLanes + kProjThreads - 1) / kProjThreads),
+                           unsigned(scenes)};
+#define GS_SH_GRAD(D)                                                                           \
+    sh_coefficient_grad_kernel<D><<<sh_grid, kProjThreads, 0, s>>>(                              \
+        means, view_matrices, intrinsics, sh_first, sh_second, cameras, surfels, offsets,      \
+        grad_app_rows, grad_sh_first, grad_sh_second)
+        if (sh_degree == 2) GS_SH_GRAD(2);
+        else GS_SH_GRAD(3);
+#undef GS_SH_GRAD
+        GS_CHECK_LAUNCH("sh_coefficient_grad_kernel");
+    }
     return GS_OK;
 }
 
