@@ -347,7 +347,16 @@ __global__ __launch_bounds__(kProjThreads, 2) void project_backward_kernel(
                 float2 t = reinterpret_cast<const float2*>(grad_xy)[pid];
                 gxy[0] = t.x; gxy[1] = t.y;
                 if constexpr (Degree >= 0) {
-                    const float* row = grad_rows + pid * GS_CLASSIC_ROW_FLOATS;
+                    // the row's 18 gradients as five 16-byte loads (rows are 80 bytes)
+                    const float4* row4 = reinterpret_cast<const float4*>(grad_rows) +
+                                         pid * (GS_CLASSIC_ROW_FLOATS / 4);
+                    float row[20];
+#pragma unroll
+                    for (int i = 0; i < 5; ++i) {
+                        const float4 q = row4[i];
+                        row[4 * i] = q.x; row[4 * i + 1] = q.y;
+                        row[4 * i + 2] = q.z; row[4 * i + 3] = q.w;
+                    }
 #pragma unroll
                     for (int i = 0; i < 6; ++i) gcol[i] = row[i];
 #pragma unroll
@@ -677,6 +686,13 @@ __global__ __launch_bounds__(kProjThreads) void sh_coefficient_grad_kernel(
 
 using namespace gs;
 
+// The kernels move quaternions, records, appearance rows, wave parameters and their
+// gradients as 16-byte vectors and scales and screen centres as 8-byte vectors: their
+// buffers must start on those boundaries (every row then does too).
+static bool misaligned(const void* p, uintptr_t bytes) {
+    return (reinterpret_cast<uintptr_t>(p) & (bytes - 1)) != 0;
+}
+
 static int project_forward_impl(const char* fn, const int64_t* offsets, const float* means,
                                 const float* quaternions, const float* scales,
                                   const float* opacities, const float* view_matrices,
@@ -695,6 +711,14 @@ static int project_forward_impl(const char* fn, const int64_t* offsets, const fl
     if (sh_degree >= 0 && (!sh_first || !sh_second || !frequency_weights || !frequency_magnitudes ||
                            !phases || !app_rows))
         return fail(GS_ERR_ARGUMENT, std::string(fn) + ": SH mode needs coefficient and row buffers");
+    if (misaligned(quaternions, 16) || misaligned(records, 16) || misaligned(scales, 8) ||
+        misaligned(xy, 8) ||
+        (sh_degree >= 0 && (misaligned(frequency_weights, 16) ||
+                            misaligned(frequency_magnitudes, 16) || misaligned(phases, 16) ||
+                            misaligned(app_rows, 16))))
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": quaternions, records, rows and wave "
+                                                       "parameters must be 16-byte aligned, "
+                                                       "scales and xy 8-byte aligned");
     const int tw = (width + kTile - 1) / kTile, th = (height + kTile - 1) / kTile;
     dim3 grid(unsigned((surfels + kProjThreads - 1) / kProjThreads), unsigned(scenes));
     auto s = as_stream(stream);
@@ -770,6 +794,17 @@ static int project_backward_impl(const char* fn, const int64_t* offsets, int64_t
         return fail(GS_ERR_ARGUMENT, std::string(fn) + ": invalid sizes");
     if (sh_degree > 3) return fail(GS_ERR_ARGUMENT, std::string(fn) + ": SH degree must be 0-3");
     if (scenes > 65535) return fail(GS_ERR_LIMIT, std::string(fn) + ": more than 65535 scenes");
+    if (misaligned(quaternions, 16) || misaligned(grad_records, 16) ||
+        misaligned(grad_quaternions, 16) || misaligned(scales, 8) || misaligned(grad_xy, 8) ||
+        misaligned(grad_scales, 8) ||
+        (sh_degree >= 0 && (misaligned(grad_app_rows, 16) ||
+                            misaligned(grad_frequency_weights, 16) ||
+                            misaligned(grad_frequency_magnitudes, 16) ||
+                            misaligned(grad_phases, 16))))
+        return fail(GS_ERR_ARGUMENT, std::string(fn) + ": quaternions, record and row gradients "
+                                                       "and their 4-vector gradients must be "
+                                                       "16-byte aligned, scales and xy 8-byte "
+                                                       "aligned");
     auto s = as_stream(stream);
     GS_CUDA(cudaMemsetAsync(grad_view_matrices, 0, sizeof(float) * 16 * scenes * cameras, s));
     GS_CUDA(cudaMemsetAsync(grad_intrinsics, 0, sizeof(float) * 9 * scenes * cameras, s));

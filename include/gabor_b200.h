@@ -65,6 +65,9 @@ const char* gs_last_error(void);
  *   45-85) and written with the surfel's weights/magnitudes/phases into
  *   app_rows[p] (classic appearance row layout).
  * Outputs: records[P][20], xy[P][2], radii[P] (int32, 0 = culled).
+ * Alignment (GS_ERR_ARGUMENT otherwise): quaternions, records, app_rows and the three
+ * wave-parameter arrays start on 16 bytes, scales and xy on 8 (the kernels move their
+ * rows as vectors).
  */
 int gs_project_forward(const float* means, const float* quaternions, const float* scales,
                        const float* opacities, const float* view_matrices,
@@ -80,7 +83,10 @@ int gs_project_forward(const float* means, const float* quaternions, const float
  * 334-374 and spherical_harmonics.cu:128-150).  grad_records[P][20] (slots 9-10
  * ignored), grad_xy[P][2], grad_app_rows[P][20] (SH mode).  Surfel gradients are
  * summed over cameras in registers; camera gradients are reduced per block and
- * added with atomics.  Every output is overwritten (zeroed first on the stream). */
+ * added with atomics.  Every output is overwritten (zeroed first on the stream).
+ * Alignment as in gs_project_forward, for the inputs and for the matching gradients
+ * (grad_records, grad_app_rows, grad_quaternions and the wave-parameter gradients on 16
+ * bytes, grad_xy and grad_scales on 8). */
 int gs_project_backward(const float* means, const float* quaternions, const float* scales,
                         const float* view_matrices, const float* intrinsics,
                         const float* sh_first, const float* sh_second, int sh_degree,

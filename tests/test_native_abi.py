@@ -69,6 +69,17 @@ def test_invalid_arguments_fail_before_any_gpu_work():
     assert lib.gs_project_forward(*([None] * 11), 4, 1, 1, 1, 8, 8, 0.2, 100.0,
                                   None, None, None, None, None) == 1
     assert b"SH degree" in lib.gs_last_error()
+    # projection buffers moved as vectors must be aligned (checked before any GPU work)
+    a16, a8, odd = ctypes.c_void_p(4096), ctypes.c_void_p(4104), ctypes.c_void_p(4100)
+    assert lib.gs_project_forward(a16, odd, a8, a16, a16, a16, *([None] * 5), -1, 1, 1, 4, 8, 8,
+                                  0.2, 100.0, a16, a8, None, a16, None) == 1
+    assert b"16-byte aligned" in lib.gs_last_error()
+    assert lib.gs_project_forward(a16, a16, odd, a16, a16, a16, *([None] * 5), -1, 1, 1, 4, 8,
+                                  8, 0.2, 100.0, a16, a8, None, a16, None) == 1
+    assert b"8-byte aligned" in lib.gs_last_error()
+    assert lib.gs_project_backward(a16, a16, a8, a16, a16, None, None, -1, 1, 1, 4, a8, a8,
+                                   None, *([a16] * 11), None) == 1
+    assert b"16-byte aligned" in lib.gs_last_error()
     # ragged projection: the per-scene surfel offsets are required
     assert lib.gs_project_forward_ragged(*([None] * 11), 0, 1, 1, None, 1, 8, 8, 0.2, 100.0,
                                          None, None, None, None, None) == 1
