@@ -128,13 +128,34 @@ struct Region {
     float yerr;           // bound on the float error of Y, added to both band edges
 };   // 72 bytes: a warp reading the fields of different records spreads over the banks
 
-__device__ __noinline__ void record_region(const float* g, int radius, int tw, int th,
-                                           bool tight, Region* out) {
+// Reads the record's T (slots 0-8), centre (9-10) and, for tight regions, opacity (17).
+// Records come in depth order, one scattered 80-byte row per lane: rows of at least 20
+// floats on 16-byte boundaries are read with four 16-byte loads (each one L2 sector)
+// instead of twelve 4-byte ones (one sector each, the L1 keeping few of them).
+__device__ __noinline__ void record_region(const float* records, int64_t r, int stride,
+                                           int radius, int tw, int th, bool tight,
+                                           Region* out) {
+    float g[18];
+    const float* row = records + r * stride;
+    const bool vector_rows =
+        stride >= 20 && stride % 4 == 0 && (reinterpret_cast<uintptr_t>(records) & 15u) == 0;
+    if (vector_rows) {
+        const float4* q = reinterpret_cast<const float4*>(row);
+        const float4 a = __ldg(q), b = __ldg(q + 1), c = __ldg(q + 2), d = __ldg(q + 4);
+        g[0] = a.x; g[1] = a.y; g[2] = a.z; g[3] = a.w;
+        g[4] = b.x; g[5] = b.y; g[6] = b.z; g[7] = b.w;
+        g[8] = c.x; g[9] = c.y; g[10] = c.z;
+        g[17] = d.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 11; ++k) g[k] = row[k];
+    }
     Region R;
     R.rect = tile_rect(g[9], g[10], radius, tw, th);
     R.exact = 0;
     const int4 b = R.rect;
     if (!tight || b.z <= b.x || b.w <= b.y) { *out = R; return; }
+    if (!vector_rows) g[17] = row[17];   // the opacity, read only for tight regions
     const double o = g[17];
     if (!(o * 255.0 >= 1.0 - 1e-6)) {   // alpha <= o < 1/255: never accepted
         R.rect = make_int4(b.x, b.y, b.x, b.y);
@@ -247,7 +268,7 @@ __global__ void spans_kernel(int64_t R, const float* __restrict__ records, int s
     int64_t slot = i ? slot_end[i - 1] : 0;
     int64_t k = first_span;
     Region G;
-    record_region(records + int64_t(r) * stride, radii[r], tw, th, tight, &G);
+    record_region(records, r, stride, radii[r], tw, th, tight, &G);
     const int64_t image = image_ids ? image_ids[r] : r / per_image;
     const uint32_t base = uint32_t(image * tw * th);
     for (int ty = G.rect.y; ty < G.rect.w; ++ty) {
@@ -308,7 +329,7 @@ __global__ __launch_bounds__(kBinThreads, 4) void tile_counts_balanced_kernel(
         const int radius = radii[r];
         if (radius > 0) {
             Region& G = sh.region[warp][lane];
-            record_region(records + int64_t(r) * stride, radius, tw, th, tight, &G);
+            record_region(records, r, stride, radius, tw, th, tight, &G);
             if (G.rect.z > G.rect.x) {
                 if (G.exact) {
                     rows = max(G.rect.w - G.rect.y, 0);
@@ -368,7 +389,7 @@ __global__ __launch_bounds__(kBinThreads, 4) void spans_rows_balanced_kernel(
         if (span_end[i] != first_span) {
             const int r = order[i];
             Region& G = sh.region[warp][lane];
-            record_region(records + int64_t(r) * stride, radii[r], tw, th, tight, &G);
+            record_region(records, r, stride, radii[r], tw, th, tight, &G);
             rows = max(G.rect.w - G.rect.y, 0);
             sh.out[warp][lane] = first_span;
             sh.end[warp][lane] = span_end[i];
