@@ -58,7 +58,8 @@ def reference_alone(method, values, kw, weights):
     return maps.detach(), {k: t.grad for k, t in leaves.items()}
 
 
-@pytest.mark.parametrize("method,sh_degree", [("classic", None), ("classic", 2), ("neural", None)])
+@pytest.mark.parametrize("method,sh_degree",
+                         [("classic", None), ("classic", 2), ("classic", 3), ("neural", None)])
 def test_ragged_batch_equals_reference_per_scene(method, sh_degree):
     counts = [150, 0, 400, 275]
     scenes = [ordered(random_scene(method, scenes=1, cameras=2, n=max(n, 1), width=W, height=H,
