@@ -473,7 +473,7 @@ __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Para
 
 // Per-record gradient fields, packed: record slots (T 0-8, xy 9-10, normal 11-13,
 // [dir 14-16 neural]), opacity (record slot 17), then the appearance row.
-template <bool Neural>
+template <bool Neural, bool Normals>
 struct Fields {
     // Packed per-record gradient fields summed over a warp's pixels: record slots 0-13
     // (T, xy, normal), the opacity, then the appearance row.  Classic: the 18-float row.
@@ -481,9 +481,12 @@ struct Fields {
     // then b1, W2, b2.  The weights of the three direction inputs and the direction
     // gradient (record slots 14-16) are per-record constants (the direction, the input
     // weights) times the b1 sums, so the flush forms them (21 values per record).
-    static constexpr int kGeo = 14;
+    // Without a normal-map gradient (Normals false: its plane is NULL, every pixel's
+    // normal gradient zero) the normal slots 11-13 have no field: the classic row then
+    // has 30 fields, one 32-column pass of the warp reduction with nothing left over.
+    static constexpr int kGeo = Normals ? 14 : 11;
     static constexpr int kRow = Neural ? 39 : 18;
-    static constexpr int kCount = kGeo + 1 + kRow;            // 33 classic, 54 neural
+    static constexpr int kCount = kGeo + 1 + kRow;   // classic 33 / 30, neural 54 / 51
     static constexpr int kB1 = kGeo + 1 + 12;                  // neural: field of b1[0]
     // classic: packed field of record slot s / appearance-row slot q (-1: no field)
     static __device__ __forceinline__ int record_field(int s) {
@@ -502,13 +505,13 @@ constexpr int kWarps = kBlock / 32;
 
 constexpr int kLaneStride = 36;   // 32 fields + 4 pad: a lane's 16-byte stores hit 4 new banks
 
-template <bool Neural>
+template <bool Neural, bool Normals>
 struct BackShared {
-    using F = Fields<Neural>;
-    // per (warp, record) row of field sums.  Classic: 33 floats, an odd stride, so the
-    // flush's reads (thread i: record i / 10, fields 4 (i % 10) + k) spread over the
-    // banks instead of four-way conflicts with a stride of 36.  Neural: 56.
-    static constexpr int kStride = Neural ? (F::kCount + 3) / 4 * 4 : F::kCount;
+    using F = Fields<Neural, Normals>;
+    // per (warp, record) row of field sums.  Classic: 33 (31) floats, an odd stride, so
+    // the flush's reads (thread i: record i / 10, fields 4 (i % 10) + k) spread over the
+    // banks instead of four-way conflicts with a stride of 36.  Neural: 56 (52).
+    static constexpr int kStride = Neural ? (F::kCount + 3) / 4 * 4 : (F::kCount | 1);
     Batch<Neural, kBackBatch> batch[2];        // double-buffered: batch b+1 lands during b
     float4 weights01[2][Neural ? 1 : kBackBatch];
     float rows[kWarps][kBackBatch][kStride];   // per (warp, record) field sums
@@ -520,15 +523,22 @@ struct BackShared {
 
 // Sum `vals` over the warp's 32 lanes into the warp's row for the record, 32 fields a
 // pass: every lane stores its fields as one row of the warp's scratch (16-byte stores,
-// conflict-free), then lane l adds up column l (32 loads + 31 adds, where a shuffle
-// butterfly costs 31 shuffles, 62 selects and 31 adds).  One or two fields left over
-// past the passes are summed with a plain butterfly.  Plain stores, no shared atomics:
-// the CTA's eight rows are summed at the flush; `mask` records which warps stored.
-template <bool Neural>
+// conflict-free).  Lane (quad q = lane % 8, group g = lane / 8) then adds columns
+// 4q..4q+3 over rows 8g..8g+7 with eight 16-byte loads (each quarter-warp reads one
+// whole row: conflict-free), and the four groups' partial sums are scattered with two
+// shuffle steps, after which the lane holds the full sum of column 4q + g: 8 loads +
+// 28 adds + 3 shuffles, 3 adds and 6 selects, where one column per lane costs 32 loads
+// and 31 adds and a shuffle butterfly 31 shuffles, 62 selects and 31 adds.  One or two
+// fields left over past the passes are summed with a plain butterfly.  Plain stores, no
+// shared atomics: the CTA's eight rows are summed at the flush; `mask` records which
+// warps stored.
+template <bool Neural, bool Normals>
 __device__ __forceinline__ void warp_store(const float* vals, float (*scratch)[kLaneStride],
                                            float* row, unsigned* mask, int warp, int lane) {
-    using F = Fields<Neural>;
+    using F = Fields<Neural, Normals>;
     constexpr int kPasses = F::kCount / 32 + (F::kCount % 32 > 2 ? 1 : 0);
+    const int quad = lane & 7, group = lane >> 3;
+    const bool high = group & 2, odd = group & 1;
 #pragma unroll
     for (int pass = 0; pass < kPasses; ++pass) {
         if (pass) __syncwarp();
@@ -543,10 +553,24 @@ __device__ __forceinline__ void warp_store(const float* vals, float (*scratch)[k
             *reinterpret_cast<float4*>(&scratch[lane][4 * k]) = q;
         }
         __syncwarp();
-        float sum = 0.f;
+        float4 s = *reinterpret_cast<const float4*>(&scratch[8 * group][4 * quad]);
 #pragma unroll
-        for (int r = 0; r < 32; ++r) sum += scratch[r][lane];
-        if (pass * 32 + lane < F::kCount) row[pass * 32 + lane] = sum;
+        for (int r = 1; r < 8; ++r) {
+            const float4 t = *reinterpret_cast<const float4*>(&scratch[8 * group + r][4 * quad]);
+            s.x += t.x;
+            s.y += t.y;
+            s.z += t.z;
+            s.w += t.w;
+        }
+        // groups g and g ^ 2: the high pair keeps columns 2-3, the low pair 0-1
+        float k0 = high ? s.z : s.x, k1 = high ? s.w : s.y;
+        k0 += __shfl_xor_sync(0xffffffffu, high ? s.x : s.z, 16);
+        k1 += __shfl_xor_sync(0xffffffffu, high ? s.y : s.w, 16);
+        // groups g and g ^ 1: the odd one keeps the second column
+        float sum = odd ? k1 : k0;
+        sum += __shfl_xor_sync(0xffffffffu, odd ? k0 : k1, 8);
+        const int column = pass * 32 + 4 * quad + group;
+        if (column < F::kCount) row[column] = sum;
     }
 #pragma unroll
     for (int f = kPasses * 32; f < F::kCount; ++f) {
@@ -559,11 +583,11 @@ __device__ __forceinline__ void warp_store(const float* vals, float (*scratch)[k
     if (lane == 0) atomicOr(mask, 1u << warp);
 }
 
-template <bool Neural, bool Count>
+template <bool Neural, bool Count, bool Normals>
 __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_kernel(const Params P) {
     unsigned tests = 0, accepts = 0;
-    using F = Fields<Neural>;
-    using S = BackShared<Neural>;
+    using F = Fields<Neural, Normals>;
+    using S = BackShared<Neural, Normals>;
     constexpr int kRow = Batch<Neural>::kRow;
     extern __shared__ float4 dynamic_smem[];
     S& sh = *reinterpret_cast<S*>(dynamic_smem);
@@ -706,9 +730,13 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                 float gw = go[4] * v.depth + go[8] * (m * m * total_a + m2 - 2 * m * m1);
 #pragma unroll
                 for (int c = 0; c < 3; ++c) {
-                    gw += go[c] * color[c] + go[5 + c] * g[11 + c];
+                    if constexpr (Normals) {
+                        gw += go[c] * color[c] + go[5 + c] * g[11 + c];
+                        gg[11 + c] += w * go[5 + c];
+                    } else {   // the same value with a zero normal gradient
+                        gw = __fadd_rn(gw, __fmul_rn(go[c], color[c]));
+                    }
                     gc[c] = w * go[c];
-                    gg[11 + c] += w * go[5 + c];
                 }
                 const float galpha = fmaf(T, gw, (background_term - suffix) * inv_transmit);
                 suffix += w * gw;
@@ -804,7 +832,8 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                     gg[6 + k] += x * gk[k] + y * gl[k];
                 }
             }
-            warp_store<Neural>(vals, sh.lanes[warp], sh.rows[warp][j], &mask[j], warp, lane);
+            warp_store<Neural, Normals>(vals, sh.lanes[warp], sh.rows[warp][j], &mask[j], warp,
+                                        lane);
         }
         // flush: sum the warps' rows of each record in warp order and add them to global
         // memory.  Classic: one 16-byte vector atomic per (tile, record, 4-slot quad) of
@@ -1011,15 +1040,19 @@ int launch_backward(Params& P, int64_t images, int neural, uint64_t* counters, v
         kernel<<<unsigned(tiles), block, smem, s>>>(P);
         return GS_OK;
     };
+    // a NULL normal-map gradient plane drops the normal fields from the kernel
+#define GS_BWD(N, C, M) launch(composite_backward_kernel<N, C, M>, sizeof(BackShared<N, M>))
+    const bool normals = P.gin[3] != nullptr;
     int st;
     if (neural && counters)
-        st = launch(composite_backward_kernel<true, true>, sizeof(BackShared<true>));
+        st = normals ? GS_BWD(true, true, true) : GS_BWD(true, true, false);
     else if (neural)
-        st = launch(composite_backward_kernel<true, false>, sizeof(BackShared<true>));
+        st = normals ? GS_BWD(true, false, true) : GS_BWD(true, false, false);
     else if (counters)
-        st = launch(composite_backward_kernel<false, true>, sizeof(BackShared<false>));
+        st = normals ? GS_BWD(false, true, true) : GS_BWD(false, true, false);
     else
-        st = launch(composite_backward_kernel<false, false>, sizeof(BackShared<false>));
+        st = normals ? GS_BWD(false, false, true) : GS_BWD(false, false, false);
+#undef GS_BWD
     if (st) return st;
     GS_CHECK_LAUNCH("composite_backward_kernel");
     return GS_OK;
