@@ -232,12 +232,34 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
         mv = reinterpret_cast<const float4*>(fmags)[sn];
         pv = reinterpret_cast<const float4*>(fphases)[sn];
     }
-    // Appearance rows with SH colours: both colours are evaluated inside the camera loop
-    // and each 80-byte row is written at once (five 16-byte stores, no partially written
-    // sectors).  The coefficient sets are re-read per camera from L1/L2; writing a row's
-    // colours in later passes instead left its first sector partly written, which with
-    // many cameras per surfel (16 on config 4: 2.5 GB of rows) reached DRAM as partial
-    // writes (projection forward 4.0 -> 2.7 ms there, config 1 unchanged).
+    // Appearance rows with SH colours: both colour sets' coefficients are loaded once
+    // into registers, both colours are evaluated inside the camera loop and each
+    // 80-byte row is written at once (five 16-byte stores, no partially written
+    // sectors).  Re-reading the coefficient sets per camera from L1/L2 instead made the
+    // kernel wait on those loads, and more so the more threads an SM held (their sets
+    // no longer fitting L1).
+    float coef[Degree >= 0 ? 2 : 1][K * 3];
+    if constexpr (Degree >= 0) {
+#pragma unroll
+        for (int set = 0; set < 2; ++set) {
+            const float4* src = reinterpret_cast<const float4*>(
+                (set == 0 ? sh_first : sh_second) + sn * K * 3);
+            if constexpr ((K * 3) % 4 == 0) {
+                // 12 or 48 floats per set: every set starts 16-byte aligned
+#pragma unroll
+                for (int i = 0; i < K * 3 / 4; ++i) {
+                    const float4 q = __ldg(src + i);
+                    coef[set][4 * i] = q.x; coef[set][4 * i + 1] = q.y;
+                    coef[set][4 * i + 2] = q.z; coef[set][4 * i + 3] = q.w;
+                }
+            } else {
+                // 3 or 27 floats per set: sets start 4-byte aligned only
+#pragma unroll
+                for (int i = 0; i < K * 3; ++i)
+                    coef[set][i] = __ldg(reinterpret_cast<const float*>(src) + i);
+            }
+        }
+    }
     for (int64_t c = 0; c < C; ++c) {
         Camera cam;
         load_camera(cam, views, intr, s * C + c);
@@ -261,28 +283,11 @@ __global__ __launch_bounds__(kProjThreads) void project_forward_kernel(
                 sh_basis<Degree>(p.dir[0], p.dir[1], p.dir[2], basis);
 #pragma unroll
                 for (int set = 0; set < 2; ++set) {
-                    const float4* src = reinterpret_cast<const float4*>(
-                        (set == 0 ? sh_first : sh_second) + sn * K * 3);
-                    float coef[K * 3];
-                    if constexpr ((K * 3) % 4 == 0) {
-                        // 12 or 48 floats per set: every set starts 16-byte aligned
-#pragma unroll
-                        for (int i = 0; i < K * 3 / 4; ++i) {
-                            const float4 q = __ldg(src + i);
-                            coef[4 * i] = q.x; coef[4 * i + 1] = q.y;
-                            coef[4 * i + 2] = q.z; coef[4 * i + 3] = q.w;
-                        }
-                    } else {
-                        // 3 or 27 floats per set: sets start 4-byte aligned only
-#pragma unroll
-                        for (int i = 0; i < K * 3; ++i)
-                            coef[i] = __ldg(reinterpret_cast<const float*>(src) + i);
-                    }
 #pragma unroll
                     for (int ch = 0; ch < 3; ++ch) {
                         float raw = 0.5f;
 #pragma unroll
-                        for (int k = 0; k < K; ++k) raw += basis[k] * coef[k * 3 + ch];
+                        for (int k = 0; k < K; ++k) raw += basis[k] * coef[set][k * 3 + ch];
                         col[set * 3 + ch] = fmaxf(raw, 0.f);
                     }
                 }
