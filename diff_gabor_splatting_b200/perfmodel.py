@@ -8,13 +8,16 @@ tested; accepts: samples blended forward / differentiated backward).
 The constants are executed FP32 flops per event (2 x FFMA + FADD + FMUL thread
 instructions with the predicate on, ncu), fitted over two classic workloads whose
 test/accept ratios differ (config 1 with 100k surfels and one camera: 1.45 tests per
-accept; config 3 with two scenes: 2.84), which both fit exactly; the neural accept cost
+accept; config 3 with two scenes: 2.84), which both fit to 0.1%; the neural accept cost
 follows from a neural workload (config 2, 50k surfels) given the classic test cost.
 They include the backward's reduction adds (the per-warp transpose sums its lanes'
-fields), which an accept pays in proportion to its warp's accepting lanes.
+fields), which an accept pays in proportion to its warp's accepting lanes.  The
+backward has two variants: without a normal-map gradient (configs 0-3) its kernel has
+no normal fields; with one (config 4's loss) it keeps them.
 
   forward:  33 flop per test + 141 (classic) / 220 (neural) per accept
-  backward: 45 flop per test + 325 (classic) / 523 (neural) per accept
+  backward: 43 flop per test + 308 (classic) / 512 (neural) per accept,
+            with a normal-map gradient 45 + 325 / 523
 """
 
 from __future__ import annotations
@@ -23,9 +26,10 @@ import torch
 
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # 74.4 nominal; bench.py measures it
 
-TEST_FLOP = {"forward": 33, "backward": 45}
+TEST_FLOP = {"forward": 33, "backward": 43, "backward_normals": 45}
 ACCEPT_FLOP = {"classic": 141, "neural": 220}
-BACKWARD_ACCEPT_FLOP = {"classic": 325, "neural": 523}
+BACKWARD_ACCEPT_FLOP = {"classic": 308, "neural": 512}
+BACKWARD_ACCEPT_FLOP_NORMALS = {"classic": 325, "neural": 523}
 
 
 # DRAM bytes (read + write) of one launch measured with ncu on small cases of two
@@ -35,8 +39,8 @@ BACKWARD_ACCEPT_FLOP = {"classic": 325, "neural": 523}
 # traffic is the record batches, gradient atomics and pixel buffers, all of which grow
 # with the accepted work); other workloads use the config-1 figures.
 PROFILED_TRAFFIC = {
-    1: {"gs_composite_forward": (16.224256e6 + 52.915456e6, 130426868),
-        "gs_composite_backward": (88.160768e6 + 4.975616e6, 130426868)},
+    1: {"gs_composite_forward": (16.188672e6 + 52.855296e6, 130426868),
+        "gs_composite_backward": (88.078080e6 + 3.940096e6, 130426868)},
     3: {"gs_composite_forward": (87.757056e6 + 26.615808e6, 74378371),
         "gs_composite_backward": (148.364288e6 + 18.006272e6, 74378371)},
 }
@@ -95,12 +99,15 @@ def stage_model(name: str, counts: dict, w) -> dict:
                           "flop/accept x accepts (kernel counters; constants = executed FP32 "
                           "flops per event, ncu-fitted)")
     if name == "gs_composite_backward":
-        flop = TEST_FLOP["backward"] * counts.get("backward_tests", 0) + \
-            BACKWARD_ACCEPT_FLOP[w.method] * counts.get("backward_accepts", 0)
+        normals = bool(w.depth_normal_loss)   # a normal-map gradient: the kernel keeps its fields
+        per_test = TEST_FLOP["backward_normals" if normals else "backward"]
+        per_accept = (BACKWARD_ACCEPT_FLOP_NORMALS if normals else BACKWARD_ACCEPT_FLOP)[w.method]
+        flop = per_test * counts.get("backward_tests", 0) + \
+            per_accept * counts.get("backward_accepts", 0)
         return dict(bound="fp32", unit="TFLOP/s", work=flop,
-                    basis=f"{TEST_FLOP['backward']} flop/test x tests + "
-                          f"{BACKWARD_ACCEPT_FLOP[w.method]} flop/accept x accepts (kernel "
-                          "counters; constants = executed FP32 flops per event, ncu-fitted)")
+                    basis=f"{per_test} flop/test x tests + {per_accept} flop/accept x accepts "
+                          "(kernel counters; constants = executed FP32 flops per event, "
+                          "ncu-fitted)")
     if name == "gs_bin_sort":
         # per record: the span writer reads the fields its region uses (T, xy, opacity:
         # 48 B), radius, depth order and span offset (16 B); per row span: 12 B written
