@@ -616,14 +616,34 @@ __device__ __forceinline__ void unpack_span(uint64_t v, int& x0, int& x1, int& r
     record = int(v >> 32);
 }
 
-// [row_first, row_end) of each tile row in the row-sorted span list (both zeroed first)
+// [row_first, row_end) of each tile row in the row-sorted span list (both zeroed first).
+// Four keys per thread, read with one 16-byte load when the key array is 16-byte
+// aligned (it starts 256 bytes into the caller's workspace; scalar loads otherwise),
+// plus its two neighbours; each bound is written by the one thread whose keys hold the
+// row change.
+constexpr int kBoundKeys = 4;
+
 __global__ void row_bounds_kernel(int64_t S, const uint32_t* __restrict__ rows,
                                   int* __restrict__ row_first, int* __restrict__ row_end) {
-    const int64_t k = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (k >= S) return;
-    const uint32_t r = rows[k];
-    if (k == 0 || rows[k - 1] != r) row_first[r] = int(k);
-    if (k == S - 1 || rows[k + 1] != r) row_end[r] = int(k + 1);
+    const int64_t k0 = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * kBoundKeys;
+    if (k0 >= S) return;
+    uint32_t r[kBoundKeys + 2];   // keys k0-1 .. k0+4 (0xffffffff outside the list)
+    if (k0 + kBoundKeys <= S && (reinterpret_cast<uintptr_t>(rows) & 15u) == 0u) {
+        const uint4 q = *reinterpret_cast<const uint4*>(rows + k0);
+        r[1] = q.x; r[2] = q.y; r[3] = q.z; r[4] = q.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < kBoundKeys; ++i) r[1 + i] = k0 + i < S ? rows[k0 + i] : 0xffffffffu;
+    }
+    r[0] = k0 > 0 ? rows[k0 - 1] : 0xffffffffu;
+    r[kBoundKeys + 1] = k0 + kBoundKeys < S ? rows[k0 + kBoundKeys] : 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < kBoundKeys; ++i) {
+        const int64_t k = k0 + i;
+        if (k >= S) break;
+        if (r[i] != r[i + 1]) row_first[r[i + 1]] = int(k);
+        if (r[i + 2] != r[i + 1]) row_end[r[i + 1]] = int(k + 1);
+    }
 }
 
 // chunks of each row, into chunk_base[1 + row] (inclusive-scanned afterwards)
@@ -917,7 +937,8 @@ int sort_phase_rows(const float* records, int record_stride, const int32_t* radi
                                             int(S), 0, tile_bits(L.rows), s));
     GS_CUDA(cudaMemsetAsync(row_first, 0, sizeof(int) * L.rows, s));
     GS_CUDA(cudaMemsetAsync(row_end, 0, sizeof(int) * L.rows, s));
-    row_bounds_kernel<<<blocks_for(S), kBinThreads, 0, s>>>(S, keys_out, row_first, row_end);
+    row_bounds_kernel<<<blocks_for((S + kBoundKeys - 1) / kBoundKeys), kBinThreads, 0, s>>>(
+        S, keys_out, row_first, row_end);
     GS_CHECK_LAUNCH("row_bounds_kernel");
     // chunks per row (staged in tile_count), inclusive-scanned into chunk_base[1..rows]
     row_chunks_kernel<<<blocks_for(L.rows), kBinThreads, 0, s>>>(L.rows, row_first, row_end,
