@@ -245,7 +245,8 @@ int gs_composite_backward(const float* records, const float* rows, int row_mode,
  * starts at planes[g] + p * plane_strides[g] (floats, channels adjacent).  The
  * backward reads each plane's gradient at grad_planes[g] + p * grad_strides[2g] +
  * k * grad_strides[2g+1] (a stride of 0 reads a broadcast value; a NULL plane is a
- * zero gradient).  `planes`, `plane_strides`, `grad_planes` and `grad_strides` are
+ * zero gradient, and a NULL normal-map plane also drops the normal terms from the
+ * backward's per-record sums).  `planes`, `plane_strides`, `grad_planes` and `grad_strides` are
  * host arrays.  No counterpart in the reference, which writes one [..][9] array and
  * slices it: with separate planes a framework hands each output's gradient to the
  * kernel as it is, without assembling a full [..][9] gradient.
