@@ -1,6 +1,8 @@
 """CPU: host-side logic of the optimiser, the graph-captured step and the work model
 (no GPU needed: every check here runs before any kernel would)."""
 
+import dataclasses
+
 import pytest
 import torch
 
@@ -72,6 +74,14 @@ def test_work_model_is_positive_and_scales_with_the_counts():
     assert backward["unit"] == "TFLOP/s"
     assert perfmodel.traffic("gs_composite_backward_split", counts) > 0
     assert perfmodel.traffic("gs_bin_sort", counts) is None
+    # a loss with a normal-map gradient runs the backward variant that keeps the normal
+    # fields, which executes more flops per event
+    with_normals = perfmodel.stage_model("gs_composite_backward_split", counts,
+                                         dataclasses.replace(w, depth_normal_loss=True))
+    assert with_normals["work"] > backward["work"]
+    assert backward["work"] == (perfmodel.TEST_FLOP["backward"] * counts["backward_tests"] +
+                                perfmodel.BACKWARD_ACCEPT_FLOP["classic"] *
+                                counts["backward_accepts"])
 
 
 def test_product_package_never_imports_the_oracle():
