@@ -44,10 +44,11 @@ SIGNATURES = {
     "gs_composite_backward": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _p, _p, _p, _l, _i, _i,
                               _i, _f, _f, _p, _p, _p, _p, _p, _p],
     "gs_composite_forward_split": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _l, _i, _i, _i, _i,
-                                   _f, _f, _p, _p, _p, _l, _p, _p, _p, _l, _p, _p, _p, _p],
+                                   _f, _f, _p, _p, _p, _l, _p, _p, _p, _l, _p, _p, _p, _l, _p,
+                                   _p],
     "gs_composite_backward_split": [_p, _p, _i, _p, _l, _l, _l, _l, _p, _p, _p, _p, _p, _p, _p, _p,
                                     _p, _l, _p, _p, _l, _l, _i, _i, _i, _f, _f, _p, _p, _p, _p,
-                                    _p, _p],
+                                    _p, _l, _p, _p],
     "gs_adam_step": [_i, _p, _p, _p, _p, _p, ctypes.c_double, ctypes.c_double, ctypes.c_double,
                      ctypes.c_double, ctypes.c_double, _l, _p],
     "gs_adam_step_capturable": [_i, _p, _p, _p, _p, _p, _p, ctypes.c_double, ctypes.c_double,

@@ -76,7 +76,30 @@ struct Params {
     float* grad_backgrounds;
     // optional work counters: [0] samples tested, [1] contributions accepted
     unsigned long long* counters;
+    // optional warp accept masks (NULL: none): plane w of warp_mask_words words holds,
+    // for warp w of a tile's CTA, bit p & 31 of word p >> 5 set when a pixel of that
+    // warp accepted the record at point-list position p (written by the forward, read
+    // by the backward, which skips the records its warp accepted nowhere)
+    unsigned* warp_mask;
+    int64_t warp_mask_words;
 };
+
+constexpr int kMaskWarps = 8;   // warps of a 256-thread tile CTA: planes of a warp mask
+
+// OR the forward's accepted bits of one warp for list positions [p0, p0 + 64) into its
+// plane: up to three words, each only when it has a bit set and lies inside the plane.
+__device__ __forceinline__ void or_accepted(const Params& P, int warp, int64_t p0,
+                                            unsigned lo, unsigned hi) {
+    unsigned* plane = P.warp_mask + int64_t(warp) * P.warp_mask_words;
+    const uint64_t bits = (uint64_t(hi) << 32) | lo;
+    const int64_t w0 = p0 >> 5;
+    const int o = int(p0 & 31);
+    const unsigned word[3] = {unsigned(bits << o), unsigned((bits << o) >> 32),
+                              o ? unsigned(bits >> (64 - o)) : 0u};
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+        if (word[k] && w0 + k < P.warp_mask_words) atomicOr(plane + w0 + k, word[k]);
+}
 
 // Each warp of a tile CTA composites an 8x4 block of the 16x16 tile (warps 0-1 the top
 // two blocks, and so on).  A splat covers a compact patch of a tile, which touches fewer
@@ -382,12 +405,20 @@ __device__ __forceinline__ void appearance_forward(const float* a, const float* 
     }
 }
 
-template <bool Neural, bool Count, bool Exact, bool Median>
+template <bool Neural, bool Count, bool Exact, bool Median, bool Mask>
 __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Params P) {
+    static_assert(kBatch == 64 && kBlock / 32 == kMaskWarps, "accept flags: two words a batch");
     unsigned tests = 0, accepts = 0;
     __shared__ Batch<Neural> batches[2];
     __shared__ float4 weights01[2][Neural ? 1 : kBatch];
+    // Mask: per warp, which of the current batch's records a pixel of the warp accepted
+    __shared__ unsigned char accepted[Mask ? kMaskWarps : 1][Mask ? kBatch : 1];
     const int rank = threadIdx.y * kTile + threadIdx.x;
+    const int warp = rank >> 5, lane = rank & 31;
+    if constexpr (Mask) {
+        accepted[warp][lane] = 0;
+        accepted[warp][32 + lane] = 0;
+    }
     const PixelSlot slot = pixel_slot(P, rank);
     const int tile = slot.tile, image = slot.image, x = slot.x, y = slot.y;
     const bool inside = slot.inside;
@@ -421,6 +452,7 @@ __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Para
             const float next = T * (1 - v.alpha);
             if (next < 0.0001f) { done = true; break; }
             if constexpr (Count) ++accepts;
+            if constexpr (Mask) accepted[warp][j] = 1;
             float color[3], hidden[6], pre[6];
             appearance_forward<Neural, Exact>(reinterpret_cast<const float*>(batch.app[j]), g, v, dirs,
                                               batch.half_weight[Neural ? 0 : j], color, hidden,
@@ -443,6 +475,15 @@ __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Para
                 median_at = last;
             }
             T = next;
+        }
+        if constexpr (Mask) {   // the warp's accepted records of this batch, as bits
+            __syncwarp();
+            const unsigned lo = __ballot_sync(0xffffffffu, accepted[warp][lane] != 0);
+            const unsigned hi = __ballot_sync(0xffffffffu, accepted[warp][32 + lane] != 0);
+            accepted[warp][lane] = 0;
+            accepted[warp][32 + lane] = 0;
+            __syncwarp();
+            if (lane == 0 && (lo | hi)) or_accepted(P, warp, start, lo, hi);
         }
     }
     if (inside) {
@@ -583,7 +624,7 @@ __device__ __forceinline__ void warp_store(const float* vals, float (*scratch)[k
     if (lane == 0) atomicOr(mask, 1u << warp);
 }
 
-template <bool Neural, bool Count, bool Normals>
+template <bool Neural, bool Count, bool Normals, bool Mask>
 __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_kernel(const Params P) {
     unsigned tests = 0, accepts = 0;
     using F = Fields<Neural, Normals>;
@@ -670,7 +711,20 @@ __global__ __launch_bounds__(kBlock, Neural ? 2 : 3) void composite_backward_ker
                         rank);
             if (rank < kBackBatch) sh.mask[(b + 1) & 1][rank] = 0u;
         }
+        // Mask: bit k of `accepted` = whether a pixel of this warp accepted the record at
+        // list position low + k in the forward (positions past the plane: assumed so)
+        uint64_t accepted = ~uint64_t(0);
+        if constexpr (Mask) {
+            const int64_t high = int64_t(range.x) + start - 1, low = high - (count - 1);
+            const unsigned* plane = P.warp_mask + int64_t(warp) * P.warp_mask_words;
+            const int64_t w0 = low >> 5, w1 = high >> 5;
+            const unsigned a0 = w0 < P.warp_mask_words ? plane[w0] : ~0u;
+            const unsigned a1 = w1 == w0 ? 0u : (w1 < P.warp_mask_words ? plane[w1] : ~0u);
+            accepted = ((uint64_t(a1) << 32) | a0) >> (low & 31);
+        }
         for (int j = 0; j < count; ++j) {
+            // a record no pixel of the warp accepted in the forward adds no gradient here
+            if (Mask && !((accepted >> (count - 1 - j)) & 1u)) continue;
             const float* g = reinterpret_cast<const float*>(batch.geo[j]);
             const float* a = reinterpret_cast<const float*>(batch.app[j]);
             Sample v;
@@ -999,9 +1053,10 @@ int launch_forward(Params& P, int64_t images, int neural, int flags, uint64_t* c
     const dim3 block(kTile, kTile);
     const bool exact = flags & GS_COMPOSITE_EXACT;
     const unsigned grid = unsigned(tiles);
-#define GS_FWD(N, C, E)                                                                    \
-    (P.median ? composite_forward_kernel<N, C, E, true><<<grid, block, 0, s>>>(P)             \
-              : composite_forward_kernel<N, C, E, false><<<grid, block, 0, s>>>(P))
+#define GS_FWD_M(N, C, E, M)                                                               \
+    (P.warp_mask ? composite_forward_kernel<N, C, E, M, true><<<grid, block, 0, s>>>(P)       \
+                 : composite_forward_kernel<N, C, E, M, false><<<grid, block, 0, s>>>(P))
+#define GS_FWD(N, C, E) (P.median ? GS_FWD_M(N, C, E, true) : GS_FWD_M(N, C, E, false))
     if (neural) {
         if (counters) { if (exact) GS_FWD(true, true, true); else GS_FWD(true, true, false); }
         else { if (exact) GS_FWD(true, false, true); else GS_FWD(true, false, false); }
@@ -1010,6 +1065,7 @@ int launch_forward(Params& P, int64_t images, int neural, int flags, uint64_t* c
         else { if (exact) GS_FWD(false, false, true); else GS_FWD(false, false, false); }
     }
 #undef GS_FWD
+#undef GS_FWD_M
     GS_CHECK_LAUNCH("composite_forward_kernel");
     return GS_OK;
 }
@@ -1041,7 +1097,9 @@ int launch_backward(Params& P, int64_t images, int neural, uint64_t* counters, v
         return GS_OK;
     };
     // a NULL normal-map gradient plane drops the normal fields from the kernel
-#define GS_BWD(N, C, M) launch(composite_backward_kernel<N, C, M>, sizeof(BackShared<N, M>))
+#define GS_BWD(N, C, M)                                                                    \
+    (P.warp_mask ? launch(composite_backward_kernel<N, C, M, true>, sizeof(BackShared<N, M>)) \
+                 : launch(composite_backward_kernel<N, C, M, false>, sizeof(BackShared<N, M>)))
     const bool normals = P.gin[3] != nullptr;
     int st;
     if (neural && counters)
@@ -1106,6 +1164,7 @@ extern "C" int gs_composite_forward_split(const float* records, const float* row
                                           int32_t* median_index, const int32_t* selected,
                                           const int32_t* groups, int64_t group_count,
                                           float* state, int32_t* contributors,
+                                          uint32_t* warp_masks, int64_t warp_mask_words,
                                           uint64_t* counters, void* stream) {
     int st = check_composite("gs_composite_forward_split", records, rows, row_mode, primitive_ids,
                              cameras, surfels, records_count, backgrounds, ranges, images, width,
@@ -1133,6 +1192,10 @@ extern "C" int gs_composite_forward_split(const float* records, const float* row
         return fail(GS_ERR_ARGUMENT, "gs_composite_forward_split: bad selected-pixel groups");
     P.selected = reinterpret_cast<const int4*>(selected);
     P.groups = reinterpret_cast<const int4*>(groups);
+    if (warp_masks && warp_mask_words < 1)
+        return fail(GS_ERR_ARGUMENT, "gs_composite_forward_split: warp masks need a positive plane size");
+    P.warp_mask = warp_masks;
+    P.warp_mask_words = warp_mask_words;
     return launch_forward(P, images, neural, flags, counters, stream, groups ? group_count : -1);
 }
 
@@ -1186,6 +1249,7 @@ extern "C" int gs_composite_backward_split(const float* records, const float* ro
                                            int width, int height, int neural, float near_plane,
                                            float far_plane, float* grad_records, float* grad_xy,
                                            float* grad_rows, float* grad_backgrounds,
+                                           const uint32_t* warp_masks, int64_t warp_mask_words,
                                            uint64_t* counters, void* stream) {
     int st = check_composite("gs_composite_backward_split", records, rows, row_mode, primitive_ids,
                              cameras, surfels, records_count, backgrounds, ranges, images, width,
@@ -1221,5 +1285,9 @@ extern "C" int gs_composite_backward_split(const float* records, const float* ro
     P.grad_xy = grad_xy;
     P.grad_rows = grad_rows;
     P.grad_backgrounds = grad_backgrounds;
+    if (warp_masks && warp_mask_words < 1)
+        return fail(GS_ERR_ARGUMENT, "gs_composite_backward_split: warp masks need a positive plane size");
+    P.warp_mask = const_cast<unsigned*>(warp_masks);
+    P.warp_mask_words = warp_mask_words;
     return launch_backward(P, images, neural, counters, stream, groups ? group_count : -1);
 }

@@ -264,12 +264,14 @@ class Composite(torch.autograd.Function):
         contributors = torch.empty((images,) + pixel_shape, device=device, dtype=torch.int32)
         stream = nat.stream_of(device)
         strides, strides_ptr = nat.host_array(ctypes.c_int64, PLANES)
-        chunk_selection = []
+        chunk_selection, chunk_masks = [], []
         for ch in chunks:
             a = _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height)
             pixel0 = ch.image0 * per_image
             sel = selection.for_images(ch.image0, ch.images) if selection is not None else None
             chunk_selection.append(sel)
+            masks = _warp_masks(ch, device)
+            chunk_masks.append(masks)
             outs, outs_ptr = nat.host_array(
                 ctypes.c_void_p, [_at(t, pixel0 * k) for t, k in zip(planes, PLANES)])
             nat.call("gs_composite_forward_split", a["records"], a["rows"], row_mode,
@@ -283,6 +285,8 @@ class Composite(torch.autograd.Function):
                      None if sel is None else nat.ptr(sel[1]),
                      0 if sel is None else sel[1].shape[0],
                      _at(state, pixel0 * 3), _at(contributors, pixel0),
+                     None if masks is None else nat.ptr(masks),
+                     0 if masks is None else masks.shape[1],
                      nat.ptr(_counters("forward", device)), stream)
         ctx.save_for_backward(records, rows, backgrounds, selected, state, contributors,
                               median_index)
@@ -290,6 +294,7 @@ class Composite(torch.autograd.Function):
         ctx.chunks = chunks
         ctx.row_ids = row_ids
         ctx.chunk_selection = chunk_selection
+        ctx.chunk_masks = chunk_masks
         ctx.pixel_shape = pixel_shape
         ctx.options = (row_mode, cameras, surfels, images, width, height, neural, near_plane,
                        far_plane)
@@ -317,7 +322,7 @@ class Composite(torch.autograd.Function):
         stream = nat.stream_of(device)
         strides, strides_ptr = nat.host_array(
             ctypes.c_int64, [x for _, px, ch in grads for x in (px, ch)])
-        for ch, sel in zip(ctx.chunks, ctx.chunk_selection):
+        for ch, sel, masks in zip(ctx.chunks, ctx.chunk_selection, ctx.chunk_masks):
             a = _chunk_args(ch, records, rows, row_mode, cameras, surfels, width, height)
             pixel0 = ch.image0 * per_image
             ins, ins_ptr = nat.host_array(
@@ -337,6 +342,8 @@ class Composite(torch.autograd.Function):
                      int(neural), near_plane, far_plane,
                      _at(g_records, ch.record0 * nat.RECORD_FLOATS), _at(g_xy, ch.record0 * 2),
                      _at(g_rows, a["row0"] * rows.shape[1]), _at(g_bg, ch.image0 * 3),
+                     None if masks is None else nat.ptr(masks),
+                     0 if masks is None else masks.shape[1],
                      nat.ptr(_counters("backward", device)), stream)
         g_pm = g_xy if selected is None else g_xy.index_select(0, selected)
         return (g_records, g_pm, g_rows, g_bg) + (None,) * 14
@@ -414,6 +421,28 @@ TIGHT_BINNING = True
 
 def _bin_flags() -> int:
     return nat.BIN_TIGHT if TIGHT_BINNING else 0
+
+
+# Warp accept masks: the forward records, per tile-list entry and warp of its tile
+# CTA, whether any pixel of the warp accepted the entry, and the backward skips the
+# entries its warp accepted nowhere (same images and gradients).  They pay when splats
+# are small against a tile (few tiles per record: most entries reach few of a tile's
+# 8x4-pixel warp blocks) and cost the forward's bookkeeping otherwise.  "auto" uses them
+# below MASK_TILES_PER_RECORD tile intersections per record; True / False force them.
+WARP_MASKS = "auto"
+MASK_TILES_PER_RECORD = 8.0
+
+
+def _warp_masks(ch, device):
+    """Zeroed accept masks for one binned chunk (8 planes of ceil(I / 32) words), or
+    None when this chunk does without."""
+    entries = ch.point_list.shape[0]
+    use = WARP_MASKS is True or (WARP_MASKS == "auto" and ARENA is None and
+                                 entries < MASK_TILES_PER_RECORD * max(ch.record_count, 1))
+    if not use or entries == 0:
+        return None
+    words = entries // 32 + 2
+    return torch.zeros((8, words), device=device, dtype=torch.int32)
 
 
 # Largest number of tile intersections binned in one pass.  Larger batches are split

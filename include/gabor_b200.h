@@ -263,7 +263,16 @@ int gs_composite_backward(const float* records, const float* rows, int row_mode,
  * with count <= 256, every listed pixel of the group inside that tile, and
  * selected[4i..4i+3] = (x, y, output index, 0) for i in [first, first + count).  All
  * per-pixel arrays (planes, state, contributors, median, gradients) are then indexed by
- * output index instead of (image H + y) W + x. */
+ * output index instead of (image H + y) W + x.
+ * Warp accept masks (optional; no counterpart in the reference): with warp_masks
+ * non-NULL (8 planes of warp_mask_words 32-bit words, zeroed by the caller before the
+ * forward; warp_mask_words >= ceil(point-list length / 32)) the forward sets, for each
+ * of a CTA's eight warps, bit p % 32 of word p / 32 of that warp's plane when a pixel
+ * of the warp accepted the record at point-list position p, and the backward, given
+ * the same masks, skips the records its warp accepted nowhere -- records that add no
+ * gradient there.  Images and gradients are the same with or without masks; they pay
+ * when most records of a tile reach few of its 8x4-pixel warp blocks (splats small
+ * against the tile).  Positions past the planes are treated as accepted. */
 int gs_composite_forward_split(const float* records, const float* rows, int row_mode,
                                const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
                                int64_t records_count, int64_t rows_count,
@@ -274,7 +283,8 @@ int gs_composite_forward_split(const float* records, const float* rows, int row_
                                float* median_depth, int64_t median_stride,
                                int32_t* median_index, const int32_t* selected,
                                const int32_t* groups, int64_t group_count, float* state,
-                               int32_t* contributors, uint64_t* counters, void* stream);
+                               int32_t* contributors, uint32_t* warp_masks,
+                               int64_t warp_mask_words, uint64_t* counters, void* stream);
 int gs_composite_backward_split(const float* records, const float* rows, int row_mode,
                                 const int64_t* primitive_ids, int64_t cameras, int64_t surfels,
                                 int64_t records_count, int64_t rows_count,
@@ -287,7 +297,8 @@ int gs_composite_backward_split(const float* records, const float* rows, int row
                                 int64_t group_count, int64_t images, int width,
                                 int height, int neural, float near_plane, float far_plane,
                                 float* grad_records, float* grad_xy, float* grad_rows,
-                                float* grad_backgrounds, uint64_t* counters, void* stream);
+                                float* grad_backgrounds, const uint32_t* warp_masks,
+                                int64_t warp_mask_words, uint64_t* counters, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Fused Adam step.  Replaces torch.optim.Adam.step() in the reference's optimisation

@@ -369,6 +369,55 @@ def test_tight_bins_render_identically_at_benchmark_size(config, cameras, scenes
         assert_grads_close(results[True][1][name], e, name, elementwise=1e-3)
 
 
+@pytest.mark.parametrize("config,scenes,surfels,cameras",
+                         [(3, 2, None, None), (2, None, 50_000, None), (1, None, 100_000, 1)])
+def test_warp_masks_change_nothing(config, scenes, surfels, cameras, monkeypatch):
+    """With warp accept masks the backward skips the records that no pixel of a warp
+    accepted in the forward; such records add no gradient, so with the masks forced on
+    and off the images are bit-identical and the compositor's gradients equal up to the
+    order of its float atomics (per field within 1e-5 of the field's scale).  "auto"
+    uses them on config 3 (small splats: few tiles per record) and not on config 1."""
+    from diff_gabor_splatting_b200.workloads import loss_of, make_workload
+
+    composite_grads, used = [], []
+    original_backward, original_masks = rendering.Composite.backward, rendering._warp_masks
+
+    def backward(ctx, *grad_planes):
+        out = original_backward(ctx, *grad_planes)
+        composite_grads.append(out[:3])
+        return out
+
+    def masks(ch, device):
+        m = original_masks(ch, device)
+        used.append(m is not None)
+        return m
+
+    monkeypatch.setattr(rendering.Composite, "backward", staticmethod(backward))
+    monkeypatch.setattr(rendering, "_warp_masks", masks)
+    w = make_workload(config, surfels=surfels, scenes=scenes, cameras=cameras)
+    fn = rasterize_gabors if w.method == "classic" else rasterize_neural_gabors
+    results = {}
+    for setting in ("auto", False, True):
+        monkeypatch.setattr(rendering, "WARP_MASKS", setting)
+        used.clear()
+        values = {k: t.cuda().requires_grad_() for k, t in w.inputs.items()}
+        rgb, alpha, meta = fn(**values, **w.kwargs())
+        maps = maps_from_result((rgb, alpha, meta))
+        loss_of(rgb, alpha, meta, w.depth_normal_loss).backward()
+        torch.cuda.synchronize()
+        results[setting] = (maps.detach(), composite_grads[-1], list(used))
+        del values, rgb, alpha, meta, maps
+    assert results["auto"][2] == [config == 3]
+    assert results[True][2] == [True] and results[False][2] == [False]
+    assert torch.equal(results[True][0], results[False][0])
+    for name, a, e in zip(("records", "centres", "rows"), results[True][1], results[False][1]):
+        if e.numel() == 0:
+            continue
+        a, e = a.reshape(e.shape[0], -1).double(), e.reshape(e.shape[0], -1).double()
+        err = ((a - e).abs().max(0).values / (e.abs().max(0).values + 1e-30)).max().item()
+        assert err <= 1e-5, f"compositor gradient of {name}: {err:.2e} of its field's scale"
+
+
 @pytest.mark.parametrize("method", ["classic", "neural"])
 def test_output_gradient_layouts_give_the_same_gradients(method):
     """The compositor reads each output's gradient in the layout autograd delivers:

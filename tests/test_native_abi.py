@@ -101,29 +101,45 @@ def test_invalid_arguments_fail_before_any_gpu_work():
     strides, strides_ptr = nat.host_array(ctypes.c_int64, [3, 1, 1, 3, 1])
     assert lib.gs_composite_forward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, 1,
                                           8, 8, 0, 0, 0.2, 100.0, planes_ptr, strides_ptr, None,
-                                          0, None, None, None, 0, fake, fake, None, None) == 1
+                                          0, None, None, None, 0, fake, fake, None, 0, None,
+                                          None) == 1
     assert b"bad plane 2" in lib.gs_last_error()
     planes, planes_ptr = nat.host_array(ctypes.c_void_p, [16] * 5)
     strides, strides_ptr = nat.host_array(ctypes.c_int64, [2, 1, 1, 3, 1])
     assert lib.gs_composite_forward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, 1,
                                           8, 8, 0, 0, 0.2, 100.0, planes_ptr, strides_ptr, None,
-                                          0, None, None, None, 0, fake, fake, None, None) == 1
+                                          0, None, None, None, 0, fake, fake, None, 0, None,
+                                          None) == 1
     assert b"bad plane 0" in lib.gs_last_error()
     strides, strides_ptr = nat.host_array(ctypes.c_int64, [3, 1, 1, 3, 1])
     assert lib.gs_composite_forward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, 1,
                                           8, 8, 0, 0, 0.2, 100.0, planes_ptr, strides_ptr, fake,
-                                          1, None, None, None, 0, fake, fake, None, None) == 1
+                                          1, None, None, None, 0, fake, fake, None, 0, None,
+                                          None) == 1
     assert b"median depth needs its index" in lib.gs_last_error()
     assert lib.gs_composite_forward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, 1,
                                           8, 8, 0, 0, 0.2, 100.0, planes_ptr, strides_ptr, None,
-                                          0, None, fake, None, 0, fake, fake, None, None) == 1
+                                          0, None, fake, None, 0, fake, fake, None, 0, None,
+                                          None) == 1
     assert b"selected-pixel groups" in lib.gs_last_error()
     grad_strides, grad_strides_ptr = nat.host_array(ctypes.c_int64, [3, 1, 1, 0, 1, 0, 3, -1, 1, 0])
     assert lib.gs_composite_backward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, fake,
                                            fake, planes_ptr, grad_strides_ptr, None, None, 0, None,
                                            None, 0, 1, 8, 8, 0, 0.2, 100.0, None, None, None, fake,
-                                           None, None) == 1
+                                           None, 0, None, None) == 1
     assert b"negative stride" in lib.gs_last_error()
+    # warp accept masks need a positive plane size
+    assert lib.gs_composite_forward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, 1,
+                                          8, 8, 0, 0, 0.2, 100.0, planes_ptr, strides_ptr, None,
+                                          0, None, None, None, 0, fake, fake, fake, 0, None,
+                                          None) == 1
+    assert b"warp masks" in lib.gs_last_error()
+    grad_strides, grad_strides_ptr = nat.host_array(ctypes.c_int64, [3, 1, 1, 0, 1, 0, 3, 1, 1, 0])
+    assert lib.gs_composite_backward_split(None, None, 0, None, 1, 1, 0, 0, fake, None, fake, fake,
+                                           fake, planes_ptr, grad_strides_ptr, None, None, 0, None,
+                                           None, 0, 1, 8, 8, 0, 0.2, 100.0, None, None, None, fake,
+                                           fake, 0, None, None) == 1
+    assert b"warp masks" in lib.gs_last_error()
     # metadata ids and the FP32 probe: sizes checked before any GPU work
     assert lib.gs_pair_ids(None, -1, 2, 3, None, None, None, None) == 1
     assert lib.gs_pair_ids(None, 4, 0, 3, None, None, None, None) == 1
