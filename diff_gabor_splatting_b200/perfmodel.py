@@ -18,6 +18,11 @@ no normal fields; with one (config 4's loss) it keeps them.
   forward:  33 flop per test + 141 (classic) / 220 (neural) per accept
   backward: 43 flop per test + 308 (classic) / 512 (neural) per accept,
             with a normal-map gradient 45 + 325 / 523
+
+With warp accept masks the backward tests only the records its warp accepted in the
+forward (the rest are skipped, not counted), so the tests it does execute are the
+costlier ones: 57 flop per executed test, fitted on the masked config-3 workload with
+the accept cost held at 308.
 """
 
 from __future__ import annotations
@@ -26,7 +31,7 @@ import torch
 
 FP32_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # 74.4 nominal; bench.py measures it
 
-TEST_FLOP = {"forward": 33, "backward": 43, "backward_normals": 45}
+TEST_FLOP = {"forward": 33, "backward": 43, "backward_normals": 45, "backward_masked": 57}
 ACCEPT_FLOP = {"classic": 141, "neural": 220}
 BACKWARD_ACCEPT_FLOP = {"classic": 308, "neural": 512}
 BACKWARD_ACCEPT_FLOP_NORMALS = {"classic": 325, "neural": 523}
@@ -100,7 +105,9 @@ def stage_model(name: str, counts: dict, w) -> dict:
                           "flops per event, ncu-fitted)")
     if name == "gs_composite_backward":
         normals = bool(w.depth_normal_loss)   # a normal-map gradient: the kernel keeps its fields
-        per_test = TEST_FLOP["backward_normals" if normals else "backward"]
+        masked = counts.get("masked_intersections", 0) > 0   # warp accept masks were used
+        per_test = TEST_FLOP["backward_masked" if masked and not normals else
+                             "backward_normals" if normals else "backward"]
         per_accept = (BACKWARD_ACCEPT_FLOP_NORMALS if normals else BACKWARD_ACCEPT_FLOP)[w.method]
         flop = per_test * counts.get("backward_tests", 0) + \
             per_accept * counts.get("backward_accepts", 0)

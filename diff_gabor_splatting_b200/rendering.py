@@ -441,6 +441,8 @@ def _warp_masks(ch, device):
                                  entries < MASK_TILES_PER_RECORD * max(ch.record_count, 1))
     if not use or entries == 0:
         return None
+    if WORK is not None:   # work accounting: the backward's tests count executed ones
+        WORK["masked_intersections"] = WORK.get("masked_intersections", 0) + entries
     words = entries // 32 + 2
     return torch.zeros((8, words), device=device, dtype=torch.int32)
 

@@ -82,6 +82,12 @@ def test_work_model_is_positive_and_scales_with_the_counts():
     assert backward["work"] == (perfmodel.TEST_FLOP["backward"] * counts["backward_tests"] +
                                 perfmodel.BACKWARD_ACCEPT_FLOP["classic"] *
                                 counts["backward_accepts"])
+    # with warp accept masks the executed tests are charged the masked per-test cost
+    masked = perfmodel.stage_model("gs_composite_backward_split",
+                                   dict(counts, masked_intersections=1), w)
+    assert masked["work"] == (perfmodel.TEST_FLOP["backward_masked"] * counts["backward_tests"] +
+                              perfmodel.BACKWARD_ACCEPT_FLOP["classic"] *
+                              counts["backward_accepts"])
 
 
 def test_product_package_never_imports_the_oracle():
