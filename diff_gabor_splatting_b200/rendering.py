@@ -434,8 +434,9 @@ MASK_TILES_PER_RECORD = 8.0
 
 
 def _warp_masks(ch, device):
-    """Zeroed accept masks for one binned chunk (8 planes of ceil(I / 32) words), or
-    None when this chunk does without."""
+    """Zeroed accept masks for one binned chunk of I list entries (8 planes of
+    I // 32 + 2 words, at least one word per 32 positions), or None when this chunk
+    does without."""
     entries = ch.point_list.shape[0]
     use = WARP_MASKS is True or (WARP_MASKS == "auto" and ARENA is None and
                                  entries < MASK_TILES_PER_RECORD * max(ch.record_count, 1))
