@@ -407,18 +407,15 @@ __device__ __forceinline__ void appearance_forward(const float* a, const float* 
 
 template <bool Neural, bool Count, bool Exact, bool Median, bool Mask>
 __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Params P) {
-    static_assert(kBatch == 64 && kBlock / 32 == kMaskWarps, "accept flags: two words a batch");
+    static_assert(kBatch == 64 && kBlock / 32 == kMaskWarps, "accepted bits: two words a batch");
     unsigned tests = 0, accepts = 0;
     __shared__ Batch<Neural> batches[2];
     __shared__ float4 weights01[2][Neural ? 1 : kBatch];
-    // Mask: per warp, which of the current batch's records a pixel of the warp accepted
-    __shared__ unsigned char accepted[Mask ? kMaskWarps : 1][Mask ? kBatch : 1];
     const int rank = threadIdx.y * kTile + threadIdx.x;
     const int warp = rank >> 5, lane = rank & 31;
-    if constexpr (Mask) {
-        accepted[warp][lane] = 0;
-        accepted[warp][32 + lane] = 0;
-    }
+    // Mask: which of the current batch's records this pixel accepted (bit j of records
+    // 0-31, then 32-63), OR-reduced over the warp after each batch
+    unsigned accepted_lo = 0, accepted_hi = 0;
     const PixelSlot slot = pixel_slot(P, rank);
     const int tile = slot.tile, image = slot.image, x = slot.x, y = slot.y;
     const bool inside = slot.inside;
@@ -452,7 +449,10 @@ __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Para
             const float next = T * (1 - v.alpha);
             if (next < 0.0001f) { done = true; break; }
             if constexpr (Count) ++accepts;
-            if constexpr (Mask) accepted[warp][j] = 1;
+            if constexpr (Mask) {
+                if (j < 32) accepted_lo |= 1u << j;
+                else accepted_hi |= 1u << (j - 32);
+            }
             float color[3], hidden[6], pre[6];
             appearance_forward<Neural, Exact>(reinterpret_cast<const float*>(batch.app[j]), g, v, dirs,
                                               batch.half_weight[Neural ? 0 : j], color, hidden,
@@ -477,12 +477,9 @@ __global__ __launch_bounds__(kBlock, 4) void composite_forward_kernel(const Para
             T = next;
         }
         if constexpr (Mask) {   // the warp's accepted records of this batch, as bits
-            __syncwarp();
-            const unsigned lo = __ballot_sync(0xffffffffu, accepted[warp][lane] != 0);
-            const unsigned hi = __ballot_sync(0xffffffffu, accepted[warp][32 + lane] != 0);
-            accepted[warp][lane] = 0;
-            accepted[warp][32 + lane] = 0;
-            __syncwarp();
+            const unsigned lo = __reduce_or_sync(0xffffffffu, accepted_lo);
+            const unsigned hi = __reduce_or_sync(0xffffffffu, accepted_hi);
+            accepted_lo = accepted_hi = 0;
             if (lane == 0 && (lo | hi)) or_accepted(P, warp, start, lo, hi);
         }
     }
